@@ -1,0 +1,145 @@
+/*
+ * moss_tts_b200.h -- C ABI of the MOSS-TTS batch-1 decode kernels for NVIDIA B200 (sm_100a).
+ *
+ * Library: libmoss_tts_b200.so (moss-tts-optimized_b200/moss_tts/_runtime/). No torch
+ * types cross this boundary: tensors are plain device pointers, sizes are ints, the
+ * stream is a cudaStream_t passed as void*. Conventions, following the reference's
+ * native launcher (src/moss_tts/_runtime/attention_native.cu:91-97):
+ *   - every function returns an int cudaError_t (0 = success); invalid arguments
+ *     (null pointers, unsupported sizes, misaligned buffers) return
+ *     cudaErrorInvalidValue (1) before anything is launched;
+ *   - nothing allocates, nothing synchronizes: all work is enqueued on `stream`,
+ *     so every call is CUDA-graph capturable; the caller owns all memory;
+ *   - bf16 tensors are row-major __nv_bfloat16; int64 ids/positions are device
+ *     arrays, read on the device (no host round-trip inside a decode step);
+ *   - `flags` bit 0 (MT_FLAG_PDL) launches with programmatic dependent launch so
+ *     a kernel's prologue (weight prefetch) overlaps its predecessor's tail.
+ *
+ * Weight format of the int4 projections (G = 32):
+ *   qweight uint8 [N, K/2]  codes, element k in nibble (k & 1) of byte k/2 (the
+ *                           reference's export packing, calibration.py:190-191;
+ *                           equivalently int32 [N, K/8], element 8i+j in nibble j)
+ *   scales  bf16  [N, K/G]
+ *   qzeros  uint8 [N, K/(2G)] one 4-bit zero point per group, even group in the
+ *                           low nibble; NULL means z = 8 (the reference's signed
+ *                           codes with bit 3 flipped: q = code + 8)
+ *   W[n][k] = bf16((q - z) * scale)
+ */
+#ifndef MOSS_TTS_B200_H
+#define MOSS_TTS_B200_H
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MT_FLAG_PDL 1
+#define MT_LINEAR_NORM 1   /* RMSNorm prologue over each activation row            */
+#define MT_LINEAR_ADD 2    /* bf16 residual add before the norm (requires NORM)    */
+#define MT_LINEAR_PAIRED 4 /* rows [0,N/2) gate, [N/2,N) up; y = bf16(silu(g)) * u */
+
+/* ABI revision of this header (1). */
+int mt_abi_version(void);
+
+/*
+ * Bit-exact dequantization: out bf16 [n, k] = bf16((q - z) * s).
+ * Replaces calibrated_backend.unpack_signed + calibrated_quant.dequantize
+ * (src/moss_tts/_runtime/calibrated_backend.py:8-13, calibrated_quant.py:41-42).
+ */
+int mt_dequant_w4(const void* qweight, const void* scales, const void* qzeros, void* out,
+                  int n, int k, int group, void* stream);
+
+/*
+ * W4A16 G32 decode GEMV, batch 1..8: y[b, :] = bf16(x'[b, :] . W^T) with fp32 accumulation,
+ * where x' = x, or RMSNorm(x) (mode NORM), or RMSNorm(bf16(x + residual)) (mode NORM|ADD,
+ * also storing bf16(x + residual) into `summed` when non-NULL). With mode PAIRED, y has
+ * N/2 columns: bf16(bf16(silu(bf16 gate)) * bf16 up).
+ * Replaces int4_dp4a (src/moss_tts/_runtime/int4_dp4a.py:56-74), dp4a_packing.linear /
+ * project (dp4a_packing.py:94-125; paired SiLU at :85-89) and the fused norm projection
+ * dp4a_norm_projection.linear (dp4a_norm_projection.py:99-117), as W4A16 instead of W4A8.
+ * Requires k % 128 == 0, n % 4 == 0 (n % 8 when PAIRED), x/residual/summed/norm_w 8-byte
+ * and qweight 16-byte aligned.
+ */
+int mt_w4a16_linear(const void* x, const void* residual, const void* norm_w, float eps,
+                    void* summed, const void* qweight, const void* scales, const void* qzeros,
+                    void* y, int batch, int n, int k, int group, int mode, int flags,
+                    void* stream);
+
+/*
+ * bf16-weight decode GEMV with the same modes as mt_w4a16_linear (w bf16 [n, k]).
+ * Replaces linear_decode (src/moss_tts/_runtime/kernels.py:93-108) and the paired gate/up
+ * SiLU GEMV fp8_silu_decode (src/moss_tts/_runtime/fused_mlp.py:7-30).
+ */
+int mt_bf16_linear(const void* x, const void* residual, const void* norm_w, float eps,
+                   void* summed, const void* w, void* y, int batch, int n, int k, int mode,
+                   int flags, void* stream);
+
+/*
+ * rmsnorm (residual == NULL) or add_rmsnorm, rows of width n:
+ * replaces kernels.rmsnorm / kernels.add_rmsnorm (src/moss_tts/_runtime/kernels.py:62, :85).
+ */
+int mt_rmsnorm(const void* x, const void* residual, const void* weight, void* summed, void* y,
+               int rows, int n, float eps, int flags, void* stream);
+
+/* y[rows, n] = bf16(bf16(silu(x[:, :n])) * x[:, n:]); replaces kernels.silu_mul (kernels.py:132). */
+int mt_silu_mul(const void* x, void* y, int rows, int n, int flags, void* stream);
+
+/*
+ * Text + n_vq audio embedding sum with per-add bf16 rounding; ids int64 [tokens, 1 + n_vq].
+ * Replaces kernels.embedding_sum (src/moss_tts/_runtime/kernels.py:21). Out-of-range ids
+ * read row 0 and set *status = 2 (status may be NULL).
+ */
+int mt_embedding_sum(const void* ids, const void* text, const void* audio, void* out, int tokens,
+                     int h, int vocab, int audio_vocab, int n_vq, void* status, int flags,
+                     void* stream);
+
+/*
+ * QK head RMSNorm + rotate-half RoPE + K/V cache-row write for `batch` sequences:
+ * qkv bf16 [batch, (nq + 2 nkv) * 128], rope tables bf16 [max_len, 128], positions int64
+ * [batch], q_out bf16 [batch, nq, 128], caches bf16 [batch, nkv, max_len, 128].
+ * Replaces the _qk_rope_cache launch of qk_rope_decode (src/moss_tts/_runtime/kernels.py:142-170,
+ * :222). A position outside [0, max_len) sets *status = 1 and writes nothing.
+ */
+int mt_qk_rope_kv(const void* qkv, const void* q_norm, const void* k_norm, const void* cos_tab,
+                  const void* sin_tab, const void* positions, void* q_out, void* k_cache,
+                  void* v_cache, int batch, int nq, int nkv, int max_len, float eps, void* status,
+                  int flags, void* stream);
+
+/*
+ * Fused decode attention: QK-norm + RoPE + cache write (as mt_qk_rope_kv), split-K GQA
+ * attention over rows 0..positions[b] with `splits` splits of ceil(len / splits) tokens,
+ * and the log-sum-exp merge, out bf16 [batch, nq * 128].
+ * Replaces qk_rope_decode (src/moss_tts/_runtime/kernels.py:211-251), which launches
+ * _qk_rope_cache, launch_attention_ordered (attention_native.cu:91-97) and the split
+ * reduction (kernels.py:198-208).
+ * Scratch (caller-allocated): partial fp32 [batch * nkv * splits * (nq/nkv) * 128],
+ * lse fp32 [batch * nkv * splits * (nq/nkv)], tickets uint32 [batch * nkv] (zero before the
+ * first call; every call leaves them zero). nq / nkv must be 1, 2 or 4.
+ */
+int mt_attention_decode(const void* qkv, const void* q_norm, const void* k_norm,
+                        const void* cos_tab, const void* sin_tab, const void* positions,
+                        void* k_cache, void* v_cache, void* out, void* partial, void* lse,
+                        void* tickets, int batch, int nq, int nkv, int max_len, int splits,
+                        float eps, void* status, int flags, void* stream);
+
+/*
+ * Output heads of one decode step with greedy selection: final add_rmsnorm of
+ * (x + residual), logits of the n_text text-head rows and n_cb audio codebooks of `vocab`
+ * rows each, argmax with the first-index tie rule, delay-pattern masks, next token ids
+ * int64 [1 + n_vq] (entries of this shard's codebooks, plus the text token when
+ * text_owner != 0). Replaces the head half of FastLLM._decode with greedy sampling
+ * (src/moss_tts/_runtime/llm.py:268-287). Scratch: best uint64 [1 + n_cb] and ticket
+ * uint32 [1], zero before the first call and left zero by every call.
+ */
+int mt_heads_greedy(const void* x, const void* residual, const void* norm_w, float eps,
+                    void* hidden, const void* text_head, const void* audio_heads,
+                    void* text_logits, void* audio_logits, const void* text_ids,
+                    const void* audio_length, const void* delay_length, void* next_ids,
+                    void* best, void* ticket, int hidden_size, int n_text, int n_cb, int vocab,
+                    int cb_offset, int n_vq, int delay_slot_id, int audio_end_id, int pad_code,
+                    int text_owner, int flags, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MOSS_TTS_B200_H */

@@ -1,0 +1,309 @@
+// Decode attention for the MOSS-TTS backbone on B200 (sm_100a).
+//
+// One launch per layer does what the reference spreads over three
+// (src/moss_tts/_runtime/kernels.py:142-251 and attention_native.cu:31-97):
+//   1. QK head RMSNorm + rotate-half RoPE of the fresh projection (kernels.py:142-170),
+//      the new K/V rows written into the static cache at `position`;
+//   2. split-K GQA attention over cache rows 0..position: CTA (kv head, split, seq)
+//      serves all query heads of its KV head, so every K/V byte is read once per
+//      layer (the reference reads each KV head once per query head);
+//   3. the log-sum-exp merge of the splits, done by the last CTA of each KV head
+//      to finish (a ticket counter in scratch memory, reset by that CTA).
+// Split boundaries follow the live length read on the device (split = ceil(len /
+// splits) tokens), so a graph captured once serves every position.
+// Scratch (fp32 partials, LSE, tickets) is caller-provided global memory.
+#include "common.cuh"
+
+namespace mt {
+
+constexpr int kHeadDim = 128;
+constexpr float kScale = 0.08838834764831845f;  // 1/sqrt(128), kernels.py:183
+
+struct AttnArgs {
+  const __nv_bfloat16* qkv;      // [B, (nq + 2 nkv) * 128]  q | k | v
+  const __nv_bfloat16* q_norm;   // [128]
+  const __nv_bfloat16* k_norm;   // [128]
+  const __nv_bfloat16* cos_tab;  // [max_len, 128]
+  const __nv_bfloat16* sin_tab;  // [max_len, 128]
+  const int64_t* positions;      // [B] cache row written this step; attends 0..position
+  __nv_bfloat16* k_cache;        // [B, nkv, max_len, 128]
+  __nv_bfloat16* v_cache;        // [B, nkv, max_len, 128]
+  __nv_bfloat16* out;            // [B, nq * 128]
+  float* partial;                // [B, nkv, splits, rep, 128]
+  float* lse;                    // [B, nkv, splits, rep]
+  unsigned* tickets;             // [B, nkv], zero on entry, zero on exit
+  int nq, nkv, max_len, splits;
+  float eps;
+  int* status;                   // optional: set to 1 when a position is out of range
+};
+
+// Head RMSNorm + RoPE for one 128-wide head held as 4 values per lane
+// (dims 4*lane .. 4*lane+3). Rounding points follow kernels.py:158-163.
+__device__ __forceinline__ void norm_rope_head(float (&x)[4], const __nv_bfloat16* w,
+                                               const __nv_bfloat16* c, const __nv_bfloat16* s,
+                                               float eps, int lane) {
+  float ss = x[0] * x[0] + x[1] * x[1] + x[2] * x[2] + x[3] * x[3];
+  ss = warp_sum(ss);
+  const float inv = 1.0f / sqrtf(ss / 128.f + eps);
+  float y[4], part[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) y[i] = round_bf16(round_bf16(x[i] * inv) * bf16f(w[4 * lane + i]));
+  // rotate_half partner of dim d is d +- 64: held by lane ^ 16
+#pragma unroll
+  for (int i = 0; i < 4; ++i) part[i] = __shfl_xor_sync(0xffffffffu, y[i], 16);
+  const float sign = lane < 16 ? -1.f : 1.f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int d = 4 * lane + i;
+    x[i] = round_bf16(round_bf16(y[i] * bf16f(c[d])) + round_bf16(sign * part[i] * bf16f(s[d])));
+  }
+}
+
+template <int REP>
+__global__ void __launch_bounds__(128) attention_decode(AttnArgs a) {
+  extern __shared__ float lg[];  // [REP][cap]
+  __shared__ float qs[REP][kHeadDim];
+  __shared__ float stat[REP][2];
+  __shared__ unsigned last;
+  const int kh = blockIdx.x, split = blockIdx.y, b = blockIdx.z;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int qkv_w = (a.nq + 2 * a.nkv) * kHeadDim;
+  pdl_wait();
+  pdl_trigger();
+  int64_t pos = a.positions[b];
+  if (pos < 0 || pos >= a.max_len) {  // host validates; never index out of the cache
+    if (a.status && tid == 0) atomicExch(a.status, 1);
+    pos = pos < 0 ? 0 : a.max_len - 1;
+  }
+  const int p = (int)pos, len = p + 1;
+  const int span = (len + a.splits - 1) / a.splits;
+  const int t0 = split * span, t1 = min(t0 + span, len);
+  const __nv_bfloat16* src = a.qkv + (size_t)b * qkv_w;
+  const size_t kv_base = ((size_t)b * a.nkv + kh) * a.max_len * kHeadDim;
+
+  // 1. Query heads of this KV head (warp w < REP handles head kh*REP + w).
+  if (warp < REP) {
+    const int h = kh * REP + warp;
+    float x[4];
+    const uint2 r = *reinterpret_cast<const uint2*>(src + h * kHeadDim + 4 * lane);
+    x[0] = bf16_lo(r.x); x[1] = bf16_hi(r.x); x[2] = bf16_lo(r.y); x[3] = bf16_hi(r.y);
+    norm_rope_head(x, a.q_norm, a.cos_tab + (size_t)p * kHeadDim, a.sin_tab + (size_t)p * kHeadDim,
+                   a.eps, lane);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) qs[warp][4 * lane + i] = x[i];
+  }
+  // The split holding the newest token writes this step's K/V cache rows.
+  if (t0 <= p && p < t1 && warp == 0) {
+    float x[4];
+    const uint2 r = *reinterpret_cast<const uint2*>(src + (a.nq + kh) * kHeadDim + 4 * lane);
+    x[0] = bf16_lo(r.x); x[1] = bf16_hi(r.x); x[2] = bf16_lo(r.y); x[3] = bf16_hi(r.y);
+    norm_rope_head(x, a.k_norm, a.cos_tab + (size_t)p * kHeadDim, a.sin_tab + (size_t)p * kHeadDim,
+                   a.eps, lane);
+    __nv_bfloat162 lo = __floats2bfloat162_rn(x[0], x[1]), hi = __floats2bfloat162_rn(x[2], x[3]);
+    uint2 o;
+    o.x = *reinterpret_cast<uint32_t*>(&lo);
+    o.y = *reinterpret_cast<uint32_t*>(&hi);
+    *reinterpret_cast<uint2*>(a.k_cache + kv_base + (size_t)p * kHeadDim + 4 * lane) = o;
+    const uint2 v = *reinterpret_cast<const uint2*>(src + (a.nq + a.nkv + kh) * kHeadDim + 4 * lane);
+    *reinterpret_cast<uint2*>(a.v_cache + kv_base + (size_t)p * kHeadDim + 4 * lane) = v;
+  }
+  __syncthreads();
+
+  const int n = t1 > t0 ? t1 - t0 : 0;
+  const int cap = (a.max_len + a.splits - 1) / a.splits;
+  const size_t slot = (((size_t)b * a.nkv + kh) * a.splits + split) * REP;
+  if (n > 0) {
+    // 2a. logits: warp w takes tokens t0 + w, t0 + w + 4, ...; lane holds 4 dims.
+    float qv[REP][4];
+#pragma unroll
+    for (int i = 0; i < REP; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) qv[i][j] = qs[i][4 * lane + j];
+    for (int t = warp; t < n; t += 4) {
+      const uint2 kr = *reinterpret_cast<const uint2*>(a.k_cache + kv_base + (size_t)(t0 + t) * kHeadDim + 4 * lane);
+      const float k0 = bf16_lo(kr.x), k1 = bf16_hi(kr.x), k2 = bf16_lo(kr.y), k3 = bf16_hi(kr.y);
+#pragma unroll
+      for (int i = 0; i < REP; ++i) {
+        float d = qv[i][0] * k0;
+        d = fmaf(qv[i][1], k1, d);
+        d = fmaf(qv[i][2], k2, d);
+        d = fmaf(qv[i][3], k3, d);
+        d = warp_sum(d);
+        if (lane == 0) lg[i * cap + t] = d * kScale;
+      }
+    }
+    __syncthreads();
+    // 2b. softmax statistics: warp i handles head i.
+    if (warp < REP) {
+      float m = -INFINITY;
+      for (int t = lane; t < n; t += 32) m = fmaxf(m, lg[warp * cap + t]);
+      m = warp_max(m);
+      float sum = 0.f;
+      for (int t = lane; t < n; t += 32) {
+        const float e = expf(lg[warp * cap + t] - m);
+        lg[warp * cap + t] = e;
+        sum += e;
+      }
+      sum = warp_sum(sum);
+      if (lane == 0) { stat[warp][0] = m; stat[warp][1] = sum; }
+    }
+    __syncthreads();
+    // 2c. weighted V: thread d accumulates dim d for every head.
+    float o[REP];
+#pragma unroll
+    for (int i = 0; i < REP; ++i) o[i] = 0.f;
+    const __nv_bfloat16* vrow = a.v_cache + kv_base + (size_t)t0 * kHeadDim + tid;
+#pragma unroll 4
+    for (int t = 0; t < n; ++t) {
+      const float v = bf16f(vrow[(size_t)t * kHeadDim]);
+#pragma unroll
+      for (int i = 0; i < REP; ++i) o[i] = fmaf(lg[i * cap + t], v, o[i]);
+    }
+#pragma unroll
+    for (int i = 0; i < REP; ++i) a.partial[(slot + i) * kHeadDim + tid] = o[i] / stat[i][1];
+    if (tid < REP) a.lse[slot + tid] = stat[tid][0] + logf(stat[tid][1]);
+  } else {
+#pragma unroll
+    for (int i = 0; i < REP; ++i) a.partial[(slot + i) * kHeadDim + tid] = 0.f;
+    if (tid < REP) a.lse[slot + tid] = -INFINITY;
+  }
+
+  // 3. The last CTA of this KV head merges all splits (kernels.py:198-208).
+  __threadfence();
+  __syncthreads();
+  unsigned* ticket = a.tickets + (size_t)b * a.nkv + kh;
+  if (tid == 0) last = (atomicAdd(ticket, 1u) == (unsigned)a.splits - 1u) ? 1u : 0u;
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  const size_t base = ((size_t)b * a.nkv + kh) * a.splits * REP;
+#pragma unroll
+  for (int i = 0; i < REP; ++i) {
+    float m = -INFINITY;
+    for (int s = 0; s < a.splits; ++s) m = fmaxf(m, __ldcg(a.lse + base + s * REP + i));
+    float wsum = 0.f, acc = 0.f;
+    for (int s = 0; s < a.splits; ++s) {
+      const float w = expf(__ldcg(a.lse + base + s * REP + i) - m);
+      wsum += w;
+      acc = fmaf(w, __ldcg(a.partial + (base + s * REP + i) * kHeadDim + tid), acc);
+    }
+    a.out[(size_t)b * a.nq * kHeadDim + (kh * REP + i) * kHeadDim + tid] = to_bf16(acc / wsum);
+  }
+  if (tid == 0) *ticket = 0u;
+}
+
+// Standalone QK-norm + RoPE + cache write (kernels.py:142-170): grid (nq + nkv, B).
+__global__ void __launch_bounds__(32) qk_rope_kv(AttnArgs a, __nv_bfloat16* q_out) {
+  const int h = blockIdx.x, b = blockIdx.y, lane = threadIdx.x;
+  pdl_wait();
+  pdl_trigger();
+  int64_t pos = a.positions[b];
+  if (pos < 0 || pos >= a.max_len) {
+    if (a.status && lane == 0) atomicExch(a.status, 1);
+    return;
+  }
+  const int p = (int)pos;
+  const __nv_bfloat16* src = a.qkv + (size_t)b * (a.nq + 2 * a.nkv) * kHeadDim;
+  const bool is_q = h < a.nq;
+  float x[4];
+  const uint2 r = *reinterpret_cast<const uint2*>(src + h * kHeadDim + 4 * lane);
+  x[0] = bf16_lo(r.x); x[1] = bf16_hi(r.x); x[2] = bf16_lo(r.y); x[3] = bf16_hi(r.y);
+  norm_rope_head(x, is_q ? a.q_norm : a.k_norm, a.cos_tab + (size_t)p * kHeadDim,
+                 a.sin_tab + (size_t)p * kHeadDim, a.eps, lane);
+  __nv_bfloat162 lo = __floats2bfloat162_rn(x[0], x[1]), hi = __floats2bfloat162_rn(x[2], x[3]);
+  uint2 o;
+  o.x = *reinterpret_cast<uint32_t*>(&lo);
+  o.y = *reinterpret_cast<uint32_t*>(&hi);
+  if (is_q) {
+    *reinterpret_cast<uint2*>(q_out + ((size_t)b * a.nq + h) * kHeadDim + 4 * lane) = o;
+  } else {
+    const int kh = h - a.nq;
+    const size_t row = (((size_t)b * a.nkv + kh) * a.max_len + p) * kHeadDim + 4 * lane;
+    *reinterpret_cast<uint2*>(a.k_cache + row) = o;
+    *reinterpret_cast<uint2*>(a.v_cache + row) =
+        *reinterpret_cast<const uint2*>(src + (a.nq + a.nkv + kh) * kHeadDim + 4 * lane);
+  }
+}
+
+static int attn_check(const AttnArgs& a, int batch) {
+  if (!a.qkv || !a.q_norm || !a.k_norm || !a.cos_tab || !a.sin_tab || !a.positions || !a.k_cache ||
+      !a.v_cache || batch < 1 || a.nkv < 1 || a.nq < a.nkv || a.nq % a.nkv || a.max_len < 1)
+    return kBadArgument;
+  if (!aligned(a.qkv, 8) || !aligned(a.k_cache, 16) || !aligned(a.v_cache, 16) ||
+      !aligned(a.positions, 8))
+    return kBadArgument;
+  return 0;
+}
+
+}  // namespace mt
+
+using namespace mt;
+
+// Fused decode attention. Replaces qk_rope_decode (src/moss_tts/_runtime/kernels.py:211-251)
+// with launch_attention_ordered (attention_native.cu:91-97) and the split reduction
+// (kernels.py:198-208 / attention_quant.py:7-23). `positions` is a device int64 [batch]
+// array (graph-capturable). Scratch: partial fp32 [batch*nkv*splits*rep*128],
+// lse fp32 [batch*nkv*splits*rep], tickets uint32 [batch*nkv] zero-initialised once.
+MT_API int mt_attention_decode(const void* qkv, const void* q_norm, const void* k_norm,
+                               const void* cos_tab, const void* sin_tab, const void* positions,
+                               void* k_cache, void* v_cache, void* out, void* partial, void* lse,
+                               void* tickets, int batch, int nq, int nkv, int max_len, int splits,
+                               float eps, void* status, int flags, void* stream) {
+  AttnArgs a;
+  a.qkv = (const __nv_bfloat16*)qkv;
+  a.q_norm = (const __nv_bfloat16*)q_norm;
+  a.k_norm = (const __nv_bfloat16*)k_norm;
+  a.cos_tab = (const __nv_bfloat16*)cos_tab;
+  a.sin_tab = (const __nv_bfloat16*)sin_tab;
+  a.positions = (const int64_t*)positions;
+  a.k_cache = (__nv_bfloat16*)k_cache;
+  a.v_cache = (__nv_bfloat16*)v_cache;
+  a.out = (__nv_bfloat16*)out;
+  a.partial = (float*)partial;
+  a.lse = (float*)lse;
+  a.tickets = (unsigned*)tickets;
+  a.nq = nq;
+  a.nkv = nkv;
+  a.max_len = max_len;
+  a.splits = splits;
+  a.eps = eps;
+  a.status = (int*)status;
+  if (attn_check(a, batch) || !out || !partial || !lse || !tickets || splits < 1 || splits > 1024)
+    return kBadArgument;
+  const int rep = nq / nkv;
+  if (rep != 4 && rep != 1 && rep != 2) return kBadArgument;
+  const size_t cap = (size_t)(max_len + splits - 1) / splits;
+  const size_t smem = (size_t)rep * cap * sizeof(float);
+  if (smem > 200 * 1024) return kBadArgument;
+  const dim3 grid(nkv, splits, batch);
+  cudaStream_t s = (cudaStream_t)stream;
+  switch (rep) {
+    case 4: return launch(attention_decode<4>, grid, dim3(128), smem, s, flags, a);
+    case 2: return launch(attention_decode<2>, grid, dim3(128), smem, s, flags, a);
+    default: return launch(attention_decode<1>, grid, dim3(128), smem, s, flags, a);
+  }
+}
+
+// Standalone QK-norm + RoPE + K/V cache write (kernels.py:142-170, grid nq + nkv heads).
+MT_API int mt_qk_rope_kv(const void* qkv, const void* q_norm, const void* k_norm,
+                         const void* cos_tab, const void* sin_tab, const void* positions,
+                         void* q_out, void* k_cache, void* v_cache, int batch, int nq, int nkv,
+                         int max_len, float eps, void* status, int flags, void* stream) {
+  AttnArgs a = {};
+  a.qkv = (const __nv_bfloat16*)qkv;
+  a.q_norm = (const __nv_bfloat16*)q_norm;
+  a.k_norm = (const __nv_bfloat16*)k_norm;
+  a.cos_tab = (const __nv_bfloat16*)cos_tab;
+  a.sin_tab = (const __nv_bfloat16*)sin_tab;
+  a.positions = (const int64_t*)positions;
+  a.k_cache = (__nv_bfloat16*)k_cache;
+  a.v_cache = (__nv_bfloat16*)v_cache;
+  a.nq = nq;
+  a.nkv = nkv;
+  a.max_len = max_len;
+  a.eps = eps;
+  a.status = (int*)status;
+  if (attn_check(a, batch) || !q_out || !aligned(q_out, 8)) return kBadArgument;
+  return launch(qk_rope_kv, dim3(nq + nkv, batch), dim3(32), 0, (cudaStream_t)stream, flags, a,
+                (__nv_bfloat16*)q_out);
+}

@@ -1,0 +1,154 @@
+// Small decode-step operators for B200 (sm_100a): RMSNorm, add + RMSNorm,
+// SiLU * up and the 33-channel embedding sum, plus library-wide helpers.
+// Rounding points follow src/moss_tts/_runtime/kernels.py exactly (cited per kernel).
+#include "common.cuh"
+
+namespace mt {
+
+int sm_count() {
+  static int cached[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) dev = 0;
+  if (!cached[dev]) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+    cached[dev] = n;
+  }
+  return cached[dev];
+}
+
+// One CTA per row. RMSNorm (kernels.py:50-59) or add + RMSNorm (kernels.py:69-90).
+__global__ void __launch_bounds__(256) rmsnorm_rows(const __nv_bfloat16* __restrict__ x,
+                                                    const __nv_bfloat16* __restrict__ residual,
+                                                    const __nv_bfloat16* __restrict__ w,
+                                                    __nv_bfloat16* __restrict__ summed,
+                                                    __nv_bfloat16* __restrict__ y, int n, float eps) {
+  extern __shared__ float buf[];
+  __shared__ float red[8];
+  const int row = blockIdx.x, tid = threadIdx.x;
+  pdl_wait();
+  pdl_trigger();
+  const __nv_bfloat16* xr = x + (size_t)row * n;
+  float ss = 0.f;
+  for (int i = tid; i < n; i += blockDim.x) {
+    float v = bf16f(xr[i]);
+    if (residual) {
+      v = round_bf16(v + bf16f(residual[(size_t)row * n + i]));
+      if (summed) summed[(size_t)row * n + i] = to_bf16(v);
+    }
+    buf[i] = v;
+    ss += v * v;
+  }
+  ss = warp_sum(ss);
+  if ((tid & 31) == 0) red[tid >> 5] = ss;
+  __syncthreads();
+  float tot = 0.f;
+  for (int i = 0; i < (int)(blockDim.x >> 5); ++i) tot += red[i];
+  const float inv = 1.0f / sqrtf(tot / (float)n + eps);
+  for (int i = tid; i < n; i += blockDim.x)
+    y[(size_t)row * n + i] = to_bf16(round_bf16(buf[i] * inv) * bf16f(w[i]));
+}
+
+// SiLU(gate) rounded to bf16, times up (kernels.py:123-139); x is [rows, 2n].
+__global__ void silu_mul_rows(const __nv_bfloat16* __restrict__ x, __nv_bfloat16* __restrict__ y,
+                              int rows, int n) {
+  pdl_wait();
+  pdl_trigger();
+  const size_t total = (size_t)rows * n;
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (size_t)gridDim.x * blockDim.x) {
+    const size_t r = i / n, c = i - r * n;
+    const float g = bf16f(x[r * 2 * n + c]), u = bf16f(x[r * 2 * n + n + c]);
+    y[i] = to_bf16(round_bf16(g / (1.0f + expf(-g))) * u);
+  }
+}
+
+// Text embedding plus the n_vq audio embeddings with a bf16 rounding after every
+// sequential addition (kernels.py:7-26). Each thread owns 8 hidden dims.
+__global__ void __launch_bounds__(128) embedding_sum_rows(const int64_t* __restrict__ ids,
+                                                          const __nv_bfloat16* __restrict__ text,
+                                                          const __nv_bfloat16* __restrict__ audio,
+                                                          __nv_bfloat16* __restrict__ out, int h,
+                                                          int vocab, int audio_vocab, int n_vq,
+                                                          int* status) {
+  const int t = blockIdx.y;
+  const int e = blockIdx.x * blockDim.x + threadIdx.x;  // 8-element slot
+  pdl_wait();
+  pdl_trigger();
+  if (e * 8 >= h) return;
+  const int64_t* row = ids + (size_t)t * (n_vq + 1);
+  int64_t tok = row[0];
+  if (tok < 0 || tok >= vocab) {  // never read outside the table
+    if (status) atomicExch(status, 2);
+    tok = 0;
+  }
+  const uint4 tv = *reinterpret_cast<const uint4*>(text + (size_t)tok * h + 8 * e);
+  float v[8];
+  const uint32_t tw[4] = {tv.x, tv.y, tv.z, tv.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) { v[2 * i] = bf16_lo(tw[i]); v[2 * i + 1] = bf16_hi(tw[i]); }
+  for (int q = 0; q < n_vq; ++q) {
+    int64_t c = row[q + 1];
+    if (c < 0 || c >= audio_vocab) {
+      if (status) atomicExch(status, 2);
+      c = 0;
+    }
+    const uint4 av = *reinterpret_cast<const uint4*>(audio + ((size_t)q * audio_vocab + c) * h + 8 * e);
+    const uint32_t aw[4] = {av.x, av.y, av.z, av.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      v[2 * i] = round_bf16(v[2 * i] + bf16_lo(aw[i]));
+      v[2 * i + 1] = round_bf16(v[2 * i + 1] + bf16_hi(aw[i]));
+    }
+  }
+  uint32_t o[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    __nv_bfloat162 p = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+    o[i] = *reinterpret_cast<uint32_t*>(&p);
+  }
+  *reinterpret_cast<uint4*>(out + (size_t)t * h + 8 * e) = make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+}  // namespace mt
+
+using namespace mt;
+
+MT_API int mt_abi_version(void) { return 1; }
+
+// rmsnorm(x, weight, eps) (src/moss_tts/_runtime/kernels.py:62) when residual is null;
+// add_rmsnorm(x, residual, weight, eps) -> (summed, normalized) (kernels.py:85) otherwise.
+MT_API int mt_rmsnorm(const void* x, const void* residual, const void* weight, void* summed, void* y,
+                      int rows, int n, float eps, int flags, void* stream) {
+  if (!x || !weight || !y || rows < 1 || n < 1 || n > 16384) return kBadArgument;
+  return launch(rmsnorm_rows, dim3(rows), dim3(256), (size_t)n * 4, (cudaStream_t)stream, flags,
+                (const __nv_bfloat16*)x, (const __nv_bfloat16*)residual, (const __nv_bfloat16*)weight,
+                (__nv_bfloat16*)summed, (__nv_bfloat16*)y, n, eps);
+}
+
+// silu_mul(x) (src/moss_tts/_runtime/kernels.py:132): x [rows, 2n] -> y [rows, n].
+MT_API int mt_silu_mul(const void* x, void* y, int rows, int n, int flags, void* stream) {
+  if (!x || !y || rows < 1 || n < 1) return kBadArgument;
+  const size_t total = (size_t)rows * n;
+  size_t blocks = (total + 255) / 256;
+  const size_t cap = (size_t)sm_count() * 8;
+  if (blocks > cap) blocks = cap;
+  return launch(silu_mul_rows, dim3((unsigned)blocks), dim3(256), 0, (cudaStream_t)stream, flags,
+                (const __nv_bfloat16*)x, (__nv_bfloat16*)y, rows, n);
+}
+
+// embedding_sum(ids, text_weight, audio_weight) (src/moss_tts/_runtime/kernels.py:21):
+// ids int64 [tokens, 1 + n_vq], text [vocab, h], audio [n_vq, audio_vocab, h] -> out [tokens, h].
+MT_API int mt_embedding_sum(const void* ids, const void* text, const void* audio, void* out,
+                            int tokens, int h, int vocab, int audio_vocab, int n_vq, void* status,
+                            int flags, void* stream) {
+  if (!ids || !text || !audio || !out || tokens < 1 || h < 8 || h % 8 || vocab < 1 ||
+      audio_vocab < 1 || n_vq < 0)
+    return kBadArgument;
+  if (!aligned(text, 16) || !aligned(audio, 16) || !aligned(out, 16) || !aligned(ids, 8))
+    return kBadArgument;
+  const dim3 grid((h / 8 + 127) / 128, tokens);
+  return launch(embedding_sum_rows, grid, dim3(128), 0, (cudaStream_t)stream, flags,
+                (const int64_t*)ids, (const __nv_bfloat16*)text, (const __nv_bfloat16*)audio,
+                (__nv_bfloat16*)out, h, vocab, audio_vocab, n_vq, (int*)status);
+}

@@ -1,0 +1,69 @@
+"""ctypes binding of ``libmoss_tts_b200.so``, the C ABI declared in ``include/moss_tts_b200.h``.
+
+The library is built in-tree for sm_100a by ``moss-tts-optimized_b200/build.py``.
+There is no fallback: if the library is missing or fails to load, every
+operator raises ``NativeLibraryError``. Launch failures (non-zero
+``cudaError_t``) raise ``RuntimeError``, as the reference's native launcher
+does (``src/moss_tts/_runtime/attention_native.py:41-44``).
+"""
+import ctypes
+import functools
+from pathlib import Path
+
+LIB_PATH = Path(__file__).with_name("libmoss_tts_b200.so")
+ABI_VERSION = 1
+FLAG_PDL = 1
+LINEAR_NORM, LINEAR_ADD, LINEAR_PAIRED = 1, 2, 4
+
+_P, _I, _F = ctypes.c_void_p, ctypes.c_int, ctypes.c_float
+
+# name -> (argtypes, restype); mirrors include/moss_tts_b200.h
+SIGNATURES = {
+    "mt_abi_version": ([], _I),
+    "mt_dequant_w4": ([_P, _P, _P, _P, _I, _I, _I, _P], _I),
+    "mt_w4a16_linear": ([_P, _P, _P, _F, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P], _I),
+    "mt_bf16_linear": ([_P, _P, _P, _F, _P, _P, _P, _I, _I, _I, _I, _I, _P], _I),
+    "mt_rmsnorm": ([_P, _P, _P, _P, _P, _I, _I, _F, _I, _P], _I),
+    "mt_silu_mul": ([_P, _P, _I, _I, _I, _P], _I),
+    "mt_embedding_sum": ([_P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _I, _P], _I),
+    "mt_qk_rope_kv": ([_P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _F, _P, _I, _P], _I),
+    "mt_attention_decode": ([_P] * 12 + [_I] * 5 + [_F, _P, _I, _P], _I),
+    "mt_heads_greedy": ([_P, _P, _P, _F] + [_P] * 11 + [_I] * 11 + [_P], _I),
+}
+
+
+class NativeLibraryError(RuntimeError):
+    """The CUDA library is not built or cannot be loaded; there is no CPU fallback."""
+
+
+@functools.lru_cache(None)
+def library() -> ctypes.CDLL:
+    if not LIB_PATH.exists():
+        raise NativeLibraryError(f"{LIB_PATH.name} is not built; run moss-tts-optimized_b200/build.py")
+    try:
+        lib = ctypes.CDLL(str(LIB_PATH))
+    except OSError as exc:
+        raise NativeLibraryError(f"cannot load {LIB_PATH}: {exc}") from exc
+    for name, (args, res) in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.argtypes = args
+        fn.restype = res
+    if lib.mt_abi_version() != ABI_VERSION:
+        raise NativeLibraryError("libmoss_tts_b200.so ABI version mismatch; rebuild it")
+    return lib
+
+
+def call(name: str, *args) -> None:
+    rc = getattr(library(), name)(*args)
+    if rc:
+        raise RuntimeError(f"{name} failed: CUDA error {rc}")
+
+
+def ptr(t) -> int | None:
+    """Device address of a tensor (None for a missing optional tensor)."""
+    return None if t is None else t.data_ptr()
+
+
+def stream_of(t) -> int:
+    import torch
+    return torch.cuda.current_stream(t.device).cuda_stream

@@ -1,0 +1,320 @@
+"""Kernel parity on a B200: each C-ABI entry point against the oracle and the golden fixtures.
+
+Bars (from the north star): dequantized bf16 weights bit-exact; projections and layer
+outputs within max-abs 2e-2 / relative 1e-2 of the oracle (bf16 in, fp32 accumulate);
+integer/index outputs (embedding sums of bf16 adds, cache rows, token ids) exact.
+"""
+import zlib
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import golden
+from oracle import ops, quant
+from oracle.numerics import bf16_bits, from_bf16_bits
+
+from moss_tts._runtime import kernels, quantized, synthetic
+
+pytestmark = pytest.mark.gpu
+ATOL, RTOL = 2e-2, 1e-2
+
+
+def dev_bf16(bits, device):
+    a = np.ascontiguousarray(bits, dtype=np.uint16)
+    return torch.from_numpy(a.view(np.int16)).view(torch.bfloat16).to(device)
+
+
+def host_bits(t):
+    return t.detach().to("cpu").contiguous().view(torch.int16).numpy().view(np.uint16)
+
+
+def close(y_bits, ref, atol=ATOL, rtol=RTOL):
+    y = from_bf16_bits(y_bits).astype(np.float64)
+    ref = np.asarray(ref, dtype=np.float64)
+    err = np.abs(y - ref)
+    bad = err > atol + rtol * np.abs(ref)
+    assert not bad.any(), f"max err {err.max():.4g} at {np.argmax(err)}; {bad.sum()} outside tolerance"
+    return err.max()
+
+
+def upload_w4(p, device):
+    return (torch.from_numpy(np.ascontiguousarray(p["qweight"])).to(device),
+            dev_bf16(p["scales"], device),
+            None if p.get("qzeros") is None else torch.from_numpy(np.ascontiguousarray(p["qzeros"])).to(device))
+
+
+# ------------------------------------------------------------------ dequantization
+def test_dequant_bit_exact_zero_point(cuda_device):
+    g = golden("quant")
+    qw, sc, qz = upload_w4({"qweight": g["zp_qweight"], "scales": g["zp_scales"], "qzeros": g["zp_qzeros"]},
+                           cuda_device)
+    w = quantized.dequantize_packed(qw, sc, qz)
+    assert np.array_equal(host_bits(w), g["zp_dequant"])
+
+
+def test_dequant_bit_exact_reference_signed_export(cuda_device):
+    g = golden("quant")
+    qw = torch.from_numpy(quant.signed_to_unsigned(g["signed_packed"])).to(cuda_device)
+    w = quantized.dequantize_packed(qw, dev_bf16(g["signed_scales"], cuda_device), None)
+    assert np.array_equal(host_bits(w), g["signed_dequant"])
+
+
+def test_dequant_config0_checksum(cuda_device):
+    g = golden("quant")
+    rng = np.random.Generator(np.random.PCG64(0))
+    big = synthetic.quantized(rng, 12288, 4096, 32, True)
+    w = quantized.dequantize_packed(*upload_w4(big, cuda_device))
+    assert zlib.crc32(host_bits(w).tobytes()) == int(g["config0_dequant_crc32"][0])
+
+
+# ------------------------------------------------------------------ W4A16 linear
+def test_w4a16_config0_matches_reference(cuda_device):
+    g = golden("linear")
+    rng = np.random.Generator(np.random.PCG64(0))
+    big = synthetic.quantized(rng, 12288, 4096, 32, True)
+    x = dev_bf16(synthetic.activation(1, (1, 4096)), cuda_device)
+    y = quantized.linear(x, *upload_w4(big, cuda_device))
+    close(host_bits(y), from_bf16_bits(g["config0_y"]))
+    # and against the oracle's dequantize-then-matmul
+    w = quant.dequantize_w4(big["qweight"], big["scales"], big["qzeros"])
+    close(host_bits(y), ops.linear(from_bf16_bits(synthetic.activation(1, (1, 4096))), w))
+
+
+@pytest.mark.parametrize("b", [1, 3, 8])
+def test_w4a16_small_batches(cuda_device, b):
+    g = golden("linear")
+    p = {"qweight": g["small_qweight"], "scales": g["small_scales"], "qzeros": g["small_qzeros"]}
+    y = quantized.linear(dev_bf16(g[f"small_x{b}"], cuda_device), *upload_w4(p, cuda_device))
+    close(host_bits(y), from_bf16_bits(g[f"small_y{b}"]))
+
+
+@pytest.mark.parametrize("n,k,zeros", [(4096, 12288, True), (512, 512, True), (4096, 1536, True),
+                                       (6144, 4096, False), (64, 128, True), (1024, 3072, False)])
+def test_w4a16_shapes_against_oracle(cuda_device, n, k, zeros):
+    rng = np.random.Generator(np.random.PCG64(n * 7 + k))
+    p = synthetic.quantized(rng, n, k, 32, zeros)
+    xb = synthetic.activation(n + k, (1, k))
+    y = quantized.linear(dev_bf16(xb, cuda_device), *upload_w4(p, cuda_device))
+    ref = ops.linear(from_bf16_bits(xb), quant.dequantize_w4(p["qweight"], p["scales"], p["qzeros"]))
+    close(host_bits(y), ref)
+
+
+@pytest.mark.parametrize("b", [1, 2, 5, 8])
+def test_w4a16_paired_silu_and_norm(cuda_device, b):
+    rng = np.random.Generator(np.random.PCG64(90 + b))
+    p = synthetic.quantized(rng, 2 * 1536, 4096, 32, True)
+    x = synthetic.activation(91, (b, 4096))
+    r = synthetic.activation(92, (b, 4096))
+    nw = synthetic.activation(93, (4096,), 0.02)
+    nw = bf16_bits(from_bf16_bits(nw) + 1.0)
+    w = quant.dequantize_w4(p["qweight"], p["scales"], p["qzeros"])
+    # add + norm + paired projection
+    summed, y = quantized.norm_linear(dev_bf16(x, cuda_device), dev_bf16(r, cuda_device),
+                                      dev_bf16(nw, cuda_device), 1e-6, *upload_w4(p, cuda_device),
+                                      paired=True)
+    s_ref, h_ref = ops.add_rmsnorm(from_bf16_bits(x), from_bf16_bits(r), from_bf16_bits(nw), 1e-6)
+    assert np.array_equal(host_bits(summed), bf16_bits(s_ref))
+    close(host_bits(y), ops.silu_mul(ops.linear(h_ref, w)))
+    # norm only, unpaired
+    s2, y2 = quantized.norm_linear(dev_bf16(x, cuda_device), None, dev_bf16(nw, cuda_device), 1e-6,
+                                   *upload_w4(p, cuda_device))
+    close(host_bits(y2), ops.linear(ops.rmsnorm(from_bf16_bits(x), from_bf16_bits(nw), 1e-6), w))
+
+
+def test_mlp_config1(cuda_device):
+    """Config 1: RMSNorm -> gate/up -> SiLU*up -> down at batch 1, 4, 8 vs the HF reference."""
+    g = golden("mlp")
+    rng = np.random.Generator(np.random.PCG64(71))
+    gu = synthetic.quantized(rng, 2 * 12288, 4096, 32, True)
+    dn = synthetic.quantized(rng, 4096, 12288, 32, True)
+    nw = synthetic._normal_bf16(rng, (4096,), 0.02, 1.0)
+    gu_d, dn_d = upload_w4(gu, cuda_device), upload_w4(dn, cuda_device)
+    for b in (1, 4, 8):
+        x = dev_bf16(synthetic.activation(80 + b, (b, 4096)), cuda_device)
+        _, mid = quantized.norm_linear(x, None, dev_bf16(nw, cuda_device), 1e-6, *gu_d, paired=True)
+        y = quantized.linear(mid, *dn_d)
+        close(host_bits(y), from_bf16_bits(g[f"b{b}_y"]), 5e-2, 2e-2)
+
+
+# ------------------------------------------------------------------ small operators
+def test_rmsnorm_add_rmsnorm(cuda_device):
+    g = golden("ops")
+    x, r, w = (dev_bf16(g[k], cuda_device) for k in ("norm_x", "norm_r", "norm_w"))
+    y = kernels.rmsnorm(x, w, 1e-6)
+    assert np.mean(host_bits(y) == g["rmsnorm_y"]) > 0.999
+    close(host_bits(y), from_bf16_bits(g["rmsnorm_y"]), 1e-2, 8e-3)
+    s, y2 = kernels.add_rmsnorm(x, r, w, 1e-6)
+    assert np.array_equal(host_bits(s), g["add_sum"])
+    assert np.mean(host_bits(y2) == g["add_y"]) > 0.999
+
+
+def test_silu_mul(cuda_device):
+    g = golden("ops")
+    y = kernels.silu_mul(dev_bf16(g["silu_in"], cuda_device))
+    assert np.mean(host_bits(y) == g["silu_out"]) > 0.995
+    close(host_bits(y), from_bf16_bits(g["silu_out"]))
+
+
+def test_embedding_sum_exact(cuda_device):
+    g = golden("ops")
+    rng = np.random.Generator(np.random.PCG64(47))
+    text = dev_bf16(synthetic._normal_bf16(rng, (2048, 4096)), cuda_device)
+    audio = dev_bf16(synthetic._normal_bf16(rng, (32, 1025, 4096)), cuda_device)
+    ids = torch.from_numpy(g["emb_ids"]).to(cuda_device)
+    y = kernels.embedding_sum(ids, text, audio)
+    assert np.array_equal(host_bits(y), g["emb_out"])
+
+
+def test_linear_decode_bf16(cuda_device):
+    rng = np.random.Generator(np.random.PCG64(5))
+    w = synthetic._normal_bf16(rng, (1030 // 2 * 2 - 2, 4096))
+    for b in (1, 3):
+        x = synthetic.activation(6 + b, (b, 4096))
+        y = kernels.linear_decode(dev_bf16(x, cuda_device), dev_bf16(w, cuda_device))
+        close(host_bits(y), ops.linear(from_bf16_bits(x), from_bf16_bits(w)))
+
+
+# ------------------------------------------------------------------ attention
+class _Cache:
+    class _Layer:
+        def __init__(self, k, v):
+            self.keys, self.values = k, v
+
+    def __init__(self, k, v):
+        self.layers = [self._Layer(k, v)]
+
+
+def _rope(device, length):
+    from moss_tts._runtime.engine import rope_tables
+    cos, sin = rope_tables(length)
+    return cos.to(device), sin.to(device)
+
+
+def test_rope_tables_match_transformers():
+    from moss_tts._runtime.engine import rope_tables
+    g = golden("ops")
+    cos, sin = rope_tables(4096)
+    pos = torch.from_numpy(g["rope_positions"])
+    assert np.array_equal(cos[pos].view(torch.int16).numpy().view(np.uint16), g["rope_cos"])
+    assert np.array_equal(sin[pos].view(torch.int16).numpy().view(np.uint16), g["rope_sin"])
+
+
+@pytest.mark.parametrize("ctx", [0, 1, 31, 96, 777, 2048])
+def test_attention_decode_against_oracle(cuda_device, ctx):
+    L = max(ctx + 1, 128)
+    g = golden("ops")
+    kc = synthetic.activation(300 + ctx, (1, 8, L, 128))
+    vc = synthetic.activation(400 + ctx, (1, 8, L, 128))
+    qkv = synthetic.activation(500 + ctx, (6144,))
+    qn, kn = g["rope_qn"], g["rope_kn"]
+    cos, sin = _rope(cuda_device, L)
+    kd, vd = dev_bf16(kc, cuda_device), dev_bf16(vc, cuda_device)
+    pos = torch.tensor([ctx], device=cuda_device)
+    out = kernels.qk_rope_decode(dev_bf16(qkv, cuda_device), dev_bf16(qn, cuda_device),
+                                 dev_bf16(kn, cuda_device), cos, sin, _Cache(kd, vd), 0, pos, 1e-6)
+    c_ref, s_ref = ops.rope_table([ctx])
+    q, krow, vrow = ops.qk_rope(from_bf16_bits(qkv), from_bf16_bits(qn), from_bf16_bits(kn),
+                                c_ref[0], s_ref[0], 1e-6)
+    kf, vf = from_bf16_bits(kc)[0].copy(), from_bf16_bits(vc)[0].copy()
+    kf[:, ctx], vf[:, ctx] = krow, vrow
+    # cache rows written by the kernel equal the oracle's rows exactly (bf16 rounding points match)
+    assert np.mean(host_bits(kd)[0, :, ctx] == bf16_bits(krow)) > 0.995
+    assert np.array_equal(host_bits(vd)[0, :, ctx], bf16_bits(vrow))
+    ref = ops.attention_decode(q, kf, vf, ctx)
+    close(host_bits(out).reshape(-1), ref)
+    # rows other than `ctx` are untouched
+    assert np.array_equal(np.delete(host_bits(kd)[0], ctx, axis=1), np.delete(kc[0], ctx, axis=1))
+
+
+def test_qk_norm_rope_matches_transformers(cuda_device):
+    g = golden("ops")
+    L = 128
+    cos, sin = _rope(cuda_device, L)
+    kd = torch.zeros((1, 8, L, 128), device=cuda_device, dtype=torch.bfloat16)
+    vd = torch.zeros_like(kd)
+    qo = torch.empty((32, 128), device=cuda_device, dtype=torch.bfloat16)
+    from moss_tts._runtime import native
+    pos = torch.tensor([77], device=cuda_device)
+    qkv = dev_bf16(g["rope_qkv"], cuda_device)
+    qn, kn = dev_bf16(g["rope_qn"], cuda_device), dev_bf16(g["rope_kn"], cuda_device)  # keep alive
+    native.call("mt_qk_rope_kv", qkv.data_ptr(), qn.data_ptr(), kn.data_ptr(), cos.data_ptr(),
+                sin.data_ptr(), pos.data_ptr(),
+                qo.data_ptr(), kd.data_ptr(), vd.data_ptr(), 1, 32, 8, L, 1e-6, None, 0,
+                torch.cuda.current_stream().cuda_stream)
+    assert np.mean(host_bits(qo) == g["rope_q"]) > 0.995
+    close(host_bits(qo), from_bf16_bits(g["rope_q"]))
+    close(host_bits(kd)[0, :, 77], from_bf16_bits(g["rope_k"]))
+
+
+def test_attention_ragged_batch(cuda_device):
+    """Config 4 shape: several sequences with different live lengths in one launch."""
+    from moss_tts._runtime import native
+    g = golden("ops")
+    lens = [256, 1000, 4095, 3]
+    B, L = len(lens), 4096
+    kc = synthetic.activation(700, (B, 8, L, 128))
+    vc = synthetic.activation(701, (B, 8, L, 128))
+    qkv = synthetic.activation(702, (B, 6144))
+    cos, sin = _rope(cuda_device, L)
+    kd, vd = dev_bf16(kc, cuda_device), dev_bf16(vc, cuda_device)
+    pos = torch.tensor(lens, device=cuda_device)
+    out = torch.empty((B, 4096), device=cuda_device, dtype=torch.bfloat16)
+    splits = 20
+    partial = torch.empty(B * 8 * splits * 4 * 128, device=cuda_device)
+    lse = torch.empty(B * 8 * splits * 4, device=cuda_device)
+    tickets = torch.zeros(B * 8, device=cuda_device, dtype=torch.int32)
+    qn, kn = dev_bf16(g["rope_qn"], cuda_device), dev_bf16(g["rope_kn"], cuda_device)
+    native.call("mt_attention_decode", dev_bf16(qkv, cuda_device).data_ptr(), qn.data_ptr(), kn.data_ptr(),
+                cos.data_ptr(), sin.data_ptr(), pos.data_ptr(), kd.data_ptr(), vd.data_ptr(), out.data_ptr(),
+                partial.data_ptr(), lse.data_ptr(), tickets.data_ptr(), B, 32, 8, L, splits, 1e-6, None, 0,
+                torch.cuda.current_stream().cuda_stream)
+    assert int(tickets.abs().sum()) == 0
+    c_all, s_all = ops.rope_table(lens)
+    for b, p in enumerate(lens):
+        q, krow, vrow = ops.qk_rope(from_bf16_bits(qkv[b]), from_bf16_bits(g["rope_qn"]),
+                                    from_bf16_bits(g["rope_kn"]), c_all[b], s_all[b], 1e-6)
+        kf, vf = from_bf16_bits(kc[b]).copy(), from_bf16_bits(vc[b]).copy()
+        kf[:, p], vf[:, p] = krow, vrow
+        close(host_bits(out[b]), ops.attention_decode(q, kf, vf, p))
+
+
+# ------------------------------------------------------------------ heads
+def test_heads_greedy_against_oracle(cuda_device):
+    from moss_tts._runtime import native
+    rng = np.random.Generator(np.random.PCG64(123))
+    H = 4096
+    x, r = synthetic.activation(124, (H,)), synthetic.activation(125, (H,))
+    nw = bf16_bits(from_bf16_bits(synthetic.activation(126, (H,), 0.02)) + 1.0)
+    text_head = synthetic._normal_bf16(rng, (2, H))
+    audio = synthetic._normal_bf16(rng, (32 * 1024, H))
+    text_ids = torch.tensor([7, 9], device=cuda_device)
+    best = torch.zeros(33, device=cuda_device, dtype=torch.int64)
+    ticket = torch.zeros(1, device=cuda_device, dtype=torch.int32)
+    tl = torch.empty(2, device=cuda_device, dtype=torch.bfloat16)
+    al = torch.empty(32 * 1024, device=cuda_device, dtype=torch.bfloat16)
+    hid = torch.empty(H, device=cuda_device, dtype=torch.bfloat16)
+    nxt = torch.empty(33, device=cuda_device, dtype=torch.long)
+    args = [dev_bf16(v, cuda_device) for v in (x, r, nw, text_head, audio)]
+    _, h_ref = ops.add_rmsnorm(from_bf16_bits(x), from_bf16_bits(r), from_bf16_bits(nw), 1e-6)
+    for alen, delay in ((32, -1), (5, -1), (32, 3), (32, 32)):
+        a_len = torch.tensor([alen], device=cuda_device)
+        d_len = torch.tensor([delay], device=cuda_device)
+        native.call("mt_heads_greedy", args[0].data_ptr(), args[1].data_ptr(), args[2].data_ptr(), 1e-6,
+                    hid.data_ptr(), args[3].data_ptr(), args[4].data_ptr(), tl.data_ptr(), al.data_ptr(),
+                    text_ids.data_ptr(), a_len.data_ptr(), d_len.data_ptr(), nxt.data_ptr(), best.data_ptr(),
+                    ticket.data_ptr(), H, 2, 32, 1024, 0, 32, 99, 98, 1024, 1, 0,
+                    torch.cuda.current_stream().cuda_stream)
+        ids_ref, t_ref, a_ref = ops.heads_greedy(h_ref, from_bf16_bits(text_head), from_bf16_bits(audio),
+                                                 np.array([7, 9]), alen, delay, 99, 98)
+        assert np.mean(host_bits(hid) == bf16_bits(h_ref)) > 0.999
+        close(host_bits(al), a_ref.reshape(-1))
+        close(host_bits(tl), t_ref)
+        got = nxt.cpu().numpy()
+        # identical ids except on a near-tie (top-2 oracle gap within 2 bf16 ulps at |logit| < 8)
+        a_ref = a_ref.reshape(32, 1024)
+        top2 = np.sort(a_ref, axis=1)[:, -2:]
+        for c in np.nonzero(got[1:] != ids_ref[1:])[0]:
+            assert top2[c, 1] - top2[c, 0] <= 0.0625, (alen, delay, c)
+        assert got[0] == ids_ref[0]
+        assert int(best.abs().sum()) == 0 and int(ticket.item()) == 0
