@@ -122,6 +122,23 @@ int mt_attention_decode(const void* qkv, const void* q_norm, const void* k_norm,
                         float eps, void* status, int flags, void* stream);
 
 /*
+ * mt_attention_decode for callers that cannot allocate device memory: code enqueueing
+ * work during CUDA-graph stream capture, real-time callbacks that must not block on an
+ * allocator, and FFI hosts without a device allocator. No counterpart in the reference.
+ * The split-K scratch is a fixed array inside this library (about 1.04 MiB per GPU that
+ * loads it, held until exit): batch*nkv*splits*(nq/nkv)*128 <= 262144 and
+ * batch*nkv <= 1024, otherwise cudaErrorMemoryAllocation (2) is returned and nothing is
+ * launched. The first call on a device resolves the array's device address, so make it
+ * before any stream capture. All calls on a device share the array: calls whose work
+ * overlaps on the GPU race and must be serialised by the caller. Never allocates.
+ */
+int mt_attention_decode_noalloc(const void* qkv, const void* q_norm, const void* k_norm,
+                                const void* cos_tab, const void* sin_tab, const void* positions,
+                                void* k_cache, void* v_cache, void* out, int batch, int nq, int nkv,
+                                int max_len, int splits, float eps, void* status, int flags,
+                                void* stream);
+
+/*
  * Output heads of one decode step with greedy selection: final add_rmsnorm of
  * (x + residual), logits of the n_text text-head rows and n_cb audio codebooks of `vocab`
  * rows each, argmax with the first-index tie rule, delay-pattern masks, next token ids

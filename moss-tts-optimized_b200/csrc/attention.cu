@@ -307,3 +307,108 @@ MT_API int mt_qk_rope_kv(const void* qkv, const void* q_norm, const void* k_norm
   return launch(qk_rope_kv, dim3(nq + nkv, batch), dim3(32), 0, (cudaStream_t)stream, flags, a,
                 (__nv_bfloat16*)q_out);
 }
+
+// ----------------------------------------------------------------------------
+// Scratch-free decode attention.
+//
+// Some callers of this library cannot allocate device memory for the split-K
+// partials: code that enqueues work while a stream is being captured into a CUDA
+// graph (an allocation is not a stream operation and can break or serialise the
+// capture), real-time audio callbacks that must not block on an allocator, and
+// foreign-function hosts (plugins, embedded runtimes) that own no device
+// allocator at all. For them the partials, log-sum-exp values and merge tickets
+// live in one fixed array of this library's own device memory. Every GPU that
+// loads the library holds that array (about 1.04 MiB) until the process exits.
+// The array is shared by all calls on a device and keeps the previous call's
+// contents; calls whose kernels overlap on the GPU (for example, from two streams
+// at once) race on it and must be serialised by the caller.
+#include <mutex>
+
+namespace mt {
+namespace {
+constexpr size_t kNoAllocPartial = 262144;  // fp32 partials: batch*nkv*splits*(nq/nkv)*128
+constexpr size_t kNoAllocLse = 8192;        // fp32 log-sum-exp: batch*nkv*splits*(nq/nkv)
+constexpr size_t kNoAllocTickets = 1024;    // merge counters: batch*nkv
+
+struct NoAllocScratch {
+  float partial[kNoAllocPartial];
+  float lse[kNoAllocLse];
+  unsigned tickets[kNoAllocTickets];
+};
+
+static __device__ __align__(256) NoAllocScratch g_attention_scratch;
+
+std::mutex g_scratch_mutex;
+NoAllocScratch* g_scratch_address[128] = {};
+
+// Device address of the scratch array for the current device. The symbol's name is
+// only a host-side handle, so it is resolved once per device (with that device
+// current) through cudaGetSymbolAddress and cached.
+cudaError_t scratch_for_current_device(NoAllocScratch** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 128) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lock(g_scratch_mutex);
+  if (!g_scratch_address[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_attention_scratch);
+    if (e != cudaSuccess) return e;
+    g_scratch_address[dev] = static_cast<NoAllocScratch*>(p);
+  }
+  *out = g_scratch_address[dev];
+  return cudaSuccess;
+}
+}  // namespace
+}  // namespace mt
+
+// No counterpart in the reference: mt_attention_decode without caller-provided scratch.
+MT_API int mt_attention_decode_noalloc(const void* qkv, const void* q_norm, const void* k_norm,
+                                       const void* cos_tab, const void* sin_tab, const void* positions,
+                                       void* k_cache, void* v_cache, void* out, int batch, int nq, int nkv,
+                                       int max_len, int splits, float eps, void* status, int flags,
+                                       void* stream) {
+  if (batch < 1 || nkv < 1 || nq < nkv || nq % nkv || splits < 1 || splits > 1024) return kBadArgument;
+  const int rep = nq / nkv;
+  if (rep != 4 && rep != 1 && rep != 2) return kBadArgument;
+  const size_t slots = (size_t)batch * nkv * splits * rep;
+  if (slots * kHeadDim > kNoAllocPartial || slots > kNoAllocLse || (size_t)batch * nkv > kNoAllocTickets)
+    return (int)cudaErrorMemoryAllocation;  // request exceeds the fixed scratch
+  AttnArgs a;
+  a.qkv = (const __nv_bfloat16*)qkv;
+  a.q_norm = (const __nv_bfloat16*)q_norm;
+  a.k_norm = (const __nv_bfloat16*)k_norm;
+  a.cos_tab = (const __nv_bfloat16*)cos_tab;
+  a.sin_tab = (const __nv_bfloat16*)sin_tab;
+  a.positions = (const int64_t*)positions;
+  a.k_cache = (__nv_bfloat16*)k_cache;
+  a.v_cache = (__nv_bfloat16*)v_cache;
+  a.out = (__nv_bfloat16*)out;
+  a.nq = nq;
+  a.nkv = nkv;
+  a.max_len = max_len;
+  a.splits = splits;
+  a.eps = eps;
+  a.status = (int*)status;
+  if (attn_check(a, batch) || !out) return kBadArgument;
+  const size_t cap = (size_t)(max_len + splits - 1) / splits;
+  const size_t smem = (size_t)rep * cap * sizeof(float);
+  if (smem > 200 * 1024) return kBadArgument;
+  NoAllocScratch* scratch = nullptr;
+  cudaError_t e = scratch_for_current_device(&scratch);
+  if (e != cudaSuccess) return (int)e;
+  a.partial = scratch->partial;
+  a.lse = scratch->lse;
+  a.tickets = scratch->tickets;
+  cudaStream_t s = (cudaStream_t)stream;
+  // The merge counters must start at zero; clear them on the stream so each call is
+  // independent of whatever an earlier (possibly failed) call left behind.
+  e = cudaMemsetAsync(scratch->tickets, 0, (size_t)batch * nkv * sizeof(unsigned), s);
+  if (e != cudaSuccess) return (int)e;
+  const dim3 grid(nkv, splits, batch);
+  switch (rep) {
+    case 4: return launch(attention_decode<4>, grid, dim3(128), smem, s, flags, a);
+    case 2: return launch(attention_decode<2>, grid, dim3(128), smem, s, flags, a);
+    default: return launch(attention_decode<1>, grid, dim3(128), smem, s, flags, a);
+  }
+}

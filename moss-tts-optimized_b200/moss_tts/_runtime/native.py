@@ -28,6 +28,7 @@ SIGNATURES = {
     "mt_embedding_sum": ([_P, _P, _P, _P, _I, _I, _I, _I, _I, _P, _I, _P], _I),
     "mt_qk_rope_kv": ([_P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _F, _P, _I, _P], _I),
     "mt_attention_decode": ([_P] * 12 + [_I] * 5 + [_F, _P, _I, _P], _I),
+    "mt_attention_decode_noalloc": ([_P] * 9 + [_I] * 5 + [_F, _P, _I, _P], _I),
     "mt_heads_greedy": ([_P, _P, _P, _F] + [_P] * 11 + [_I] * 11 + [_P], _I),
 }
 
