@@ -33,12 +33,21 @@ extern "C" {
 #endif
 
 #define MT_FLAG_PDL 1
+#define MT_FLAG_REGISTER_PIPELINE 2 /* mt_w4a16_linear: use the register-pipelined kernel at batch 1 */
 #define MT_LINEAR_NORM 1   /* RMSNorm prologue over each activation row            */
 #define MT_LINEAR_ADD 2    /* bf16 residual add before the norm (requires NORM)    */
 #define MT_LINEAR_PAIRED 4 /* rows [0,N/2) gate, [N/2,N) up; y = bf16(silu(g)) * u */
 
 /* ABI revision of this header (1). */
 int mt_abi_version(void);
+
+/*
+ * Diagnostic: copies the library's error word for the current device into *value (1 after a
+ * kernel abandoned a bounded wait on its own asynchronous copies, then drained them and
+ * returned early; 0 otherwise) and clears it when `clear` is non-zero. This one call is
+ * synchronous. No counterpart in the reference (its kernels never wait).
+ */
+int mt_read_error_word(int* value, int clear);
 
 /*
  * Bit-exact dequantization: out bf16 [n, k] = bf16((q - z) * s).
@@ -57,7 +66,9 @@ int mt_dequant_w4(const void* qweight, const void* scales, const void* qzeros, v
  * project (dp4a_packing.py:94-125; paired SiLU at :85-89) and the fused norm projection
  * dp4a_norm_projection.linear (dp4a_norm_projection.py:99-117), as W4A16 instead of W4A8.
  * Requires k % 128 == 0, n % 4 == 0 (n % 8 when PAIRED), x/residual/summed/norm_w 8-byte
- * and qweight 16-byte aligned.
+ * and qweight 16-byte aligned. Batch 1 with k/32 a multiple of 32 (k = 1024 ... 12288) and
+ * 16-byte aligned buffers runs the bulk-copy streaming kernel; flags bit 1
+ * (MT_FLAG_REGISTER_PIPELINE) selects the register-pipelined kernel instead.
  */
 int mt_w4a16_linear(const void* x, const void* residual, const void* norm_w, float eps,
                     void* summed, const void* qweight, const void* scales, const void* qzeros,

@@ -13,6 +13,7 @@ from pathlib import Path
 LIB_PATH = Path(__file__).with_name("libmoss_tts_b200.so")
 ABI_VERSION = 1
 FLAG_PDL = 1
+FLAG_REGISTER_PIPELINE = 2
 LINEAR_NORM, LINEAR_ADD, LINEAR_PAIRED = 1, 2, 4
 
 _P, _I, _F = ctypes.c_void_p, ctypes.c_int, ctypes.c_float
@@ -20,6 +21,7 @@ _P, _I, _F = ctypes.c_void_p, ctypes.c_int, ctypes.c_float
 # name -> (argtypes, restype); mirrors include/moss_tts_b200.h
 SIGNATURES = {
     "mt_abi_version": ([], _I),
+    "mt_read_error_word": ([ctypes.POINTER(ctypes.c_int), _I], _I),
     "mt_dequant_w4": ([_P, _P, _P, _P, _I, _I, _I, _P], _I),
     "mt_w4a16_linear": ([_P, _P, _P, _F, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P], _I),
     "mt_bf16_linear": ([_P, _P, _P, _F, _P, _P, _P, _I, _I, _I, _I, _I, _P], _I),
@@ -58,6 +60,13 @@ def call(name: str, *args) -> None:
     rc = getattr(library(), name)(*args)
     if rc:
         raise RuntimeError(f"{name} failed: CUDA error {rc}")
+
+
+def error_word(clear: bool = False) -> int:
+    """The library's device error word (1 after a kernel gave up a bounded wait)."""
+    v = ctypes.c_int(0)
+    call("mt_read_error_word", ctypes.byref(v), 1 if clear else 0)
+    return v.value
 
 
 def ptr(t) -> int | None:

@@ -22,7 +22,9 @@ def header_prototypes():
         args = [a.strip() for a in m.group(2).split(",") if a.strip() and a.strip() != "void"]
         kinds = []
         for a in args:
-            if "*" in a:
+            if a.startswith("int*"):
+                kinds.append("ip")
+            elif "*" in a:
                 kinds.append("p")
             elif a.startswith("float"):
                 kinds.append("f")
@@ -59,7 +61,7 @@ def test_library_exports_every_declared_symbol(lib):
 
 def test_ctypes_signatures_match_header():
     from moss_tts._runtime import native
-    kind = {ctypes.c_void_p: "p", ctypes.c_int: "i", ctypes.c_float: "f"}
+    kind = {ctypes.c_void_p: "p", ctypes.c_int: "i", ctypes.c_float: "f", ctypes.POINTER(ctypes.c_int): "ip"}
     protos = header_prototypes()
     assert set(native.SIGNATURES) == set(protos)
     for name, (args, res) in native.SIGNATURES.items():

@@ -47,7 +47,9 @@ def test_teacher_forced_decode_matches_reference(model):
         nxt = eng.step(torch.from_numpy(g["ids"][step]), step, alen, delay).reshape(-1).cpu().numpy()
         bad = nxt != g["next"][step]
         if bad.any():
-            assert not bad[0], step
+            if bad[0]:  # text channel: the reference's two text logits must be a near-tie
+                t = from_bf16_bits(g["text"][step])
+                assert abs(float(t[0] - t[1])) <= 0.0625, step
             margins = g["audio_top2"][step][bad[1:]]
             assert np.all(margins <= 0.0625), (step, margins)
             mismatched += int(bad.sum())
