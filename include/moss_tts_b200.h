@@ -154,7 +154,8 @@ int mt_attention_decode_noalloc(const void* qkv, const void* q_norm, const void*
  * (x + residual), logits of the n_text text-head rows and n_cb audio codebooks of `vocab`
  * rows each, argmax with the first-index tie rule, delay-pattern masks, next token ids
  * int64 [1 + n_vq] (entries of this shard's codebooks, plus the text token when
- * text_owner != 0). Replaces the head half of FastLLM._decode with greedy sampling
+ * text_owner != 0). hidden_size 4096 runs the bulk-copy streaming kernel; flags bit 1 selects
+ * the register-pipelined one. Replaces the head half of FastLLM._decode with greedy sampling
  * (src/moss_tts/_runtime/llm.py:268-287). Scratch: best uint64 [1 + n_cb] and ticket
  * uint32 [1], zero before the first call and left zero by every call.
  */

@@ -9,8 +9,10 @@
 //      layer (the reference reads each KV head once per query head);
 //   3. the log-sum-exp merge of the splits, done by the last CTA of each KV head
 //      to finish (a ticket counter in scratch memory, reset by that CTA).
-// Split boundaries follow the live length read on the device (split = ceil(len /
-// splits) tokens), so a graph captured once serves every position.
+// Split boundaries follow the live length read on the device (span = max(64, ceil(len /
+// splits)) tokens), so a graph captured once serves every position. Each CTA fetches its
+// contiguous K and V row ranges into shared memory with two bulk copies issued before
+// the programmatic-dependency wait.
 // Scratch (fp32 partials, LSE, tickets) is caller-provided global memory.
 #include "common.cuh"
 
@@ -59,81 +61,150 @@ __device__ __forceinline__ void norm_rope_head(float (&x)[4], const __nv_bfloat1
   }
 }
 
+constexpr int kMinSpan = 64;  // fewest tokens a split handles (short contexts use few splits)
+
+// Tokens of the longest split for a cache of max_len rows and `splits` splits.
+__host__ __device__ __forceinline__ int attn_cap(int max_len, int splits) {
+  const int even = (max_len + splits - 1) / splits;
+  return even > kMinSpan ? even : kMinSpan;
+}
+
+__device__ __forceinline__ uint32_t attn_smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+// Rotated 16-byte chunk of row t: thread-specific start so that eight threads reading
+// different 256-byte rows at the same step touch eight different bank groups.
+__device__ __forceinline__ int rot(int j, int t) { return (j + t) & 15; }
+
 template <int REP>
 __global__ void __launch_bounds__(128) attention_decode(AttnArgs a) {
-  extern __shared__ float lg[];  // [REP][cap]
-  __shared__ float qs[REP][kHeadDim];
+  extern __shared__ __align__(128) uint8_t sm[];
+  __shared__ __align__(16) __nv_bfloat16 qs[REP][kHeadDim];
   __shared__ float stat[REP][2];
+  __shared__ __align__(8) uint64_t bar;
   __shared__ unsigned last;
   const int kh = blockIdx.x, split = blockIdx.y, b = blockIdx.z;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int qkv_w = (a.nq + 2 * a.nkv) * kHeadDim;
+  const int cap = attn_cap(a.max_len, a.splits);
+  __nv_bfloat16* ks = reinterpret_cast<__nv_bfloat16*>(sm);                  // [cap][128]
+  __nv_bfloat16* vs = ks + (size_t)cap * kHeadDim;                           // [cap][128]
+  float* lg = reinterpret_cast<float*>(vs + (size_t)cap * kHeadDim);         // [REP][cap]
+
+  // The position and every cache row before it were written before this kernel's
+  // predecessor started (earlier steps), so the K/V rows of this split are fetched
+  // before the dependency wait; row `position` itself is recomputed below.
+  int64_t pos = a.positions[b];
+  const bool bad_pos = pos < 0 || pos >= a.max_len;
+  if (bad_pos) pos = pos < 0 ? 0 : a.max_len - 1;
+  const int p = (int)pos, len = p + 1;
+  int span = (len + a.splits - 1) / a.splits;
+  if (span < kMinSpan) span = kMinSpan;
+  const int t0 = split * span, t1 = min(t0 + span, len);
+  const int n = t1 > t0 ? t1 - t0 : 0;
+  const size_t kv_base = ((size_t)b * a.nkv + kh) * a.max_len * kHeadDim;
+  if (tid == 0) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(attn_smem_u32(&bar)) : "memory");
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    if (n > 0) {
+      const unsigned bytes = (unsigned)(n * kHeadDim * 2);
+      asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(attn_smem_u32(&bar)),
+                   "r"(2 * bytes) : "memory");
+      asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                       attn_smem_u32(ks)), "l"(a.k_cache + kv_base + (size_t)t0 * kHeadDim), "r"(bytes),
+                   "r"(attn_smem_u32(&bar)) : "memory");
+      asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                       attn_smem_u32(vs)), "l"(a.v_cache + kv_base + (size_t)t0 * kHeadDim), "r"(bytes),
+                   "r"(attn_smem_u32(&bar)) : "memory");
+    }
+  }
+  __syncthreads();  // the barrier is initialised before any thread polls it
   pdl_wait();
   pdl_trigger();
-  int64_t pos = a.positions[b];
-  if (pos < 0 || pos >= a.max_len) {  // host validates; never index out of the cache
-    if (a.status && tid == 0) atomicExch(a.status, 1);
-    pos = pos < 0 ? 0 : a.max_len - 1;
-  }
-  const int p = (int)pos, len = p + 1;
-  const int span = (len + a.splits - 1) / a.splits;
-  const int t0 = split * span, t1 = min(t0 + span, len);
+  if (bad_pos && a.status && tid == 0) atomicExch(a.status, 1);
   const __nv_bfloat16* src = a.qkv + (size_t)b * qkv_w;
-  const size_t kv_base = ((size_t)b * a.nkv + kh) * a.max_len * kHeadDim;
 
-  // 1. Query heads of this KV head (warp w < REP handles head kh*REP + w).
+  // 1. Query heads of this KV head (warp w < REP handles head kh*REP + w), rounded to bf16
+  //    as the reference stores them (kernels.py:165).
   if (warp < REP) {
     const int h = kh * REP + warp;
     float x[4];
     const uint2 r = *reinterpret_cast<const uint2*>(src + h * kHeadDim + 4 * lane);
     x[0] = bf16_lo(r.x); x[1] = bf16_hi(r.x); x[2] = bf16_lo(r.y); x[3] = bf16_hi(r.y);
-    norm_rope_head(x, a.q_norm, a.cos_tab + (size_t)p * kHeadDim, a.sin_tab + (size_t)p * kHeadDim,
-                   a.eps, lane);
-#pragma unroll
-    for (int i = 0; i < 4; ++i) qs[warp][4 * lane + i] = x[i];
-  }
-  // The split holding the newest token writes this step's K/V cache rows.
-  if (t0 <= p && p < t1 && warp == 0) {
-    float x[4];
-    const uint2 r = *reinterpret_cast<const uint2*>(src + (a.nq + kh) * kHeadDim + 4 * lane);
-    x[0] = bf16_lo(r.x); x[1] = bf16_hi(r.x); x[2] = bf16_lo(r.y); x[3] = bf16_hi(r.y);
-    norm_rope_head(x, a.k_norm, a.cos_tab + (size_t)p * kHeadDim, a.sin_tab + (size_t)p * kHeadDim,
-                   a.eps, lane);
+    norm_rope_head(x, a.q_norm, a.cos_tab + (size_t)p * kHeadDim, a.sin_tab + (size_t)p * kHeadDim, a.eps, lane);
     __nv_bfloat162 lo = __floats2bfloat162_rn(x[0], x[1]), hi = __floats2bfloat162_rn(x[2], x[3]);
     uint2 o;
     o.x = *reinterpret_cast<uint32_t*>(&lo);
     o.y = *reinterpret_cast<uint32_t*>(&hi);
-    *reinterpret_cast<uint2*>(a.k_cache + kv_base + (size_t)p * kHeadDim + 4 * lane) = o;
-    const uint2 v = *reinterpret_cast<const uint2*>(src + (a.nq + a.nkv + kh) * kHeadDim + 4 * lane);
-    *reinterpret_cast<uint2*>(a.v_cache + kv_base + (size_t)p * kHeadDim + 4 * lane) = v;
+    *reinterpret_cast<uint2*>(&qs[warp][4 * lane]) = o;
+  }
+  // 2. The split holding the newest token computes and writes this step's K/V rows.
+  const bool owner = t0 <= p && p < t1;
+  uint2 krow = make_uint2(0, 0), vrow = make_uint2(0, 0);
+  if (owner && warp == 0) {
+    float x[4];
+    const uint2 r = *reinterpret_cast<const uint2*>(src + (a.nq + kh) * kHeadDim + 4 * lane);
+    x[0] = bf16_lo(r.x); x[1] = bf16_hi(r.x); x[2] = bf16_lo(r.y); x[3] = bf16_hi(r.y);
+    norm_rope_head(x, a.k_norm, a.cos_tab + (size_t)p * kHeadDim, a.sin_tab + (size_t)p * kHeadDim, a.eps, lane);
+    __nv_bfloat162 lo = __floats2bfloat162_rn(x[0], x[1]), hi = __floats2bfloat162_rn(x[2], x[3]);
+    krow.x = *reinterpret_cast<uint32_t*>(&lo);
+    krow.y = *reinterpret_cast<uint32_t*>(&hi);
+    vrow = *reinterpret_cast<const uint2*>(src + (a.nq + a.nkv + kh) * kHeadDim + 4 * lane);
+    *reinterpret_cast<uint2*>(a.k_cache + kv_base + (size_t)p * kHeadDim + 4 * lane) = krow;
+    *reinterpret_cast<uint2*>(a.v_cache + kv_base + (size_t)p * kHeadDim + 4 * lane) = vrow;
+  }
+  // 3. Wait (bounded) for this split's K/V rows; patch in the fresh row.
+  auto wait_copies = [&]() -> bool {
+    for (long it = 0; it < (1L << 22); ++it) {
+      uint32_t done;
+      asm volatile("{\n .reg .pred q;\n mbarrier.try_wait.parity.shared::cta.b64 q, [%1], 0;\n selp.u32 %0, 1, 0, q;\n}"
+                   : "=r"(done) : "r"(attn_smem_u32(&bar)) : "memory");
+      if (done) return true;
+    }
+    return false;
+  };
+  const bool ok = n > 0 ? wait_copies() : true;
+  if (!__syncthreads_and(ok ? 1 : 0)) {
+    // The copies did not complete within the bound: raise the status, give them one more
+    // bounded chance to land (they target this CTA's shared memory), then leave this head
+    // unmerged.
+    if (tid == 0) {
+      if (a.status) atomicExch(a.status, 3);
+      wait_copies();
+    }
+    __syncthreads();
+    return;
+  }
+  if (owner && warp == 0) {
+    *reinterpret_cast<uint2*>(ks + (size_t)(p - t0) * kHeadDim + 4 * lane) = krow;
+    *reinterpret_cast<uint2*>(vs + (size_t)(p - t0) * kHeadDim + 4 * lane) = vrow;
   }
   __syncthreads();
 
-  const int n = t1 > t0 ? t1 - t0 : 0;
-  const int cap = (a.max_len + a.splits - 1) / a.splits;
   const size_t slot = (((size_t)b * a.nkv + kh) * a.splits + split) * REP;
   if (n > 0) {
-    // 2a. logits: warp w takes tokens t0 + w, t0 + w + 4, ...; lane holds 4 dims.
-    float qv[REP][4];
+    // 4. logits: item (token t, head i) per thread; 16-byte chunks in rotated order.
+    for (int item = tid; item < n * REP; item += 128) {
+      const int t = item / REP, i = item - t * REP;
+      const uint4* krow4 = reinterpret_cast<const uint4*>(ks + (size_t)t * kHeadDim);
+      const uint4* q4 = reinterpret_cast<const uint4*>(&qs[i][0]);
+      float d0 = 0.f, d1 = 0.f;
 #pragma unroll
-    for (int i = 0; i < REP; ++i)
-#pragma unroll
-      for (int j = 0; j < 4; ++j) qv[i][j] = qs[i][4 * lane + j];
-    for (int t = warp; t < n; t += 4) {
-      const uint2 kr = *reinterpret_cast<const uint2*>(a.k_cache + kv_base + (size_t)(t0 + t) * kHeadDim + 4 * lane);
-      const float k0 = bf16_lo(kr.x), k1 = bf16_hi(kr.x), k2 = bf16_lo(kr.y), k3 = bf16_hi(kr.y);
-#pragma unroll
-      for (int i = 0; i < REP; ++i) {
-        float d = qv[i][0] * k0;
-        d = fmaf(qv[i][1], k1, d);
-        d = fmaf(qv[i][2], k2, d);
-        d = fmaf(qv[i][3], k3, d);
-        d = warp_sum(d);
-        if (lane == 0) lg[i * cap + t] = d * kScale;
+      for (int j = 0; j < 16; ++j) {
+        const int c = rot(j, t);
+        const uint4 kk = krow4[c], qq = q4[c];
+        d0 = fmaf(bf16_lo(qq.x), bf16_lo(kk.x), d0);
+        d1 = fmaf(bf16_hi(qq.x), bf16_hi(kk.x), d1);
+        d0 = fmaf(bf16_lo(qq.y), bf16_lo(kk.y), d0);
+        d1 = fmaf(bf16_hi(qq.y), bf16_hi(kk.y), d1);
+        d0 = fmaf(bf16_lo(qq.z), bf16_lo(kk.z), d0);
+        d1 = fmaf(bf16_hi(qq.z), bf16_hi(kk.z), d1);
+        d0 = fmaf(bf16_lo(qq.w), bf16_lo(kk.w), d0);
+        d1 = fmaf(bf16_hi(qq.w), bf16_hi(kk.w), d1);
       }
+      lg[i * cap + t] = (d0 + d1) * kScale;
     }
     __syncthreads();
-    // 2b. softmax statistics: warp i handles head i.
+    // 5. softmax statistics: warp i handles head i.
     if (warp < REP) {
       float m = -INFINITY;
       for (int t = lane; t < n; t += 32) m = fmaxf(m, lg[warp * cap + t]);
@@ -148,14 +219,14 @@ __global__ void __launch_bounds__(128) attention_decode(AttnArgs a) {
       if (lane == 0) { stat[warp][0] = m; stat[warp][1] = sum; }
     }
     __syncthreads();
-    // 2c. weighted V: thread d accumulates dim d for every head.
+    // 6. weighted V: thread d accumulates dim d for every head.
     float o[REP];
 #pragma unroll
     for (int i = 0; i < REP; ++i) o[i] = 0.f;
-    const __nv_bfloat16* vrow = a.v_cache + kv_base + (size_t)t0 * kHeadDim + tid;
-#pragma unroll 4
+    const __nv_bfloat16* vcol = vs + tid;
+#pragma unroll 8
     for (int t = 0; t < n; ++t) {
-      const float v = bf16f(vrow[(size_t)t * kHeadDim]);
+      const float v = bf16f(vcol[(size_t)t * kHeadDim]);
 #pragma unroll
       for (int i = 0; i < REP; ++i) o[i] = fmaf(lg[i * cap + t], v, o[i]);
     }
@@ -168,7 +239,7 @@ __global__ void __launch_bounds__(128) attention_decode(AttnArgs a) {
     if (tid < REP) a.lse[slot + tid] = -INFINITY;
   }
 
-  // 3. The last CTA of this KV head merges all splits (kernels.py:198-208).
+  // 7. The last CTA of this KV head merges all splits (kernels.py:198-208).
   __threadfence();
   __syncthreads();
   unsigned* ticket = a.tickets + (size_t)b * a.nkv + kh;
@@ -177,12 +248,15 @@ __global__ void __launch_bounds__(128) attention_decode(AttnArgs a) {
   if (!last) return;
   __threadfence();
   const size_t base = ((size_t)b * a.nkv + kh) * a.splits * REP;
+  const int active = (len + span - 1) / span;  // splits beyond this one hold no tokens
 #pragma unroll
   for (int i = 0; i < REP; ++i) {
     float m = -INFINITY;
-    for (int s = 0; s < a.splits; ++s) m = fmaxf(m, __ldcg(a.lse + base + s * REP + i));
+#pragma unroll 8
+    for (int s = 0; s < active; ++s) m = fmaxf(m, __ldcg(a.lse + base + s * REP + i));
     float wsum = 0.f, acc = 0.f;
-    for (int s = 0; s < a.splits; ++s) {
+#pragma unroll 8
+    for (int s = 0; s < active; ++s) {
       const float w = expf(__ldcg(a.lse + base + s * REP + i) - m);
       wsum += w;
       acc = fmaf(w, __ldcg(a.partial + (base + s * REP + i) * kHeadDim + tid), acc);
@@ -190,6 +264,11 @@ __global__ void __launch_bounds__(128) attention_decode(AttnArgs a) {
     a.out[(size_t)b * a.nq * kHeadDim + (kh * REP + i) * kHeadDim + tid] = to_bf16(acc / wsum);
   }
   if (tid == 0) *ticket = 0u;
+}
+
+static size_t attn_smem_bytes(int rep, int max_len, int splits) {
+  const size_t cap = (size_t)attn_cap(max_len, splits);
+  return cap * kHeadDim * 2 * 2 + (size_t)rep * cap * sizeof(float);
 }
 
 // Standalone QK-norm + RoPE + cache write (kernels.py:142-170): grid (nq + nkv, B).
@@ -272,8 +351,7 @@ MT_API int mt_attention_decode(const void* qkv, const void* q_norm, const void* 
     return kBadArgument;
   const int rep = nq / nkv;
   if (rep != 4 && rep != 1 && rep != 2) return kBadArgument;
-  const size_t cap = (size_t)(max_len + splits - 1) / splits;
-  const size_t smem = (size_t)rep * cap * sizeof(float);
+  const size_t smem = attn_smem_bytes(rep, max_len, splits);
   if (smem > 200 * 1024) return kBadArgument;
   const dim3 grid(nkv, splits, batch);
   cudaStream_t s = (cudaStream_t)stream;
@@ -391,8 +469,7 @@ MT_API int mt_attention_decode_noalloc(const void* qkv, const void* q_norm, cons
   a.eps = eps;
   a.status = (int*)status;
   if (attn_check(a, batch) || !out) return kBadArgument;
-  const size_t cap = (size_t)(max_len + splits - 1) / splits;
-  const size_t smem = (size_t)rep * cap * sizeof(float);
+  const size_t smem = attn_smem_bytes(rep, max_len, splits);
   if (smem > 200 * 1024) return kBadArgument;
   NoAllocScratch* scratch = nullptr;
   cudaError_t e = scratch_for_current_device(&scratch);

@@ -320,6 +320,9 @@ static cudaError_t bf16_mode(const Bf16Args& a, int mode, cudaStream_t s, int fl
   return bf16_paired<B, false, false>(a, paired, s, flags);
 }
 
+cudaError_t heads_stream_dispatch(const struct HeadsArgs& a, int flags, cudaStream_t s);
+bool heads_stream_supported(int hidden_size, int n_text, int n_cb, int vocab, int text_owner);
+
 }  // namespace mt
 
 using namespace mt;
@@ -417,11 +420,13 @@ MT_API int mt_heads_greedy(const void* x, const void* residual, const void* norm
   a.pad_code = pad_code;
   a.text_owner = text_owner;
   a.eps = eps;
+  if (!(flags & 2) && heads_stream_supported(hidden_size, n_text, n_cb, vocab, text_owner))
+    return (int)heads_stream_dispatch(a, flags & kFlagPdl, (cudaStream_t)stream);
   const int tasks = n_cb * vocab / 4 + (text_owner ? 1 : 0);
   int blocks = sm_count() * 2;
   const int need = (tasks + 7) / 8;
   if (blocks > need) blocks = need;
   if (blocks < 1) blocks = 1;
   return launch(heads_greedy, dim3(blocks), dim3(256), (size_t)hidden_size * 4,
-                (cudaStream_t)stream, flags, a);
+                (cudaStream_t)stream, flags & kFlagPdl, a);
 }

@@ -64,41 +64,55 @@ __global__ void silu_mul_rows(const __nv_bfloat16* __restrict__ x, __nv_bfloat16
 }
 
 // Text embedding plus the n_vq audio embeddings with a bf16 rounding after every
-// sequential addition (kernels.py:7-26). Each thread owns 8 hidden dims.
-__global__ void __launch_bounds__(128) embedding_sum_rows(const int64_t* __restrict__ ids,
-                                                          const __nv_bfloat16* __restrict__ text,
-                                                          const __nv_bfloat16* __restrict__ audio,
-                                                          __nv_bfloat16* __restrict__ out, int h,
-                                                          int vocab, int audio_vocab, int n_vq,
-                                                          int* status) {
+// sequential addition (kernels.py:7-26). Each thread owns 8 hidden dims; the rows it
+// adds are fetched in batches ahead of the (order-preserving) additions.
+constexpr int kEmbBatch = 11;
+
+__device__ __forceinline__ int64_t clamp_id(int64_t c, int limit, int* status) {
+  if (c < 0 || c >= limit) {  // never read outside the table
+    if (status) atomicExch(status, 2);
+    return 0;
+  }
+  return c;
+}
+
+__global__ void __launch_bounds__(64) embedding_sum_rows(const int64_t* __restrict__ ids,
+                                                         const __nv_bfloat16* __restrict__ text,
+                                                         const __nv_bfloat16* __restrict__ audio,
+                                                         __nv_bfloat16* __restrict__ out, int h, int vocab,
+                                                         int audio_vocab, int n_vq, int* status) {
   const int t = blockIdx.y;
   const int e = blockIdx.x * blockDim.x + threadIdx.x;  // 8-element slot
   pdl_wait();
   pdl_trigger();
   if (e * 8 >= h) return;
   const int64_t* row = ids + (size_t)t * (n_vq + 1);
-  int64_t tok = row[0];
-  if (tok < 0 || tok >= vocab) {  // never read outside the table
-    if (status) atomicExch(status, 2);
-    tok = 0;
-  }
+  const int64_t tok = clamp_id(row[0], vocab, status);
   const uint4 tv = *reinterpret_cast<const uint4*>(text + (size_t)tok * h + 8 * e);
   float v[8];
   const uint32_t tw[4] = {tv.x, tv.y, tv.z, tv.w};
 #pragma unroll
   for (int i = 0; i < 4; ++i) { v[2 * i] = bf16_lo(tw[i]); v[2 * i + 1] = bf16_hi(tw[i]); }
-  for (int q = 0; q < n_vq; ++q) {
-    int64_t c = row[q + 1];
-    if (c < 0 || c >= audio_vocab) {
-      if (status) atomicExch(status, 2);
-      c = 0;
-    }
-    const uint4 av = *reinterpret_cast<const uint4*>(audio + ((size_t)q * audio_vocab + c) * h + 8 * e);
-    const uint32_t aw[4] = {av.x, av.y, av.z, av.w};
+  for (int q0 = 0; q0 < n_vq; q0 += kEmbBatch) {
+    uint4 rows[kEmbBatch];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      v[2 * i] = round_bf16(v[2 * i] + bf16_lo(aw[i]));
-      v[2 * i + 1] = round_bf16(v[2 * i + 1] + bf16_hi(aw[i]));
+    for (int j = 0; j < kEmbBatch; ++j) {
+      const int q = q0 + j;
+      if (q < n_vq) {
+        const int64_t c = clamp_id(row[q + 1], audio_vocab, status);
+        rows[j] = *reinterpret_cast<const uint4*>(audio + ((size_t)q * audio_vocab + c) * h + 8 * e);
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < kEmbBatch; ++j) {
+      if (q0 + j < n_vq) {
+        const uint32_t aw[4] = {rows[j].x, rows[j].y, rows[j].z, rows[j].w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          v[2 * i] = round_bf16(v[2 * i] + bf16_lo(aw[i]));
+          v[2 * i + 1] = round_bf16(v[2 * i + 1] + bf16_hi(aw[i]));
+        }
+      }
     }
   }
   uint32_t o[4];
@@ -147,8 +161,8 @@ MT_API int mt_embedding_sum(const void* ids, const void* text, const void* audio
     return kBadArgument;
   if (!aligned(text, 16) || !aligned(audio, 16) || !aligned(out, 16) || !aligned(ids, 8))
     return kBadArgument;
-  const dim3 grid((h / 8 + 127) / 128, tokens);
-  return launch(embedding_sum_rows, grid, dim3(128), 0, (cudaStream_t)stream, flags,
+  const dim3 grid((h / 8 + 63) / 64, tokens);
+  return launch(embedding_sum_rows, grid, dim3(64), 0, (cudaStream_t)stream, flags,
                 (const int64_t*)ids, (const __nv_bfloat16*)text, (const __nv_bfloat16*)audio,
                 (__nv_bfloat16*)out, h, vocab, audio_vocab, n_vq, (int*)status);
 }

@@ -19,47 +19,13 @@
 // waits (bounded) for its outstanding copies and returns.
 #include <stdlib.h>
 
-#include "common.cuh"
+#include "stream_pipeline.cuh"
 
 namespace mt {
 
 __device__ int g_error_word;  // non-zero after a bounded wait expired (see mt_error_word)
 
 namespace {
-
-constexpr long kSpinLimit = 1L << 22;
-
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-  return (uint32_t)__cvta_generic_to_shared(p);
-}
-__device__ __forceinline__ void mbar_init(uint64_t* bar, unsigned count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
-}
-__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, unsigned bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
-               : "memory");
-}
-__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, unsigned parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
-      : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, unsigned parity) {
-  for (long i = 0; i < kSpinLimit; ++i)
-    if (mbar_try_wait(bar, parity)) return true;
-  return false;
-}
-__device__ __forceinline__ void bulk_copy(void* dst, const void* src, unsigned bytes, uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-          smem_u32(dst)),
-      "l"(src), "r"(bytes), "r"(smem_u32(bar))
-      : "memory");
-}
 
 __device__ __forceinline__ float magic_lo(uint32_t w) { return __uint_as_float((w & 0x000F0000u) | 0x43000000u); }
 __device__ __forceinline__ float magic_hi(uint32_t w) { return __uint_as_float((w & 0x0000F000u) | 0x45000000u); }
@@ -74,44 +40,9 @@ __device__ __forceinline__ void dot_word(uint32_t w, const float* x, float2& acc
   acc = __ffma2_rn(make_float2(magic_lo(r8), magic_hi(r16)), make_float2(x[6], x[7]), acc);
 }
 
-// Transposed warp reduction of N (power of two <= 32) per-lane values: afterwards lane l
-// holds the warp-wide sum of value index row_of<N>(l).
-template <int N>
-__device__ __forceinline__ float butterfly(float (&v)[N], int lane) {
-  int n = N;
-#pragma unroll
-  for (int o = 16; o >= 1; o >>= 1) {
-    if (n > 1) {
-      const bool upper = lane & o;
-#pragma unroll
-      for (int i = 0; i < N / 2; ++i) {
-        if (i < n / 2) {
-          const float send = upper ? v[i] : v[i + n / 2];
-          const float keep = upper ? v[i + n / 2] : v[i];
-          v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
-        }
-      }
-      n >>= 1;
-    } else {
-      v[0] += __shfl_xor_sync(0xffffffffu, v[0], o);
-    }
-  }
-  return v[0];
-}
-template <int N>
-__device__ __forceinline__ int row_of(int lane) {
-  int r = 0, n = N;
-#pragma unroll
-  for (int o = 16; o >= 1; o >>= 1) {
-    if (n > 1) {
-      r = r * 2 + ((lane & o) ? 1 : 0);
-      n >>= 1;
-    }
-  }
-  return r;
-}
-
 }  // namespace
+
+using namespace pipe;
 
 struct StreamArgs {
   const __nv_bfloat16* x;
@@ -145,9 +76,14 @@ __device__ __forceinline__ float fma_bf16_hi(uint32_t a, uint32_t b, float c) {
 }
 
 // One 8-code word against the thread's activation pairs xp[i] = (x[i], x[i+4]) (bf16x2):
-// acc.x/acc.y accumulate sum x * (128 + q) over the word.
+// acc.x/acc.y accumulate sum x * (128 + q) over the word. MULHI: the nibble shifts are
+// done as 32x32 multiply-high (w * 2^(32-s)) >> 32, which issues outside the logic pipe.
+template <bool MULHI>
 __device__ __forceinline__ void dot_word_mixed(uint32_t w, const uint32_t* xp, float2& acc) {
-  const uint32_t p0 = pair_magic(w), p1 = pair_magic(w >> 4), p2 = pair_magic(w >> 8), p3 = pair_magic(w >> 12);
+  const uint32_t s4 = MULHI ? __umulhi(w, 1u << 28) : (w >> 4);
+  const uint32_t s8 = MULHI ? __umulhi(w, 1u << 24) : (w >> 8);
+  const uint32_t s12 = MULHI ? __umulhi(w, 1u << 20) : (w >> 12);
+  const uint32_t p0 = pair_magic(w), p1 = pair_magic(s4), p2 = pair_magic(s8), p3 = pair_magic(s12);
   acc.x = fma_bf16_lo(p0, xp[0], acc.x);
   acc.y = fma_bf16_hi(p0, xp[0], acc.y);
   acc.x = fma_bf16_lo(p1, xp[1], acc.x);
@@ -158,18 +94,11 @@ __device__ __forceinline__ void dot_word_mixed(uint32_t w, const uint32_t* xp, f
   acc.y = fma_bf16_hi(p3, xp[3], acc.y);
 }
 
-__device__ __forceinline__ void named_sync(int id, int threads) {
-  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
-}
-__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
-}
-
 // Warp-specialized streaming GEMV. Warps [0, C) consume, warp C produces (bulk copies).
 // RS output rows per stage, NS stages, P row partitions, DOT: 0 = fp32 magic + FFMA2,
 // 1 = bf16 magic pairs + mixed-precision FMA. blockDim = P * G + 32.
 template <int RS, int NS, int P, int DOT, bool NORM, bool ADD, bool PAIRED>
-__global__ void __launch_bounds__(416, 1) w4a16_stream(StreamArgs a, int max_rows) {
+__global__ void __launch_bounds__(P * 128 + 32 > 416 ? P * 128 + 32 : 416, 1) w4a16_stream(StreamArgs a, int max_rows) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ __align__(8) uint64_t full[NS];
   __shared__ __align__(8) uint64_t empty[NS];
@@ -177,7 +106,7 @@ __global__ void __launch_bounds__(416, 1) w4a16_stream(StreamArgs a, int max_row
   constexpr int RP = RS / P;         // rows per partition per stage
   constexpr int NV = RP * H;         // values reduced per lane per stage
   static_assert(RS % P == 0 && (NV & (NV - 1)) == 0 && NV <= 32, "bad tile");
-  __shared__ float ssum[16];
+  __shared__ float ssum[32];
   __shared__ int failed;
 
   const int K = a.k, G = K >> 5;
@@ -350,10 +279,10 @@ __global__ void __launch_bounds__(416, 1) w4a16_stream(StreamArgs a, int max_row
             dot_word(w.z, xv + 16, d0);
             dot_word(w.w, xv + 24, d1);
           } else {
-            dot_word_mixed(w.x, xpair + 0, d0);
-            dot_word_mixed(w.y, xpair + 4, d1);
-            dot_word_mixed(w.z, xpair + 8, d0);
-            dot_word_mixed(w.w, xpair + 12, d1);
+            dot_word_mixed<DOT == 2>(w.x, xpair + 0, d0);
+            dot_word_mixed<DOT == 2>(w.y, xpair + 4, d1);
+            dot_word_mixed<DOT == 2>(w.z, xpair + 8, d0);
+            dot_word_mixed<DOT == 2>(w.w, xpair + 12, d1);
           }
           v = s * fmaf(-z, xsum, (d0.x + d1.x) + (d0.y + d1.y));
         }
@@ -402,13 +331,22 @@ size_t stream_smem(int rs, int ns, bool paired, int k, bool zeros, int cwarps, i
          (size_t)cwarps * max_rows * h * sizeof(float);
 }
 
+// Tuning knobs read once from the environment (defaults are the measured best):
+// MT_W4_DOT = 0 (fp32 magic + FFMA2), 1 (bf16 pairs + mixed FMA), 2 (as 1, multiply-high
+// shifts); MT_W4_PARTS = row partitions per CTA for K <= 4096 (2 or 4).
+static int env_int(const char* name, int dflt) {
+  const char* e = getenv(name);
+  return (e && e[0] >= '0' && e[0] <= '9') ? atoi(e) : dflt;
+}
 static int stream_dot_mode() {
   static int mode = -1;
-  if (mode < 0) {
-    const char* e = getenv("MT_W4_DOT");
-    mode = (e && e[0] == '0') ? 0 : 1;
-  }
+  if (mode < 0) mode = env_int("MT_W4_DOT", 1);
   return mode;
+}
+static int stream_parts() {
+  static int parts = -1;
+  if (parts < 0) parts = env_int("MT_W4_PARTS", 4) == 2 ? 2 : 4;
+  return parts;
 }
 
 template <int RS, int NS, int P, int DOT, bool NORM, bool ADD, bool PAIRED>
@@ -427,8 +365,11 @@ static cudaError_t go_dot(const StreamArgs& a, cudaStream_t s, int flags) {
 
 template <int RS, int NS, int P, bool NORM, bool ADD, bool PAIRED>
 static cudaError_t go(const StreamArgs& a, cudaStream_t s, int flags) {
-  return stream_dot_mode() == 0 ? go_dot<RS, NS, P, 0, NORM, ADD, PAIRED>(a, s, flags)
-                                : go_dot<RS, NS, P, 1, NORM, ADD, PAIRED>(a, s, flags);
+  switch (stream_dot_mode()) {
+    case 0: return go_dot<RS, NS, P, 0, NORM, ADD, PAIRED>(a, s, flags);
+    case 2: return go_dot<RS, NS, P, 2, NORM, ADD, PAIRED>(a, s, flags);
+    default: return go_dot<RS, NS, P, 1, NORM, ADD, PAIRED>(a, s, flags);
+  }
 }
 
 template <bool NORM, bool ADD>
@@ -437,6 +378,8 @@ static cudaError_t go_k(const StreamArgs& a, bool paired, cudaStream_t s, int fl
   if (G > 128) {  // wide K (down projection): one partition of G consumer threads
     return paired ? go<8, 2, 1, NORM, ADD, true>(a, s, flags) : go<8, 2, 1, NORM, ADD, false>(a, s, flags);
   }
+  if (stream_parts() == 4)
+    return paired ? go<8, 3, 4, NORM, ADD, true>(a, s, flags) : go<16, 3, 4, NORM, ADD, false>(a, s, flags);
   return paired ? go<8, 3, 2, NORM, ADD, true>(a, s, flags) : go<16, 3, 2, NORM, ADD, false>(a, s, flags);
 }
 
@@ -476,6 +419,10 @@ using namespace mt;
 
 // Diagnostic read of the library's error word on the current device (1 after a kernel
 // abandoned a bounded wait); optionally clears it. Synchronous, unlike every other call.
+namespace mt {
+cudaError_t heads_error_word(int* value, bool clear);
+}
+
 MT_API int mt_read_error_word(int* value, int clear) {
   if (!value) return kBadArgument;
   cudaError_t e = cudaMemcpyFromSymbol(value, g_error_word, sizeof(int));
@@ -483,5 +430,6 @@ MT_API int mt_read_error_word(int* value, int clear) {
     const int zero = 0;
     e = cudaMemcpyToSymbol(g_error_word, &zero, sizeof(int));
   }
+  if (e == cudaSuccess) e = heads_error_word(value, clear != 0);
   return (int)e;
 }

@@ -4,6 +4,7 @@ Bars (from the north star): dequantized bf16 weights bit-exact; projections and 
 outputs within max-abs 2e-2 / relative 1e-2 of the oracle (bf16 in, fp32 accumulate);
 integer/index outputs (embedding sums of bf16 adds, cache rows, token ids) exact.
 """
+import itertools
 import zlib
 
 import numpy as np
@@ -297,13 +298,14 @@ def test_heads_greedy_against_oracle(cuda_device):
     nxt = torch.empty(33, device=cuda_device, dtype=torch.long)
     args = [dev_bf16(v, cuda_device) for v in (x, r, nw, text_head, audio)]
     _, h_ref = ops.add_rmsnorm(from_bf16_bits(x), from_bf16_bits(r), from_bf16_bits(nw), 1e-6)
-    for alen, delay in ((32, -1), (5, -1), (32, 3), (32, 32)):
+    for (alen, delay), flags in itertools.product(((32, -1), (5, -1), (32, 3), (32, 32)), (0, 2)):
         a_len = torch.tensor([alen], device=cuda_device)
         d_len = torch.tensor([delay], device=cuda_device)
+        nxt.fill_(-7)
         native.call("mt_heads_greedy", args[0].data_ptr(), args[1].data_ptr(), args[2].data_ptr(), 1e-6,
                     hid.data_ptr(), args[3].data_ptr(), args[4].data_ptr(), tl.data_ptr(), al.data_ptr(),
                     text_ids.data_ptr(), a_len.data_ptr(), d_len.data_ptr(), nxt.data_ptr(), best.data_ptr(),
-                    ticket.data_ptr(), H, 2, 32, 1024, 0, 32, 99, 98, 1024, 1, 0,
+                    ticket.data_ptr(), H, 2, 32, 1024, 0, 32, 99, 98, 1024, 1, flags,
                     torch.cuda.current_stream().cuda_stream)
         ids_ref, t_ref, a_ref = ops.heads_greedy(h_ref, from_bf16_bits(text_head), from_bf16_bits(audio),
                                                  np.array([7, 9]), alen, delay, 99, 98)
@@ -362,3 +364,33 @@ def test_stream_kernel_matches_register_kernel_and_oracle(cuda_device, n, k, mod
     assert np.all(np.abs(a - b) <= 2.0 ** -6 * np.maximum(np.abs(a), np.abs(b)) + 2.0 ** -14)
     assert np.array_equal(outs[0], outs[2])
     assert native.error_word() == 0
+
+
+def test_heads_tensor_parallel_shard_writes_only_its_codebooks(cuda_device):
+    """A shard owning codebooks 8..15 and no text row: its ids there, zeros elsewhere."""
+    from moss_tts._runtime import native
+    rng = np.random.Generator(np.random.PCG64(321))
+    H = 4096
+    x, r = synthetic.activation(322, (H,)), synthetic.activation(323, (H,))
+    nw = bf16_bits(from_bf16_bits(synthetic.activation(324, (H,), 0.02)) + 1.0)
+    audio = synthetic._normal_bf16(rng, (8 * 1024, H))
+    xs, rs, ws, au = (dev_bf16(v, cuda_device) for v in (x, r, nw, audio))
+    best = torch.zeros(9, device=cuda_device, dtype=torch.int64)
+    ticket = torch.zeros(1, device=cuda_device, dtype=torch.int32)
+    al = torch.empty(8 * 1024, device=cuda_device, dtype=torch.bfloat16)
+    nxt = torch.full((33,), -7, device=cuda_device, dtype=torch.long)
+    a_len = torch.tensor([32], device=cuda_device)
+    d_len = torch.tensor([-1], device=cuda_device)
+    native.call("mt_heads_greedy", xs.data_ptr(), rs.data_ptr(), ws.data_ptr(), 1e-6, None, None, au.data_ptr(),
+                None, al.data_ptr(), None, a_len.data_ptr(), d_len.data_ptr(), nxt.data_ptr(), best.data_ptr(),
+                ticket.data_ptr(), H, 2, 8, 1024, 8, 32, 99, 98, 1024, 0, 0,
+                torch.cuda.current_stream().cuda_stream)
+    _, h_ref = ops.add_rmsnorm(from_bf16_bits(x), from_bf16_bits(r), from_bf16_bits(nw), 1e-6)
+    logits = ops.linear(h_ref, from_bf16_bits(audio)).reshape(8, 1024)
+    got = nxt.cpu().numpy()
+    assert got[0] == 0 and np.all(got[1:9] == 0) and np.all(got[17:] == 0)
+    top2 = np.sort(logits, axis=1)[:, -2:]
+    want = np.argmax(logits, axis=1)
+    for c in range(8):
+        assert got[9 + c] == want[c] or top2[c, 1] - top2[c, 0] <= 0.0625
+    assert int(best.abs().sum()) == 0 and int(ticket.item()) == 0
