@@ -33,7 +33,7 @@ extern "C" {
 #endif
 
 #define MT_FLAG_PDL 1
-#define MT_FLAG_REGISTER_PIPELINE 2 /* mt_w4a16_linear: use the register-pipelined kernel at batch 1 */
+#define MT_FLAG_REGISTER_PIPELINE 2 /* alternative kernels: split-K attention, register-pipelined heads */
 #define MT_LINEAR_NORM 1   /* RMSNorm prologue over each activation row            */
 #define MT_LINEAR_ADD 2    /* bf16 residual add before the norm (requires NORM)    */
 #define MT_LINEAR_PAIRED 4 /* rows [0,N/2) gate, [N/2,N) up; y = bf16(silu(g)) * u */
@@ -66,14 +66,45 @@ int mt_dequant_w4(const void* qweight, const void* scales, const void* qzeros, v
  * project (dp4a_packing.py:94-125; paired SiLU at :85-89) and the fused norm projection
  * dp4a_norm_projection.linear (dp4a_norm_projection.py:99-117), as W4A16 instead of W4A8.
  * Requires k % 128 == 0, n % 4 == 0 (n % 8 when PAIRED), x/residual/summed/norm_w 8-byte
- * and qweight 16-byte aligned. Batch 1 with k/32 a multiple of 32 (k = 1024 ... 12288) and
- * 16-byte aligned buffers runs the bulk-copy streaming kernel; flags bit 1
- * (MT_FLAG_REGISTER_PIPELINE) selects the register-pipelined kernel instead.
+ * and qweight 16-byte aligned. Reads the GPTQ layout directly (register-pipelined kernel);
+ * the decode engine's batch-1 path is mt_w4a16_linear_packed over the packed layout.
  */
 int mt_w4a16_linear(const void* x, const void* residual, const void* norm_w, float eps,
                     void* summed, const void* qweight, const void* scales, const void* qzeros,
                     void* y, int batch, int n, int k, int group, int mode, int flags,
                     void* stream);
+
+/*
+ * Packed W4 layout for the batch-1 tensor-core GEMV (mt_w4a16_linear_packed): sizes of the
+ * packed weights and of the per-call workspace for an [n, k] projection with `mode`
+ * (PAIRED changes the row order). Requires k % 256 == 0, 256 <= k <= 16384, n even when
+ * PAIRED. Pure host arithmetic.
+ */
+int mt_w4a16_packed_size(int n, int k, int has_zeros, int mode, long long* packed_bytes,
+                         long long* workspace_bytes);
+
+/*
+ * Load-time repack of GPTQ W4 weights (qweight/scales/qzeros as above; qzeros NULL for
+ * symmetric weights) into the packed layout: tiles of 16 weight rows (8 gate + 8 up rows
+ * when PAIRED) x 256 input columns, each 2368 bytes (2304 without zero points) laid out in
+ * the order the tensor-core lanes read them. Counterpart of the reference's load-time
+ * repack install_packing / pack_interleaved (src/moss_tts/_runtime/dp4a_packing.py:15-20,
+ * 128-160). `packed` must hold mt_w4a16_packed_size bytes, 16-byte aligned.
+ */
+int mt_w4a16_pack(const void* qweight, const void* scales, const void* qzeros, int n, int k,
+                  int mode, void* packed, void* stream);
+
+/*
+ * Batch-1 W4A16 GEMV over packed weights, same math and modes as mt_w4a16_linear (replaces
+ * the same reference projections): bulk-copy streaming of the packed tiles, dequantization
+ * into bf16 pairs feeding mma.sync m16n8k16, split-K over the SMs. `workspace` holds
+ * mt_w4a16_packed_size's workspace bytes, zero-filled by the caller once before first
+ * use; every call leaves it zeroed again. Calls that share a workspace must be ordered on
+ * one stream. All pointers 16-byte aligned.
+ */
+int mt_w4a16_linear_packed(const void* x, const void* residual, const void* norm_w, float eps,
+                           void* summed, const void* packed, int has_zeros, void* y, int n, int k,
+                           int mode, void* workspace, int flags, void* stream);
 
 /*
  * bf16-weight decode GEMV with the same modes as mt_w4a16_linear (w bf16 [n, k]).

@@ -14,7 +14,11 @@
 // contiguous K and V row ranges into shared memory with two bulk copies issued before
 // the programmatic-dependency wait.
 // Scratch (fp32 partials, LSE, tickets) is caller-provided global memory.
+#include <cooperative_groups.h>
+
 #include "common.cuh"
+
+namespace cg = cooperative_groups;
 
 namespace mt {
 
@@ -266,6 +270,252 @@ __global__ void __launch_bounds__(128) attention_decode(AttnArgs a) {
   if (tid == 0) *ticket = 0u;
 }
 
+// ----------------------------------------------------------------------------
+// Cluster decode attention: one thread-block cluster of kClusterCtas CTAs per (sequence,
+// KV head). CTA r of the cluster owns tokens [r*span, (r+1)*span), span = ceil(len / C),
+// streams them in kChunk-token chunks (K and V rows are contiguous in the cache: two bulk
+// copies per chunk, double-buffered, the first two issued before the dependency wait),
+// and keeps an online softmax per query head. The CTAs then merge through distributed
+// shared memory (cluster rank 0 reads every peer's running max, sum and unnormalised
+// output), so no global scratch, atomics or memory fences are involved.
+constexpr int kClusterCtas = 8;
+constexpr int kChunk = 64;
+
+template <int REP>
+__global__ void __launch_bounds__(256) attention_cluster(AttnArgs a) {
+  extern __shared__ __align__(128) uint8_t sm[];  // 2 slots x {K[kChunk][128], V[kChunk][128]} bf16
+  __shared__ __align__(16) float qs[REP][kHeadDim];
+  __shared__ float lg[REP][kChunk];
+  __shared__ float cmax[REP][2], csum[REP][2];
+  __shared__ float m_run[REP], l_run[REP], scale[REP];
+  __shared__ float accsm[REP][kHeadDim];
+  __shared__ __align__(8) uint64_t full[2];
+  __shared__ int failed;
+  cg::cluster_group cluster = cg::this_cluster();
+  const int rank = (int)cluster.block_rank();
+  const int kh = blockIdx.x / kClusterCtas, b = blockIdx.z;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int qkv_w = (a.nq + 2 * a.nkv) * kHeadDim;
+  constexpr size_t kRowBytes = kHeadDim * 2, kSlotBytes = (size_t)kChunk * kRowBytes * 2;
+
+  int64_t pos = a.positions[b];
+  const bool bad_pos = pos < 0 || pos >= a.max_len;
+  if (bad_pos) pos = pos < 0 ? 0 : a.max_len - 1;
+  const int p = (int)pos, len = p + 1;
+  const int span = (len + kClusterCtas - 1) / kClusterCtas;
+  const int t0 = rank * span, t1 = min(t0 + span, len);
+  const int n = t1 > t0 ? t1 - t0 : 0;
+  const int chunks = (n + kChunk - 1) / kChunk;
+  const size_t kv_base = ((size_t)b * a.nkv + kh) * a.max_len * kHeadDim;
+
+  auto issue = [&](int c) {
+    const int slot = c & 1, cs = t0 + c * kChunk, rows = min(kChunk, t1 - cs);
+    const unsigned bytes = (unsigned)(rows * kRowBytes);
+    uint8_t* kdst = sm + (size_t)slot * kSlotBytes;
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(attn_smem_u32(&full[slot])),
+                 "r"(2 * bytes) : "memory");
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     attn_smem_u32(kdst)), "l"(a.k_cache + kv_base + (size_t)cs * kHeadDim), "r"(bytes),
+                 "r"(attn_smem_u32(&full[slot])) : "memory");
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     attn_smem_u32(kdst + kSlotBytes / 2)), "l"(a.v_cache + kv_base + (size_t)cs * kHeadDim),
+                 "r"(bytes), "r"(attn_smem_u32(&full[slot])) : "memory");
+  };
+  auto wait_slot = [&](int c) -> bool {
+    for (long it = 0; it < (1L << 22); ++it) {
+      uint32_t done;
+      asm volatile("{\n .reg .pred q;\n mbarrier.try_wait.parity.shared::cta.b64 q, [%1], %2;\n selp.u32 %0, 1, 0, q;\n}"
+                   : "=r"(done) : "r"(attn_smem_u32(&full[c & 1])), "r"((unsigned)((c >> 1) & 1)) : "memory");
+      if (done) return true;
+    }
+    return false;
+  };
+
+  if (tid == 0) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(attn_smem_u32(&full[0])) : "memory");
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(attn_smem_u32(&full[1])) : "memory");
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    failed = 0;
+    // rows before `position` were written by earlier steps: fetch before the wait
+    for (int c = 0; c < 2 && c < chunks; ++c) issue(c);
+  }
+  if (tid < REP) { m_run[tid] = -INFINITY; l_run[tid] = 0.f; }
+  __syncthreads();
+  pdl_wait();
+  pdl_trigger();
+  if (bad_pos && a.status && tid == 0 && rank == 0) atomicExch(a.status, 1);
+  const __nv_bfloat16* src = a.qkv + (size_t)b * qkv_w;
+
+  // Query heads (warp w < REP handles head kh*REP + w), rounded to bf16 as stored by the
+  // reference (kernels.py:165), kept as fp32 for the dot products.
+  if (warp < REP) {
+    const int h = kh * REP + warp;
+    float x[4];
+    const uint2 r = *reinterpret_cast<const uint2*>(src + h * kHeadDim + 4 * lane);
+    x[0] = bf16_lo(r.x); x[1] = bf16_hi(r.x); x[2] = bf16_lo(r.y); x[3] = bf16_hi(r.y);
+    norm_rope_head(x, a.q_norm, a.cos_tab + (size_t)p * kHeadDim, a.sin_tab + (size_t)p * kHeadDim, a.eps, lane);
+    *reinterpret_cast<float4*>(&qs[warp][4 * lane]) = make_float4(x[0], x[1], x[2], x[3]);
+  }
+  const bool owner = t0 <= p && p < t1;
+  uint2 krow = make_uint2(0, 0), vrow = make_uint2(0, 0);
+  if (owner && warp == 0) {
+    float x[4];
+    const uint2 r = *reinterpret_cast<const uint2*>(src + (a.nq + kh) * kHeadDim + 4 * lane);
+    x[0] = bf16_lo(r.x); x[1] = bf16_hi(r.x); x[2] = bf16_lo(r.y); x[3] = bf16_hi(r.y);
+    norm_rope_head(x, a.k_norm, a.cos_tab + (size_t)p * kHeadDim, a.sin_tab + (size_t)p * kHeadDim, a.eps, lane);
+    __nv_bfloat162 lo = __floats2bfloat162_rn(x[0], x[1]), hi = __floats2bfloat162_rn(x[2], x[3]);
+    krow.x = *reinterpret_cast<uint32_t*>(&lo);
+    krow.y = *reinterpret_cast<uint32_t*>(&hi);
+    vrow = *reinterpret_cast<const uint2*>(src + (a.nq + a.nkv + kh) * kHeadDim + 4 * lane);
+    *reinterpret_cast<uint2*>(a.k_cache + kv_base + (size_t)p * kHeadDim + 4 * lane) = krow;
+    *reinterpret_cast<uint2*>(a.v_cache + kv_base + (size_t)p * kHeadDim + 4 * lane) = vrow;
+  }
+
+  // V accumulation layout: thread (d = tid % 128, half = tid / 128) owns heads half*HPT ...
+  constexpr int HPT = REP >= 2 ? REP / 2 : 1;
+  const int d = tid & 127, half = tid >> 7;
+  const bool vlive = half * HPT < REP;
+  float acc[HPT];
+#pragma unroll
+  for (int j = 0; j < HPT; ++j) acc[j] = 0.f;
+  __syncthreads();
+
+  int c = 0;
+  for (; c < chunks; ++c) {
+    if (!__syncthreads_and(wait_slot(c) ? 1 : 0)) break;
+    const int slot = c & 1, cs = t0 + c * kChunk, rows = min(kChunk, t1 - cs);
+    const __nv_bfloat16* ks = reinterpret_cast<const __nv_bfloat16*>(sm + (size_t)slot * kSlotBytes);
+    const __nv_bfloat16* vs = ks + (size_t)kChunk * kHeadDim;
+    if (owner && warp == 0 && p >= cs && p < cs + rows) {  // this step's row, fresh
+      *reinterpret_cast<uint2*>(const_cast<__nv_bfloat16*>(ks) + (size_t)(p - cs) * kHeadDim + 4 * lane) = krow;
+      *reinterpret_cast<uint2*>(const_cast<__nv_bfloat16*>(vs) + (size_t)(p - cs) * kHeadDim + 4 * lane) = vrow;
+    }
+    __syncthreads();
+    // logits: item (head h, token t); a warp covers 32 tokens of one head
+    for (int item = tid; item < REP * kChunk; item += 256) {
+      const int h = item / kChunk, t = item - h * kChunk;
+      float v = -INFINITY;
+      if (t < rows) {
+        const uint4* krow4 = reinterpret_cast<const uint4*>(ks + (size_t)t * kHeadDim);
+        const float4* q4 = reinterpret_cast<const float4*>(&qs[h][0]);
+        float d0 = 0.f, d1 = 0.f;
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          const int cc = rot(j, t);
+          const uint4 kk = krow4[cc];
+          const float4 qa = q4[2 * cc], qb = q4[2 * cc + 1];
+          d0 = fmaf(qa.x, bf16_lo(kk.x), d0);
+          d1 = fmaf(qa.y, bf16_hi(kk.x), d1);
+          d0 = fmaf(qa.z, bf16_lo(kk.y), d0);
+          d1 = fmaf(qa.w, bf16_hi(kk.y), d1);
+          d0 = fmaf(qb.x, bf16_lo(kk.z), d0);
+          d1 = fmaf(qb.y, bf16_hi(kk.z), d1);
+          d0 = fmaf(qb.z, bf16_lo(kk.w), d0);
+          d1 = fmaf(qb.w, bf16_hi(kk.w), d1);
+        }
+        v = (d0 + d1) * kScale;
+      }
+      lg[h][t] = v;
+    }
+    __syncthreads();
+    // online softmax: warps 2h and 2h+1 reduce head h's 64 logits
+    if (warp < 2 * REP) {
+      const int h = warp >> 1, hf = warp & 1;
+      const float v = lg[h][hf * 32 + lane];
+      const float m = warp_max(v);
+      if (lane == 0) cmax[h][hf] = m;
+    }
+    __syncthreads();
+    if (warp < 2 * REP) {
+      const int h = warp >> 1, hf = warp & 1;
+      const float mnew = fmaxf(m_run[h], fmaxf(cmax[h][0], cmax[h][1]));
+      const float e = expf(lg[h][hf * 32 + lane] - mnew);
+      lg[h][hf * 32 + lane] = e;
+      const float sum = warp_sum(e);
+      if (lane == 0) csum[h][hf] = sum;
+    }
+    __syncthreads();
+    if (tid < REP) {
+      const float mnew = fmaxf(m_run[tid], fmaxf(cmax[tid][0], cmax[tid][1]));
+      const float sc = expf(m_run[tid] - mnew);
+      scale[tid] = sc;
+      l_run[tid] = l_run[tid] * sc + csum[tid][0] + csum[tid][1];
+      m_run[tid] = mnew;
+    }
+    __syncthreads();
+    if (vlive) {
+      const __nv_bfloat16* vcol = vs + d;
+#pragma unroll
+      for (int j = 0; j < HPT; ++j) acc[j] *= scale[half * HPT + j];
+#pragma unroll 8
+      for (int t = 0; t < rows; ++t) {
+        const float v = bf16f(vcol[(size_t)t * kHeadDim]);
+#pragma unroll
+        for (int j = 0; j < HPT; ++j) acc[j] = fmaf(lg[half * HPT + j][t], v, acc[j]);
+      }
+    }
+    __syncthreads();  // every thread is done with this slot
+    if (tid == 0 && c + 2 < chunks) issue(c + 2);
+  }
+  if (c < chunks) {  // a copy did not land within the bound
+    if (tid == 0) {
+      failed = 1;
+      if (a.status) atomicExch(a.status, 3);
+      for (int k = c; k < chunks && k < c + 2; ++k) wait_slot(k);  // drain this CTA's copies
+    }
+    __syncthreads();
+  }
+  if (vlive) {
+#pragma unroll
+    for (int j = 0; j < HPT; ++j) accsm[half * HPT + j][d] = acc[j];
+  }
+  cluster.sync();
+  if (rank == 0) {
+    for (int item = tid; item < REP * kHeadDim; item += 256) {
+      const int h = item / kHeadDim, dd = item - h * kHeadDim;
+      float M = -INFINITY;
+      for (int r = 0; r < kClusterCtas; ++r) M = fmaxf(M, *cluster.map_shared_rank(&m_run[h], r));
+      float S = 0.f, O = 0.f;
+      for (int r = 0; r < kClusterCtas; ++r) {
+        const float mr = *cluster.map_shared_rank(&m_run[h], r);
+        const float w = mr == -INFINITY ? 0.f : expf(mr - M);
+        S = fmaf(w, *cluster.map_shared_rank(&l_run[h], r), S);
+        O = fmaf(w, *cluster.map_shared_rank(&accsm[h][dd], r), O);
+      }
+      a.out[(size_t)b * a.nq * kHeadDim + (kh * REP + h) * kHeadDim + dd] = to_bf16(O / S);
+    }
+  }
+  cluster.sync();  // peers keep their shared memory until rank 0 has read it
+}
+
+static cudaError_t launch_cluster_attention(const AttnArgs& a, int batch, int rep, cudaStream_t s, int flags) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(kClusterCtas * a.nkv, 1, batch);
+  cfg.blockDim = dim3(256);
+  cfg.dynamicSmemBytes = 2 * (size_t)kChunk * kHeadDim * 2 * 2;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = kClusterCtas;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = (flags & kFlagPdl) ? 2 : 1;
+  switch (rep) {
+    case 4:
+      cudaFuncSetAttribute(attention_cluster<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)cfg.dynamicSmemBytes);
+      return cudaLaunchKernelEx(&cfg, attention_cluster<4>, a);
+    case 2:
+      cudaFuncSetAttribute(attention_cluster<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)cfg.dynamicSmemBytes);
+      return cudaLaunchKernelEx(&cfg, attention_cluster<2>, a);
+    default:
+      cudaFuncSetAttribute(attention_cluster<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)cfg.dynamicSmemBytes);
+      return cudaLaunchKernelEx(&cfg, attention_cluster<1>, a);
+  }
+}
+
 static size_t attn_smem_bytes(int rep, int max_len, int splits) {
   const size_t cap = (size_t)attn_cap(max_len, splits);
   return cap * kHeadDim * 2 * 2 + (size_t)rep * cap * sizeof(float);
@@ -351,10 +601,14 @@ MT_API int mt_attention_decode(const void* qkv, const void* q_norm, const void* 
     return kBadArgument;
   const int rep = nq / nkv;
   if (rep != 4 && rep != 1 && rep != 2) return kBadArgument;
+  cudaStream_t s = (cudaStream_t)stream;
+  // Default: the cluster kernel (its merge needs no scratch). Flags bit 1 selects the
+  // split-K kernel with the caller's scratch and `splits` splits.
+  if (!(flags & 2)) return (int)launch_cluster_attention(a, batch, rep, s, flags & kFlagPdl);
+  flags &= kFlagPdl;
   const size_t smem = attn_smem_bytes(rep, max_len, splits);
   if (smem > 200 * 1024) return kBadArgument;
   const dim3 grid(nkv, splits, batch);
-  cudaStream_t s = (cudaStream_t)stream;
   switch (rep) {
     case 4: return launch(attention_decode<4>, grid, dim3(128), smem, s, flags, a);
     case 2: return launch(attention_decode<2>, grid, dim3(128), smem, s, flags, a);

@@ -304,11 +304,6 @@ static cudaError_t dispatch_mode(const W4Args& a, int mode, cudaStream_t s, int 
   return dispatch_paired<B, false, false>(a, paired, s, flags);
 }
 
-bool stream_supported(int batch, int n, int k, int mode);
-cudaError_t stream_launch(const void* x, const void* residual, const void* norm_w, float eps, void* summed,
-                          const void* qweight, const void* scales, const void* qzeros, void* y, int n, int k,
-                          int mode, int flags, cudaStream_t s);
-
 }  // namespace mt
 
 using namespace mt;
@@ -330,14 +325,6 @@ MT_API int mt_w4a16_linear(const void* x, const void* residual, const void* norm
   if (!aligned(x, 8) || !aligned(qweight, 16) || (residual && !aligned(residual, 8)) ||
       (summed && !aligned(summed, 8)) || (norm_w && !aligned(norm_w, 8)) || !aligned(scales, 2))
     return kBadArgument;
-  // Batch 1 (the decode step): the bulk-copy streaming kernel, unless the caller asks for
-  // the register-pipelined kernel (MT_FLAG_REGISTER_PIPELINE) or the buffers do not meet
-  // its 16-byte alignment.
-  if (!(flags & 2) && stream_supported(batch, n, k, mode) && aligned(x, 16) &&
-      (!residual || aligned(residual, 16)) && (!summed || aligned(summed, 16)) &&
-      (!norm_w || aligned(norm_w, 16)) && aligned(scales, 16) && (!qzeros || aligned(qzeros, 16)))
-    return (int)stream_launch(x, residual, norm_w, eps, summed, qweight, scales, qzeros, y, n, k, mode,
-                              flags & kFlagPdl, (cudaStream_t)stream);
   // Rows per launch: the whole batch when its staged activations fit in shared memory,
   // otherwise chunks of it (each chunk streams the weights again).
   int chunk = batch;

@@ -1,166 +1,257 @@
-// Batch-1 W4A16 G32 GEMV streamed through shared memory with bulk asynchronous copies.
+// Batch-1 W4A16 G32 GEMV on the tensor cores over a packed, tile-major weight layout
+// streamed through shared memory by bulk copies.
 //
-// Structure (one CTA per SM, persistent):
-//   * CTA c owns a contiguous, balanced range of output rows (in units of two rows);
-//     its weight rows are one contiguous byte range per tensor (codes, scales, zeros),
-//     so each pipeline stage of RS rows is a handful of cp.async.bulk copies that
-//     complete on an mbarrier (transaction-count based);
-//   * one thread issues the first NS stages *before* griddepcontrol.wait, so the
-//     weight stream starts while the previous kernel of the decode step finishes;
-//   * thread t owns quantization group g = t % G of partition p = t / G and keeps the
-//     32 activation values of that group in registers for the whole kernel (after the
-//     optional residual add + RMSNorm), so shared memory only carries weight bytes;
-//   * partition p handles stage rows i = p, p + P, ...; per row a thread reads its 16
-//     code bytes, its scale and zero point, and accumulates with magic-number
-//     dequantization and packed FFMA2 (see w4a16.cu);
-//   * rows are reduced across the warp with a transposed butterfly (one shuffle per
-//     row per lane) and across the partition's warps through shared memory.
+// Packed layout (written once at load time by mt_w4a16_pack, the counterpart of the
+// reference's load-time repack install_packing, dp4a_packing.py:128-160):
+//   * weight rows are grouped in tiles of 16 (8 gate + 8 up rows when the gate/up pair is
+//     fused, so that both halves of an output land in the same tile); K is cut in slices
+//     of 256 columns (8 quantization groups). One "slice block" = 16 rows x 256 columns:
+//       codes  2048 B  [q = 0..3][lane 0..31][16 B]: lane (r = lane / 4, c = lane % 4) holds
+//                      bytes 32c + 16 (q & 1) .. +15 of the slice of row r (q < 2) or r + 8;
+//       scales  256 B  [lane][4 x bf16]: s[r][2c], s[r][2c+1], s[r+8][2c], s[r+8][2c+1];
+//       zeros    64 B  [lane][2 B]: zero-point bytes (groups 2c | 2c+1) of rows r and r + 8
+//                      (absent for symmetric weights);
+//     blocks are stored tile-major, slice-minor. Every shared-memory read of a block is a
+//     lane-ordered vector load (bank-conflict free) and a run of blocks is one contiguous
+//     bulk copy.
+// Kernel (one persistent CTA per SM):
+//   * the T x S slice blocks are split evenly over the CTAs (split-K across tile
+//     boundaries); a pipeline stage is up to 16 consecutive blocks, one bulk copy issued by
+//     a producer warp into an NS-stage ring; the first NS copies go out before
+//     griddepcontrol.wait, because weights never depend on the previous kernel;
+//   * consumer warp w takes block w of every stage. Lane (r, c) turns its 64 codes of rows
+//     r and r + 8 into bf16 pairs (128 + q_j, 128 + q_{j+4}) with one LOP3 each and feeds
+//     them as the A operand of 16 mma.sync.m16n8k16 (bf16 -> fp32). The B operand carries
+//     the activation only in column n = 2c + h for the codes of group 2c + h and zeros
+//     elsewhere, so accumulator column n holds every row's dot product with group n alone
+//     and the group's scale and zero point apply afterwards:
+//         y_r += s_rg * (D_rg - (128 + z_rg) * sum(x_g));
+//   * row sums are kept per warp and tile in shared memory and reduced at the end; a tile
+//     split between two CTAs is finished by whichever arrives second, through a small
+//     workspace and a per-tile ticket (own + other: the same fp32 sum in either order),
+//     which also applies SiLU(gate) * up for the fused pair.
 // Every mbarrier wait is bounded: on expiry the kernel raises the library error word,
 // waits (bounded) for its outstanding copies and returns.
 #include <stdlib.h>
+#include <string.h>
+
+#include <cuda_fp16.h>
 
 #include "stream_pipeline.cuh"
 
 namespace mt {
 
-__device__ int g_error_word;  // non-zero after a bounded wait expired (see mt_error_word)
-
-namespace {
-
-__device__ __forceinline__ float magic_lo(uint32_t w) { return __uint_as_float((w & 0x000F0000u) | 0x43000000u); }
-__device__ __forceinline__ float magic_hi(uint32_t w) { return __uint_as_float((w & 0x0000F000u) | 0x45000000u); }
-
-__device__ __forceinline__ void dot_word(uint32_t w, const float* x, float2& acc) {
-  const uint32_t r8 = __funnelshift_r(w, w, 8);
-  const uint32_t r16 = __byte_perm(w, w, 0x1032);
-  const uint32_t r24 = __funnelshift_r(w, w, 24);
-  acc = __ffma2_rn(make_float2(magic_lo(r16), magic_hi(r24)), make_float2(x[0], x[1]), acc);
-  acc = __ffma2_rn(make_float2(magic_lo(r24), magic_hi(w)), make_float2(x[2], x[3]), acc);
-  acc = __ffma2_rn(make_float2(magic_lo(w), magic_hi(r8)), make_float2(x[4], x[5]), acc);
-  acc = __ffma2_rn(make_float2(magic_lo(r8), magic_hi(r16)), make_float2(x[6], x[7]), acc);
-}
-
-}  // namespace
+__device__ int g_error_word;  // non-zero after a bounded wait expired (see mt_read_error_word)
 
 using namespace pipe;
+
+constexpr int kSliceCols = 256;   // input columns per slice block
+constexpr int kCodeBytes = 2048;  // 16 rows x 128 bytes
+constexpr int kScaleBytes = 256;  // 16 rows x 8 groups x bf16
+constexpr int kZeroBytes = 64;    // 16 rows x 8 groups x 4 bits
+
+struct PackGeom {
+  int n_out, rt, tiles, slices, block_b;
+  long long blocks;
+  PackGeom(int n, int k, bool zeros, bool paired) {
+    n_out = paired ? n / 2 : n;
+    rt = paired ? 8 : 16;
+    tiles = (n_out + rt - 1) / rt;
+    slices = k / kSliceCols;
+    block_b = kCodeBytes + kScaleBytes + (zeros ? kZeroBytes : 0);
+    blocks = (long long)tiles * slices;
+  }
+  size_t packed_bytes() const { return (size_t)blocks * block_b; }
+  static constexpr int kMaxCtas = 1024;  // workspace capacity: one slot per CTA boundary
+  static size_t workspace_bytes() { return (size_t)kMaxCtas * (2 * 16 * sizeof(float) + sizeof(int)); }
+};
+
+// Weight row held at tile row tr (0..15) of tile t, or -1 for padding past the last row.
+__host__ __device__ inline long long tile_row(int t, int tr, int n_out, bool paired) {
+  if (paired) {
+    const int o = t * 8 + (tr & 7);
+    return o < n_out ? (long long)o + (tr >= 8 ? n_out : 0) : -1;
+  }
+  const int o = t * 16 + tr;
+  return o < n_out ? o : -1;
+}
+
+// One warp per slice block; lane (r, c) writes its code chunks, scales and zero points.
+__global__ void w4a16_pack_blocks(const uint8_t* __restrict__ qweight, const uint16_t* __restrict__ scales,
+                                  const uint8_t* __restrict__ qzeros, uint8_t* __restrict__ packed, int n_out,
+                                  int k, int slices, long long blocks, int block_b, int paired) {
+  const long long b = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (b >= blocks) return;
+  const int lane = threadIdx.x & 31, r = lane >> 2, c = lane & 3;
+  const int t = (int)(b / slices), j = (int)(b - (long long)t * slices);
+  uint8_t* blk = packed + (size_t)b * block_b;
+  const long long ra = tile_row(t, r, n_out, paired != 0), rb = tile_row(t, r + 8, n_out, paired != 0);
+  const int G = k / 32;
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const long long row = q < 2 ? ra : rb;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (row >= 0)
+      v = *reinterpret_cast<const uint4*>(qweight + (size_t)row * (k / 2) + (size_t)j * 128 + 32 * c + 16 * (q & 1));
+    *reinterpret_cast<uint4*>(blk + q * 512 + lane * 16) = v;
+  }
+  const int g = j * 8 + 2 * c;
+  uint16_t sv[4] = {0, 0, 0, 0};
+  if (ra >= 0) { sv[0] = scales[(size_t)ra * G + g]; sv[1] = scales[(size_t)ra * G + g + 1]; }
+  if (rb >= 0) { sv[2] = scales[(size_t)rb * G + g]; sv[3] = scales[(size_t)rb * G + g + 1]; }
+  *reinterpret_cast<uint2*>(blk + kCodeBytes + lane * 8) =
+      make_uint2(sv[0] | ((uint32_t)sv[1] << 16), sv[2] | ((uint32_t)sv[3] << 16));
+  if (qzeros) {
+    const uint8_t za = ra >= 0 ? qzeros[(size_t)ra * (k / 64) + g / 2] : 0;
+    const uint8_t zb = rb >= 0 ? qzeros[(size_t)rb * (k / 64) + g / 2] : 0;
+    *reinterpret_cast<uint16_t*>(blk + kCodeBytes + kScaleBytes + lane * 2) = (uint16_t)(za | (zb << 8));
+  }
+}
 
 struct StreamArgs {
   const __nv_bfloat16* x;
   const __nv_bfloat16* residual;
   const __nv_bfloat16* norm_w;
   __nv_bfloat16* summed;
-  const uint8_t* qweight;
-  const __nv_bfloat16* scales;
-  const uint8_t* qzeros;
+  const uint8_t* packed;
   __nv_bfloat16* y;
-  int n, k;
+  float* ws;      // [CTA boundary][2][16] partial rows of the tile two neighbouring CTAs share
+  int* tickets;   // [CTA boundary], zero between launches
+  int n, k, zeros;
   float eps;
 };
 
-// bf16 magic pairs: (w >> s) masked to nibbles at bits 0..3 and 16..19 with the bf16
-// exponent of 128 gives the pair (128 + q_j, 128 + q_{j+4}) in one LOP3.
-__device__ __forceinline__ uint32_t pair_magic(uint32_t w) { return (w & 0x000F000Fu) | 0x43004300u; }
-
-// fp32 += bf16 * bf16 (exact product, one rounding): sm_100's mixed-precision FMA.
-__device__ __forceinline__ float fma_bf16_lo(uint32_t a, uint32_t b, float c) {
-  float d;
-  asm("{.reg .b16 al, ah, bl, bh;\n mov.b32 {al, ah}, %1;\n mov.b32 {bl, bh}, %2;\n"
-      " fma.rn.f32.bf16 %0, al, bl, %3;}" : "=f"(d) : "r"(a), "r"(b), "f"(c));
-  return d;
-}
-__device__ __forceinline__ float fma_bf16_hi(uint32_t a, uint32_t b, float c) {
-  float d;
-  asm("{.reg .b16 al, ah, bl, bh;\n mov.b32 {al, ah}, %1;\n mov.b32 {bl, bh}, %2;\n"
-      " fma.rn.f32.bf16 %0, ah, bh, %3;}" : "=f"(d) : "r"(a), "r"(b), "f"(c));
-  return d;
+// Codes as fp16 subnormals: (w & 0x000F000F) is the fp16 pair (q_j, q_{j+4}) * 2^-24 and
+// (w & 0x00F000F0) the pair 16 (q_{j+1}, q_{j+5}) * 2^-24, exactly (the tensor cores keep
+// fp16 subnormal operands). The matching activation slots carry x c and x c / 16.
+__device__ __forceinline__ void mma_f16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                        uint32_t b0, uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-// One 8-code word against the thread's activation pairs xp[i] = (x[i], x[i+4]) (bf16x2):
-// acc.x/acc.y accumulate sum x * (128 + q) over the word. MULHI: the nibble shifts are
-// done as 32x32 multiply-high (w * 2^(32-s)) >> 32, which issues outside the logic pipe.
-template <bool MULHI>
-__device__ __forceinline__ void dot_word_mixed(uint32_t w, const uint32_t* xp, float2& acc) {
-  const uint32_t s4 = MULHI ? __umulhi(w, 1u << 28) : (w >> 4);
-  const uint32_t s8 = MULHI ? __umulhi(w, 1u << 24) : (w >> 8);
-  const uint32_t s12 = MULHI ? __umulhi(w, 1u << 20) : (w >> 12);
-  const uint32_t p0 = pair_magic(w), p1 = pair_magic(s4), p2 = pair_magic(s8), p3 = pair_magic(s12);
-  acc.x = fma_bf16_lo(p0, xp[0], acc.x);
-  acc.y = fma_bf16_hi(p0, xp[0], acc.y);
-  acc.x = fma_bf16_lo(p1, xp[1], acc.x);
-  acc.y = fma_bf16_hi(p1, xp[1], acc.y);
-  acc.x = fma_bf16_lo(p2, xp[2], acc.x);
-  acc.y = fma_bf16_hi(p2, xp[2], acc.y);
-  acc.x = fma_bf16_lo(p3, xp[3], acc.x);
-  acc.y = fma_bf16_hi(p3, xp[3], acc.y);
+__device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
+  __half2 h = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&h);
 }
 
-// Warp-specialized streaming GEMV. Warps [0, C) consume, warp C produces (bulk copies).
-// RS output rows per stage, NS stages, P row partitions, DOT: 0 = fp32 magic + FFMA2,
-// 1 = bf16 magic pairs + mixed-precision FMA. blockDim = P * G + 32.
-template <int RS, int NS, int P, int DOT, bool NORM, bool ADD, bool PAIRED>
-__global__ void __launch_bounds__(P * 128 + 32 > 416 ? P * 128 + 32 : 416, 1) w4a16_stream(StreamArgs a, int max_rows) {
+// y row of tile row pair (gate = v, up = u) or plain row v (kernels.py / dp4a_packing.py:86-89).
+template <bool PAIRED>
+__device__ __forceinline__ float finish_row(float v, float u) {
+  if (!PAIRED) return v;
+  const float gate = round_bf16(v), up = round_bf16(u);
+  return round_bf16(gate / (1.0f + expf(-gate))) * up;
+}
+
+// Consumer-side dot product of one slice block (16 rows x 256 columns) against the B
+// fragments of its slice: returns the block's contribution to rows r (va) and r + 8 (vb),
+// already summed over the lane quad (lanes with c == 0 hold the row totals).
+struct BlockRegs {
+  uint4 c0, c1, c2, c3;  // codes: row r (c0, c1) and row r + 8 (c2, c3)
+  uint2 sw;              // scales: (s[r][2c], s[r][2c+1]) | (s[r+8][2c], s[r+8][2c+1])
+  uint32_t zz;           // zero points: groups 2c | 2c+1 of row r (low byte) and r + 8
+};
+
+__device__ __forceinline__ BlockRegs load_block(const uint8_t* blk, int lane, bool zeros) {
+  BlockRegs b;
+  b.c0 = *reinterpret_cast<const uint4*>(blk + lane * 16);
+  b.c1 = *reinterpret_cast<const uint4*>(blk + 512 + lane * 16);
+  b.c2 = *reinterpret_cast<const uint4*>(blk + 1024 + lane * 16);
+  b.c3 = *reinterpret_cast<const uint4*>(blk + 1536 + lane * 16);
+  b.sw = *reinterpret_cast<const uint2*>(blk + kCodeBytes + lane * 8);
+  b.zz = zeros ? (uint32_t)*reinterpret_cast<const uint16_t*>(blk + kCodeBytes + kScaleBytes + lane * 2) : 0x8888u;
+  return b;
+}
+
+__device__ __forceinline__ void block_dot(const BlockRegs& bk, const uint32_t (&bl)[16], const uint32_t (&bh)[16],
+                                          uint32_t bz0, uint32_t bz1, float& va, float& vb) {
+  const uint32_t wa[8] = {bk.c0.x, bk.c0.y, bk.c0.z, bk.c0.w, bk.c1.x, bk.c1.y, bk.c1.z, bk.c1.w};
+  const uint32_t wb[8] = {bk.c2.x, bk.c2.y, bk.c2.z, bk.c2.w, bk.c3.x, bk.c3.y, bk.c3.z, bk.c3.w};
+  float d[2][4] = {};  // two independent accumulators halve the mma dependency chains
+  // zero points: A = (z[r][2c], 16 z[r][2c+1]) (and row r + 8) as fp16 subnormals against
+  // B = -(c sum x) of groups 2c / 2c + 1 split into fp16 hi and lo parts
+  const uint32_t za = __byte_perm(bk.zz, 0, 0x4040) & 0x00F0000Fu, zb = __byte_perm(bk.zz, 0, 0x4141) & 0x00F0000Fu;
+  mma_f16(d[1], za, zb, za, zb, bz0, bz1);
+#pragma unroll
+  for (int u = 0; u < 8; ++u) {
+    const uint32_t* bsel = u < 4 ? bl : bh;
+    const int bi = (u & 3) * 4;
+    const uint32_t sa = wa[u] >> 8, sb = wb[u] >> 8;
+    mma_f16(d[0], wa[u] & 0x000F000Fu, wb[u] & 0x000F000Fu, wa[u] & 0x00F000F0u, wb[u] & 0x00F000F0u, bsel[bi],
+            bsel[bi + 1]);
+    mma_f16(d[1], sa & 0x000F000Fu, sb & 0x000F000Fu, sa & 0x00F000F0u, sb & 0x00F000F0u, bsel[bi + 2], bsel[bi + 3]);
+  }
+  // column 2c = group 2c (element 0: row r, element 2: row r + 8), column 2c + 1 = group 2c + 1
+  va = fmaf(__uint_as_float(bk.sw.x & 0xFFFF0000u), d[0][1] + d[1][1], __uint_as_float(bk.sw.x << 16) * (d[0][0] + d[1][0]));
+  vb = fmaf(__uint_as_float(bk.sw.y & 0xFFFF0000u), d[0][3] + d[1][3], __uint_as_float(bk.sw.y << 16) * (d[0][2] + d[1][2]));
+  va += __shfl_xor_sync(0xffffffffu, va, 1);
+  vb += __shfl_xor_sync(0xffffffffu, vb, 1);
+  va += __shfl_xor_sync(0xffffffffu, va, 2);
+  vb += __shfl_xor_sync(0xffffffffu, vb, 2);
+}
+
+constexpr int kWarps = 16;  // consumer warps per CTA
+
+// NS ring stages of kWarps * BPW slice blocks; consumer warp w takes blocks w + 16 m
+// (m < BPW) of every stage, which share one slice when S divides 16.
+template <int NS, int BPW, bool NORM, bool ADD, bool PAIRED>
+__global__ void __launch_bounds__(kWarps * 32 + 32, 1) w4a16_packed(StreamArgs a, int max_tiles) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ __align__(8) uint64_t full[NS];
   __shared__ __align__(8) uint64_t empty[NS];
-  constexpr int H = PAIRED ? 2 : 1;  // weight-row blocks per stage (gate, up)
-  constexpr int RP = RS / P;         // rows per partition per stage
-  constexpr int NV = RP * H;         // values reduced per lane per stage
-  static_assert(RS % P == 0 && (NV & (NV - 1)) == 0 && NV <= 32, "bad tile");
-  __shared__ float ssum[32];
+  __shared__ float red[kWarps];
+  __shared__ float redmax[kWarps];
+  __shared__ __align__(16) uint4 zero16[4];
   __shared__ int failed;
+  constexpr int RT = PAIRED ? 8 : 16;  // output rows per tile
+  constexpr int consumers = kWarps * 32;
+  constexpr int SB = kWarps * BPW;     // slice blocks per stage
 
-  const int K = a.k, G = K >> 5;
-  const int consumers = P * G, cwarps = consumers >> 5;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const bool producer = tid >= consumers;
-  const int part = producer ? 0 : tid / G, g = producer ? 0 : tid - part * G;
-  const int wpp = G >> 5;  // warps per partition
-  const size_t row_bytes = (size_t)K >> 1, srow = (size_t)G * 2, zrow = (size_t)(G >> 1);
-  const bool zeros = a.qzeros != nullptr;
-  const size_t stage_rows_bytes = row_bytes + srow + (zeros ? zrow : 0);
-  const size_t stage_bytes = (size_t)RS * H * stage_rows_bytes;
-
+  const int K = a.k, S = K / kSliceCols;
+  const bool zeros = a.zeros != 0;
+  const int block_b = kCodeBytes + kScaleBytes + (zeros ? kZeroBytes : 0);
+  const int stage_b = SB * block_b;
   const int n_out = PAIRED ? a.n / 2 : a.n;
-  const int units = n_out >> 1;
-  const int u0 = (int)((long)blockIdx.x * units / gridDim.x), u1 = (int)((long)(blockIdx.x + 1) * units / gridDim.x);
-  const int r0 = u0 * 2, r1 = u1 * 2, nrows = r1 - r0;
-  const int stages = (nrows + RS - 1) / RS;
-  float* partial = reinterpret_cast<float*>(smem + (size_t)NS * stage_bytes);  // [cwarps][max_rows][H]
+  const int T = (n_out + RT - 1) / RT;
+  const int NB = T * S;  // < 2^31 for every accepted shape (n < 2^24, S <= 64)
+  const int b0 = (int)((long long)blockIdx.x * NB / gridDim.x), b1 = (int)((long long)(blockIdx.x + 1) * NB / gridDim.x);
+  const int nblk = b1 - b0;
+  const int stages = (nblk + SB - 1) / SB;
+  const int t_first = b0 / S, t_last = (b1 - 1) / S;
+  const int ntiles = t_last - t_first + 1;
 
-  auto codes_at = [&](int slot) { return smem + (size_t)slot * stage_bytes; };
-  auto scales_at = [&](int slot) { return codes_at(slot) + (size_t)RS * H * row_bytes; };
-  auto zeros_at = [&](int slot) { return scales_at(slot) + (size_t)RS * H * srow; };
-  auto issue = [&](int st) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  uint8_t* ring = smem;
+  uint4* xp = reinterpret_cast<uint4*>(smem + (size_t)NS * stage_b);  // [K / 8] bf16 pairs
+  float* xsum = reinterpret_cast<float*>(xp + K / 8);                 // [K / 32]
+  float* partial = xsum + K / 32;                                     // [kWarps][max_tiles][16]
+
+  auto issue = [&](int st) {  // one lane: stage st = blocks [b0 + SB st, ...)
     const int slot = st % NS;
-    const int rows = min(RS, nrows - st * RS);
-    mbar_expect_tx(&full[slot], (unsigned)(rows * H * stage_rows_bytes));
-#pragma unroll
-    for (int h = 0; h < H; ++h) {
-      const size_t row = (size_t)r0 + (size_t)st * RS + (size_t)h * n_out;
-      bulk_copy(codes_at(slot) + (size_t)h * RS * row_bytes, a.qweight + row * row_bytes,
-                (unsigned)(rows * row_bytes), &full[slot]);
-      bulk_copy(scales_at(slot) + (size_t)h * RS * srow, reinterpret_cast<const uint8_t*>(a.scales) + row * srow,
-                (unsigned)(rows * srow), &full[slot]);
-      if (zeros)
-        bulk_copy(zeros_at(slot) + (size_t)h * RS * zrow, a.qzeros + row * zrow, (unsigned)(rows * zrow),
-                  &full[slot]);
-    }
+    const int nb = min(SB, nblk - st * SB);
+    const unsigned bytes = (unsigned)(nb * block_b);
+    mbar_expect_tx(&full[slot], bytes);
+    bulk_copy(ring + (size_t)slot * stage_b, a.packed + (size_t)(b0 + st * SB) * block_b, bytes, &full[slot]);
   };
 
   if (tid == consumers) {
 #pragma unroll
     for (int s = 0; s < NS; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], cwarps);
+      mbar_init(&empty[s], kWarps);
     }
     failed = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     // weights never depend on the previous kernel: start streaming before the PDL wait
     for (int st = 0; st < NS && st < stages; ++st) issue(st);
   }
+  if (tid < 4) zero16[tid] = make_uint4(0, 0, 0, 0);
+  for (int i = tid; i < kWarps * max_tiles * 16; i += blockDim.x) partial[i] = 0.f;
   __syncthreads();
 
-  if (producer) {
+  if (warp == kWarps) {  // producer warp
     pdl_trigger();
     if (lane == 0) {
       int st = NS;
@@ -178,125 +269,171 @@ __global__ void __launch_bounds__(P * 128 + 32 > 416 ? P * 128 + 32 : 416, 1) w4
     return;
   }
 
+  // ---- activation prologue: x (+ residual, RMSNorm) -> bf16 pairs and group sums in smem ----
+  // Thread t owns the 8-value words t, t + 512, ... (kernels.py:57-59, 76-82).
+  const int wpt = (K / 8 + consumers - 1) / consumers;  // words per thread, at most 4
+  uint4 nwv[4];
+  if (NORM) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      if (j < wpt && tid + j * consumers < K / 8) nwv[j] = reinterpret_cast<const uint4*>(a.norm_w)[tid + j * consumers];
+  }
   pdl_wait();
   pdl_trigger();
-
-  // Activation of this thread's group, optionally add + RMSNorm (kernels.py:57-59,76-82).
-  float xv[32];
-  {
-    const uint4* xp = reinterpret_cast<const uint4*>(a.x + (size_t)g * 32);
+  float v[4][8];
+  float ss = 0.f;
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const uint4 w = xp[q];
-      const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+  for (int j = 0; j < 4; ++j) {
+    const int word = tid + j * consumers;
+    if (j >= wpt || word >= K / 8) continue;
+    const uint4 xw = reinterpret_cast<const uint4*>(a.x)[word];
+    const uint32_t xa[4] = {xw.x, xw.y, xw.z, xw.w};
 #pragma unroll
-      for (int i = 0; i < 4; ++i) { xv[8 * q + 2 * i] = bf16_lo(ww[i]); xv[8 * q + 2 * i + 1] = bf16_hi(ww[i]); }
-    }
+    for (int i = 0; i < 4; ++i) { v[j][2 * i] = bf16_lo(xa[i]); v[j][2 * i + 1] = bf16_hi(xa[i]); }
     if (ADD) {
-      const uint4* rp = reinterpret_cast<const uint4*>(a.residual + (size_t)g * 32);
+      const uint4 rw = reinterpret_cast<const uint4*>(a.residual)[word];
+      const uint32_t ra[4] = {rw.x, rw.y, rw.z, rw.w};
+      uint32_t o[4];
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const uint4 w = rp[q];
-        const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
-        uint32_t o[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          float& lo = xv[8 * q + 2 * i];
-          float& hi = xv[8 * q + 2 * i + 1];
-          lo = round_bf16(lo + bf16_lo(ww[i]));
-          hi = round_bf16(hi + bf16_hi(ww[i]));
-          __nv_bfloat162 pr = __floats2bfloat162_rn(lo, hi);
-          o[i] = *reinterpret_cast<uint32_t*>(&pr);
-        }
-        if (a.summed && blockIdx.x == 0 && part == 0)
-          reinterpret_cast<uint4*>(a.summed + (size_t)g * 32)[q] = make_uint4(o[0], o[1], o[2], o[3]);
+      for (int i = 0; i < 4; ++i) {
+        v[j][2 * i] = round_bf16(v[j][2 * i] + bf16_lo(ra[i]));
+        v[j][2 * i + 1] = round_bf16(v[j][2 * i + 1] + bf16_hi(ra[i]));
+        __nv_bfloat162 pr = __floats2bfloat162_rn(v[j][2 * i], v[j][2 * i + 1]);
+        o[i] = *reinterpret_cast<uint32_t*>(&pr);
       }
+      if (a.summed && blockIdx.x == 0) reinterpret_cast<uint4*>(a.summed)[word] = make_uint4(o[0], o[1], o[2], o[3]);
     }
     if (NORM) {
-      float ss = 0.f;
 #pragma unroll
-      for (int i = 0; i < 32; ++i) ss += xv[i] * xv[i];
-      ss = warp_sum(part == 0 ? ss : 0.f);
-      if (lane == 0) ssum[warp] = ss;
-      named_sync(1, consumers);
-      float tot = 0.f;
-      for (int w = 0; w < wpp; ++w) tot += ssum[w];
-      const float inv = 1.0f / sqrtf(tot / (float)K + a.eps);
-      const uint4* wp = reinterpret_cast<const uint4*>(a.norm_w + (size_t)g * 32);
+      for (int i = 0; i < 8; ++i) ss += v[j][i] * v[j][i];
+    }
+  }
+  if (NORM) {
+    ss = warp_sum(ss);
+    if (lane == 0) red[warp] = ss;
+    named_sync(1, consumers);
+    float tot = 0.f;
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const uint4 w = wp[q];
-        const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+    for (int w = 0; w < kWarps; ++w) tot += red[w];
+    const float inv = 1.0f / sqrtf(tot / (float)K + a.eps);
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          xv[8 * q + 2 * i] = round_bf16(round_bf16(xv[8 * q + 2 * i] * inv) * bf16_lo(ww[i]));
-          xv[8 * q + 2 * i + 1] = round_bf16(round_bf16(xv[8 * q + 2 * i + 1] * inv) * bf16_hi(ww[i]));
-        }
+    for (int j = 0; j < 4; ++j) {
+      if (j >= wpt || tid + j * consumers >= K / 8) continue;
+      const uint32_t na[4] = {nwv[j].x, nwv[j].y, nwv[j].z, nwv[j].w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        v[j][2 * i] = round_bf16(round_bf16(v[j][2 * i] * inv) * bf16_lo(na[i]));
+        v[j][2 * i + 1] = round_bf16(round_bf16(v[j][2 * i + 1] * inv) * bf16_hi(na[i]));
       }
     }
   }
-  float ev = 0.f, od = 0.f;
+  // Activation scale c = 2^(9 - e), e the exponent of max |x|: |x| c < 2^10, so c sum(x) over a
+  // group of 32 stays below 2^15 (fp16 range), and x c (x c / 16) is an exact fp16 normal for
+  // every |x| >= 2^-23 max |x| (2^-19 max |x|); smaller values keep their fp16 subnormal bits.
+  float mx = 0.f;
 #pragma unroll
-  for (int i = 0; i < 32; i += 2) { ev += xv[i]; od += xv[i + 1]; }
-  const float xsum = ev + od;
-  // DOT 0: fp32 magic (128 + q even k, 2048 + q odd k); DOT 1: bf16 pairs, 128 + q everywhere.
-  const float2 c0 = DOT == 0 ? make_float2(-128.f * ev, -2048.f * od) : make_float2(-128.f * xsum, 0.f);
-  uint32_t xpair[16];  // DOT 1: (x[8w + i], x[8w + i + 4]) as bf16x2, exact (x is bf16)
+  for (int j = 0; j < 4; ++j) {
+    if (j >= wpt || tid + j * consumers >= K / 8) continue;
 #pragma unroll
-  for (int w = 0; w < 4; ++w)
+    for (int i = 0; i < 8; ++i) mx = fmaxf(mx, fabsf(v[j][i]));
+  }
+  mx = warp_max(mx);
+  if (lane == 0) redmax[warp] = mx;
+  named_sync(1, consumers);
+  mx = 0.f;
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      __nv_bfloat162 pr = __floats2bfloat162_rn(xv[8 * w + i], xv[8 * w + i + 4]);
-      xpair[4 * w + i] = *reinterpret_cast<uint32_t*>(&pr);
-    }
+  for (int w = 0; w < kWarps; ++w) mx = fmaxf(mx, redmax[w]);
+  const int ex = mx > 0.f ? min(max((int)((__float_as_uint(mx) >> 23) & 0xFF) - 127, -100), 100) : 0;
+  const float cs = __uint_as_float((uint32_t)(127 + 9 - ex) << 23);           // c
+  const float inv_c = __uint_as_float((uint32_t)(127 + 24 - 9 + ex) << 23);   // 2^24 / c
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int word = tid + j * consumers;
+    if (j >= wpt || word >= K / 8) continue;  // K / 8 is a multiple of 32: whole warps skip
+    float wsum = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) wsum += v[j][i];
+    // pairs (x0, x4) c, (x1, x5) c / 16, (x2, x6) c, (x3, x7) c / 16: the code slots'
+    // (q_j, q_{j+4}) and 16 (q_{j+1}, q_{j+5}) factors
+    xp[word] = make_uint4(pack_half2(v[j][0] * cs, v[j][4] * cs), pack_half2(v[j][1] * cs * 0.0625f, v[j][5] * cs * 0.0625f),
+                          pack_half2(v[j][2] * cs, v[j][6] * cs), pack_half2(v[j][3] * cs * 0.0625f, v[j][7] * cs * 0.0625f));
+    wsum += __shfl_xor_sync(0xffffffffu, wsum, 1);
+    wsum += __shfl_xor_sync(0xffffffffu, wsum, 2);
+    if ((lane & 3) == 0) xsum[word >> 2] = wsum * cs;
+  }
+  named_sync(1, consumers);
 
+  // ---- main loop ----
+  const int r = lane >> 2, c = lane & 3;
+  const int hsel = r - 2 * c;  // this lane's B column carries group 2c + hsel (if 0 or 1)
+  uint32_t bl[16], bh[16];     // B operands of mmas 0-7 (group 2c) and 8-15 (group 2c + 1)
+  uint32_t bz0 = 0, bz1 = 0;   // B operands of the zero-point mma (hi and lo fp16 parts)
+  int cur_j = -1;
+  auto load_b = [&](int j) {   // B fragments of slice j: real data for the designated lanes only
+    const uint4* pl = hsel == 0 ? xp + j * 32 + 8 * c : zero16;
+    const uint4* ph = hsel == 1 ? xp + j * 32 + 8 * c + 4 : zero16;
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const uint4 ql = pl[u], qh = ph[u];
+      bl[4 * u] = ql.x; bl[4 * u + 1] = ql.y; bl[4 * u + 2] = ql.z; bl[4 * u + 3] = ql.w;
+      bh[4 * u] = qh.x; bh[4 * u + 1] = qh.y; bh[4 * u + 2] = qh.z; bh[4 * u + 3] = qh.w;
+    }
+    // -c sum(x) of group 2c in column 2c, of group 2c + 1 (over 16) in column 2c + 1
+    const float z0 = hsel == 0 ? -xsum[j * 8 + 2 * c] : 0.f;
+    const float z1 = hsel == 1 ? -xsum[j * 8 + 2 * c + 1] * 0.0625f : 0.f;
+    const float h0 = __half2float(__float2half_rn(z0)), h1 = __half2float(__float2half_rn(z1));
+    bz0 = pack_half2(h0, h1);
+    bz1 = pack_half2(z0 - h0, z1 - h1);
+    cur_j = j;
+  };
+
+  // block m of this warp in stage st: b0 + SB st + warp + 16 m = tile tt[m], slice jj[m]
+  int tt[BPW], jj[BPW];
+#pragma unroll
+  for (int m = 0; m < BPW; ++m) {
+    const int b = b0 + warp + kWarps * m;
+    tt[m] = b / S;
+    jj[m] = b - tt[m] * S;
+  }
   bool ok = true;
   for (int st = 0; st < stages; ++st) {
     const int slot = st % NS;
-    const unsigned parity = (unsigned)((st / NS) & 1);
-    if (!__all_sync(0xffffffffu, mbar_wait_bounded(&full[slot], parity))) { ok = false; break; }
-    const int rows = min(RS, nrows - st * RS);
-    const uint8_t* cb = codes_at(slot);
-    const __nv_bfloat16* sb = reinterpret_cast<const __nv_bfloat16*>(scales_at(slot));
-    const uint8_t* zb = zeros_at(slot);
-    float acc[NV];
+    if (st > 0) {
 #pragma unroll
-    for (int j = 0; j < RP; ++j) {
-      const int i = j * P + part;
-#pragma unroll
-      for (int h = 0; h < H; ++h) {
-        float v = 0.f;
-        if (i < rows) {
-          const int rr = h * RS + i;
-          const uint4 w = *reinterpret_cast<const uint4*>(cb + (size_t)rr * row_bytes + (size_t)g * 16);
-          const float s = bf16f(sb[(size_t)rr * G + g]);
-          float z = 8.f;
-          if (zeros) z = (float)((zb[(size_t)rr * (G >> 1) + (g >> 1)] >> ((g & 1) << 2)) & 15u);
-          float2 d0 = c0, d1 = make_float2(0.f, 0.f);
-          if (DOT == 0) {
-            dot_word(w.x, xv + 0, d0);
-            dot_word(w.y, xv + 8, d1);
-            dot_word(w.z, xv + 16, d0);
-            dot_word(w.w, xv + 24, d1);
-          } else {
-            dot_word_mixed<DOT == 2>(w.x, xpair + 0, d0);
-            dot_word_mixed<DOT == 2>(w.y, xpair + 4, d1);
-            dot_word_mixed<DOT == 2>(w.z, xpair + 8, d0);
-            dot_word_mixed<DOT == 2>(w.w, xpair + 12, d1);
-          }
-          v = s * fmaf(-z, xsum, (d0.x + d1.x) + (d0.y + d1.y));
+      for (int m = 0; m < BPW; ++m) {
+        jj[m] += SB;
+        if (jj[m] >= S) {
+          const int q = jj[m] / S;
+          tt[m] += q;
+          jj[m] -= q * S;
         }
-        acc[j * H + h] = v;
       }
     }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[slot]);  // stage slot may be refilled
-    const float tot = butterfly<NV>(acc, lane);
-    constexpr int dup = 32 / NV;
-    if ((lane & (dup - 1)) == 0) {
-      const int v = row_of<NV>(lane), j = v / H, h = v - j * H;
-      const int i = j * P + part;
-      if (i < rows) partial[((size_t)warp * max_rows + st * RS + i) * H + h] = tot;
+    if (!__all_sync(0xffffffffu, mbar_wait_bounded(&full[slot], (unsigned)((st / NS) & 1)))) { ok = false; break; }
+    const uint8_t* sbase = ring + (size_t)slot * stage_b + (size_t)warp * block_b;
+    const int first = b0 + st * SB + warp;
+    // Blocks are processed one after the other (one block's codes live at a time, which keeps
+    // the kernel within 96 registers: 17 warps put 5 on one scheduler's 16K registers); the
+    // slot is released once the last block's registers are loaded.
+#pragma unroll
+    for (int m = 0; m < BPW; ++m) {
+      const bool live = first + kWarps * m < b1;  // else past the end of this CTA's range
+      BlockRegs bk;
+      if (live) bk = load_block(sbase + (size_t)m * kWarps * block_b, lane, zeros);
+      if (m == BPW - 1) {
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[slot]);  // the slot may be refilled
+      }
+      if (live) {
+        if (jj[m] != cur_j) load_b(jj[m]);
+        float va, vb;
+        block_dot(bk, bl, bh, bz0, bz1, va, vb);
+        if (c == 0) {
+          float* pp = partial + ((size_t)warp * max_tiles + (tt[m] - t_first)) * 16;
+          pp[r] += va;
+          pp[r + 8] += vb;
+        }
+      }
     }
   }
   if (!__all_sync(0xffffffffu, ok)) ok = false;
@@ -306,116 +443,167 @@ __global__ void __launch_bounds__(P * 128 + 32 > 416 ? P * 128 + 32 : 416, 1) w4
     if (tid == 0) atomicExch(&g_error_word, 1);
     return;
   }
-  for (int i = tid; i < nrows; i += consumers) {
-    const int p = i % P;
-    float vals[H];
+  // sum the warps' rows of every local tile into partial[0][lt][*]
+  for (int i = tid; i < ntiles * 16; i += consumers) {
+    const int lt = i >> 4, tr = i & 15;
+    float sum = 0.f;
+#pragma unroll 4
+    for (int w = 0; w < kWarps; ++w) sum += partial[((size_t)w * max_tiles + lt) * 16 + tr];
+    partial[(size_t)lt * 16 + tr] = sum * inv_c;
+  }
+  named_sync(1, consumers);
+  // tiles wholly inside this CTA's range
+  for (int i = tid; i < ntiles * RT; i += consumers) {
+    const int lt = i / RT, tr = i - lt * RT, tq = t_first + lt;
+    if (tq * S < b0 || (tq + 1) * S > b1) continue;
+    const int o = tq * RT + tr;
+    if (o < n_out) a.y[o] = to_bf16(finish_row<PAIRED>(partial[lt * 16 + tr], partial[lt * 16 + 8 + tr]));
+  }
+  // Tiles shared with a neighbouring CTA. Every range holds at least S blocks, so only the
+  // first tile can miss its head (shared with CTA - 1, boundary slot CTA - 1) and only the
+  // last, a different tile, its tail (shared with CTA + 1, slot CTA). Lane 0 of warp 0 / 1
+  // publishes the tile's 16 row partials and takes the slot's ticket with one acquire-release
+  // atomic; the second CTA to arrive adds the two halves (the same fp32 sum in either order)
+  // and writes the rows.
+  if (warp < 2) {
+    const int ts = warp == 0 ? t_first : t_last;
+    const bool shared = warp == 0 ? ts * S < b0 : (t_last != t_first && (ts + 1) * S > b1);
+    if (shared && lane == 0) {
+      const int lt = ts - t_first;
+      const int side = warp == 0 ? 1 : 0;  // 1: this CTA holds the tile's tail
+      const int slot = warp == 0 ? blockIdx.x - 1 : blockIdx.x;
+      float own[16];
 #pragma unroll
-    for (int h = 0; h < H; ++h) {
-      float sacc = 0.f;
-      for (int w = 0; w < wpp; ++w) sacc += partial[((size_t)(p * wpp + w) * max_rows + i) * H + h];
-      vals[h] = sacc;
+      for (int i = 0; i < 16; ++i) own[i] = partial[lt * 16 + i];
+      float4* mine = reinterpret_cast<float4*>(a.ws + ((size_t)slot * 2 + side) * 16);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) mine[i] = make_float4(own[4 * i], own[4 * i + 1], own[4 * i + 2], own[4 * i + 3]);
+      int prev;
+      asm volatile("atom.add.acq_rel.gpu.s32 %0, [%1], 1;" : "=r"(prev) : "l"(a.tickets + slot) : "memory");
+      if (prev == 1) {  // second to arrive: finish the tile
+        const float4* other = reinterpret_cast<const float4*>(a.ws + ((size_t)slot * 2 + (1 - side)) * 16);
+        float tot[16];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float4 o = __ldcg(other + i);
+          tot[4 * i] = own[4 * i] + o.x;
+          tot[4 * i + 1] = own[4 * i + 1] + o.y;
+          tot[4 * i + 2] = own[4 * i + 2] + o.z;
+          tot[4 * i + 3] = own[4 * i + 3] + o.w;
+        }
+#pragma unroll
+        for (int tr = 0; tr < RT; ++tr) {
+          const int o = ts * RT + tr;
+          if (o < n_out) a.y[o] = to_bf16(finish_row<PAIRED>(tot[tr], tot[(tr + 8) & 15]));
+        }
+        a.tickets[slot] = 0;
+      }
     }
-    float out = vals[0];
-    if (PAIRED) {  // dp4a_packing.py:86-89
-      const float gate = round_bf16(vals[0]), up = round_bf16(vals[H - 1]);
-      out = round_bf16(gate / (1.0f + expf(-gate))) * up;
-    }
-    a.y[(size_t)r0 + i] = to_bf16(out);
   }
 }
 
-size_t stream_smem(int rs, int ns, bool paired, int k, bool zeros, int cwarps, int max_rows) {
-  const size_t G = (size_t)k / 32;
-  const int h = paired ? 2 : 1;
-  return (size_t)ns * rs * h * ((size_t)k / 2 + 2 * G + (zeros ? G / 2 : 0)) +
-         (size_t)cwarps * max_rows * h * sizeof(float);
+static size_t packed_smem(int ns, int bpw, int k, bool zeros, int max_tiles) {
+  const int block_b = kCodeBytes + kScaleBytes + (zeros ? kZeroBytes : 0);
+  return (size_t)ns * kWarps * bpw * block_b + (size_t)k / 8 * 16 + (size_t)k / 32 * 4 +
+         (size_t)kWarps * max_tiles * 16 * 4;
 }
 
-// Tuning knobs read once from the environment (defaults are the measured best):
-// MT_W4_DOT = 0 (fp32 magic + FFMA2), 1 (bf16 pairs + mixed FMA), 2 (as 1, multiply-high
-// shifts); MT_W4_PARTS = row partitions per CTA for K <= 4096 (2 or 4).
-static int env_int(const char* name, int dflt) {
-  const char* e = getenv(name);
-  return (e && e[0] >= '0' && e[0] <= '9') ? atoi(e) : dflt;
-}
-static int stream_dot_mode() {
-  static int mode = -1;
-  if (mode < 0) mode = env_int("MT_W4_DOT", 1);
-  return mode;
-}
-static int stream_parts() {
-  static int parts = -1;
-  if (parts < 0) parts = env_int("MT_W4_PARTS", 4) == 2 ? 2 : 4;
-  return parts;
-}
-
-template <int RS, int NS, int P, int DOT, bool NORM, bool ADD, bool PAIRED>
-static cudaError_t go_dot(const StreamArgs& a, cudaStream_t s, int flags) {
-  const int n_out = PAIRED ? a.n / 2 : a.n;
-  int blocks = sm_count();
-  if (blocks > n_out / 2) blocks = n_out / 2;
-  const int units = n_out / 2;
-  const int max_rows = 2 * ((units + blocks - 1) / blocks);
-  const int cwarps = P * (a.k / 32) / 32;
-  const size_t smem = stream_smem(RS, NS, PAIRED, a.k, a.qzeros != nullptr, cwarps, max_rows);
-  if (smem > 227 * 1024) return cudaErrorInvalidValue;
-  return launch(w4a16_stream<RS, NS, P, DOT, NORM, ADD, PAIRED>, dim3(blocks), dim3(P * (a.k / 32) + 32), smem,
-                s, flags, a, max_rows);
-}
-
-template <int RS, int NS, int P, bool NORM, bool ADD, bool PAIRED>
+template <int NS, int BPW, bool NORM, bool ADD, bool PAIRED>
 static cudaError_t go(const StreamArgs& a, cudaStream_t s, int flags) {
-  switch (stream_dot_mode()) {
-    case 0: return go_dot<RS, NS, P, 0, NORM, ADD, PAIRED>(a, s, flags);
-    case 2: return go_dot<RS, NS, P, 2, NORM, ADD, PAIRED>(a, s, flags);
-    default: return go_dot<RS, NS, P, 1, NORM, ADD, PAIRED>(a, s, flags);
+  const PackGeom pg(a.n, a.k, a.zeros != 0, PAIRED);
+  int grid = sm_count();
+  if (grid > pg.tiles) grid = pg.tiles;  // >= one tile of blocks per CTA: a tile spans at most two CTAs
+  if (grid > PackGeom::kMaxCtas) grid = PackGeom::kMaxCtas;
+  const long long max_blocks = (pg.blocks + grid - 1) / grid;
+  const int max_tiles = (int)((max_blocks + pg.slices - 1) / pg.slices) + 1;
+  const size_t smem = packed_smem(NS, BPW, a.k, a.zeros != 0, max_tiles);
+  if (smem > 227 * 1024) return cudaErrorInvalidValue;
+  return launch(w4a16_packed<NS, BPW, NORM, ADD, PAIRED>, dim3(grid), dim3(kWarps * 32 + 32), smem, s, flags, a,
+                max_tiles);
+}
+
+// Pipeline shape: MT_W4_PIPE = "<stages><blocks per warp>", e.g. 22 (default: two stages of
+// 32 blocks) or 31 (three stages of 16), read once from the environment.
+static int stream_pipe() {
+  static int p = -1;
+  if (p < 0) {
+    const char* e = getenv("MT_W4_PIPE");
+    p = (e && (!strcmp(e, "31") || !strcmp(e, "21") || !strcmp(e, "41") || !strcmp(e, "22"))) ? atoi(e) : 22;
+  }
+  return p;
+}
+
+template <bool NORM, bool ADD, bool PAIRED>
+static cudaError_t go_ns(const StreamArgs& a, cudaStream_t s, int flags) {
+  switch (stream_pipe()) {
+    case 21: return go<2, 1, NORM, ADD, PAIRED>(a, s, flags);
+    case 31: return go<3, 1, NORM, ADD, PAIRED>(a, s, flags);
+    case 41: return go<4, 1, NORM, ADD, PAIRED>(a, s, flags);
+    default: return go<2, 2, NORM, ADD, PAIRED>(a, s, flags);
   }
 }
 
-template <bool NORM, bool ADD>
-static cudaError_t go_k(const StreamArgs& a, bool paired, cudaStream_t s, int flags) {
-  const int G = a.k / 32;
-  if (G > 128) {  // wide K (down projection): one partition of G consumer threads
-    return paired ? go<8, 2, 1, NORM, ADD, true>(a, s, flags) : go<8, 2, 1, NORM, ADD, false>(a, s, flags);
-  }
-  if (stream_parts() == 4)
-    return paired ? go<8, 3, 4, NORM, ADD, true>(a, s, flags) : go<16, 3, 4, NORM, ADD, false>(a, s, flags);
-  return paired ? go<8, 3, 2, NORM, ADD, true>(a, s, flags) : go<16, 3, 2, NORM, ADD, false>(a, s, flags);
-}
-
-// Batch-1 entry used by mt_w4a16_linear when the shape fits this kernel.
-bool stream_supported(int batch, int n, int k, int mode) {
-  const int G = k / 32;
-  if (batch != 1 || G % 32 || G > 384) return false;
+static bool packed_shape_ok(int n, int k, int mode) {
+  if (k < kSliceCols || k % kSliceCols || k > 16384 || (mode & ~7)) return false;
   const int n_out = (mode & 4) ? n / 2 : n;
-  if (n_out % 2) return false;
-  return true;
-}
-
-cudaError_t stream_launch(const void* x, const void* residual, const void* norm_w, float eps, void* summed,
-                          const void* qweight, const void* scales, const void* qzeros, void* y, int n, int k,
-                          int mode, int flags, cudaStream_t s) {
-  StreamArgs a;
-  a.x = (const __nv_bfloat16*)x;
-  a.residual = (const __nv_bfloat16*)residual;
-  a.norm_w = (const __nv_bfloat16*)norm_w;
-  a.summed = (__nv_bfloat16*)summed;
-  a.qweight = (const uint8_t*)qweight;
-  a.scales = (const __nv_bfloat16*)scales;
-  a.qzeros = (const uint8_t*)qzeros;
-  a.y = (__nv_bfloat16*)y;
-  a.n = n;
-  a.k = k;
-  a.eps = eps;
-  const bool paired = mode & 4;
-  if (mode & 2) return go_k<true, true>(a, paired, s, flags);
-  if (mode & 1) return go_k<true, false>(a, paired, s, flags);
-  return go_k<false, false>(a, paired, s, flags);
+  return n >= 2 && (!(mode & 4) || n % 2 == 0) && n_out >= 1;
 }
 
 }  // namespace mt
 
 using namespace mt;
+
+MT_API int mt_w4a16_packed_size(int n, int k, int has_zeros, int mode, long long* packed_bytes,
+                                long long* workspace_bytes) {
+  if (!packed_shape_ok(n, k, mode)) return kBadArgument;
+  const PackGeom pg(n, k, has_zeros != 0, (mode & 4) != 0);
+  if (packed_bytes) *packed_bytes = (long long)pg.packed_bytes();
+  if (workspace_bytes) *workspace_bytes = (long long)PackGeom::workspace_bytes();
+  return 0;
+}
+
+MT_API int mt_w4a16_pack(const void* qweight, const void* scales, const void* qzeros, int n, int k, int mode,
+                         void* packed, void* stream) {
+  if (!qweight || !scales || !packed || !packed_shape_ok(n, k, mode)) return kBadArgument;
+  if (!aligned(qweight, 16) || !aligned(scales, 2) || !aligned(packed, 16)) return kBadArgument;
+  const PackGeom pg(n, k, qzeros != nullptr, (mode & 4) != 0);
+  const unsigned warps_per_cta = 8;
+  const long long ctas = (pg.blocks + warps_per_cta - 1) / warps_per_cta;
+  w4a16_pack_blocks<<<(unsigned)ctas, warps_per_cta * 32, 0, (cudaStream_t)stream>>>(
+      (const uint8_t*)qweight, (const uint16_t*)scales, (const uint8_t*)qzeros, (uint8_t*)packed, pg.n_out, k,
+      pg.slices, pg.blocks, pg.block_b, (mode & 4) ? 1 : 0);
+  return (int)cudaGetLastError();
+}
+
+MT_API int mt_w4a16_linear_packed(const void* x, const void* residual, const void* norm_w, float eps, void* summed,
+                                  const void* packed, int has_zeros, void* y, int n, int k, int mode,
+                                  void* workspace, int flags, void* stream) {
+  if (!x || !packed || !y || !workspace || !packed_shape_ok(n, k, mode)) return kBadArgument;
+  if ((mode & 2) && (!(mode & 1) || !residual)) return kBadArgument;
+  if ((mode & 1) && !norm_w) return kBadArgument;
+  if (!aligned(x, 16) || !aligned(packed, 16) || !aligned(workspace, 16) || (residual && !aligned(residual, 16)) ||
+      (summed && !aligned(summed, 16)) || (norm_w && !aligned(norm_w, 16)))
+    return kBadArgument;
+  StreamArgs a;
+  a.x = (const __nv_bfloat16*)x;
+  a.residual = (const __nv_bfloat16*)residual;
+  a.norm_w = (const __nv_bfloat16*)norm_w;
+  a.summed = (__nv_bfloat16*)summed;
+  a.packed = (const uint8_t*)packed;
+  a.y = (__nv_bfloat16*)y;
+  a.ws = (float*)workspace;
+  a.tickets = (int*)((uint8_t*)workspace + (size_t)PackGeom::kMaxCtas * 2 * 16 * sizeof(float));
+  a.n = n;
+  a.k = k;
+  a.zeros = has_zeros ? 1 : 0;
+  a.eps = eps;
+  cudaStream_t s = (cudaStream_t)stream;
+  flags &= kFlagPdl;
+  const bool paired = mode & 4;
+  if (mode & 2) return (int)(paired ? go_ns<true, true, true>(a, s, flags) : go_ns<true, true, false>(a, s, flags));
+  if (mode & 1) return (int)(paired ? go_ns<true, false, true>(a, s, flags) : go_ns<true, false, false>(a, s, flags));
+  return (int)(paired ? go_ns<false, false, true>(a, s, flags) : go_ns<false, false, false>(a, s, flags));
+}
 
 // Diagnostic read of the library's error word on the current device (1 after a kernel
 // abandoned a bounded wait); optionally clears it. Synchronous, unlike every other call.

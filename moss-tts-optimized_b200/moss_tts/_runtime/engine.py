@@ -139,14 +139,31 @@ class DecodeEngine:
         self._host_next = torch.zeros(CONTROL_IDS, dtype=torch.long, pin_memory=True)
         self._scalars = torch.zeros(3, dtype=torch.long, pin_memory=True)
         self._staged = None
+        # batch-1 W4 projections run on the packed layout; one workspace serves them all
+        ws = 0
+        for lw in weights.layers:
+            for p, paired in ((lw.qkv, False), (lw.out, False), (lw.gate_up, True), (lw.down, False)):
+                if self._packed_ok(p, paired):
+                    p.packed_tiles(paired)
+                    ws = max(ws, native.w4a16_packed_size(p.n, p.k, p.qzeros is not None,
+                                                          native.LINEAR_PAIRED if paired else 0)[1])
+        self.w4_workspace = torch.zeros(max(ws, 16), device=dev, dtype=torch.uint8)
 
     # ------------------------------------------------------------------ kernels
+    @staticmethod
+    def _packed_ok(p: Projection, paired: bool) -> bool:
+        return p.quantized and p.k % 256 == 0 and 256 <= p.k <= 16384 and (not paired or p.n % 2 == 0)
+
     def _linear(self, p: Projection, x, y, *, residual=None, norm=None, summed=None, paired=False):
         mode = (native.LINEAR_NORM if norm is not None else 0) | (native.LINEAR_ADD if residual is not None else 0)
         mode |= native.LINEAR_PAIRED if paired else 0
         eps = float(self.cfg.rms_norm_eps)
         s = torch.cuda.current_stream(self.device).cuda_stream
-        if p.quantized:
+        if self._packed_ok(p, paired):
+            native.call("mt_w4a16_linear_packed", x.data_ptr(), native.ptr(residual), native.ptr(norm), eps,
+                        native.ptr(summed), p.packed_tiles(paired).data_ptr(), 1 if p.qzeros is not None else 0,
+                        y.data_ptr(), p.n, p.k, mode, self.w4_workspace.data_ptr(), self.flags, s)
+        elif p.quantized:
             native.call("mt_w4a16_linear", x.data_ptr(), native.ptr(residual), native.ptr(norm), eps,
                         native.ptr(summed), p.qweight.data_ptr(), p.scales.data_ptr(), native.ptr(p.qzeros),
                         y.data_ptr(), 1, p.n, p.k, 32, mode, self.flags, s)

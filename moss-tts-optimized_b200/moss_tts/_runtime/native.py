@@ -17,6 +17,7 @@ FLAG_REGISTER_PIPELINE = 2
 LINEAR_NORM, LINEAR_ADD, LINEAR_PAIRED = 1, 2, 4
 
 _P, _I, _F = ctypes.c_void_p, ctypes.c_int, ctypes.c_float
+_LLP = ctypes.POINTER(ctypes.c_longlong)
 
 # name -> (argtypes, restype); mirrors include/moss_tts_b200.h
 SIGNATURES = {
@@ -24,6 +25,9 @@ SIGNATURES = {
     "mt_read_error_word": ([ctypes.POINTER(ctypes.c_int), _I], _I),
     "mt_dequant_w4": ([_P, _P, _P, _P, _I, _I, _I, _P], _I),
     "mt_w4a16_linear": ([_P, _P, _P, _F, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P], _I),
+    "mt_w4a16_packed_size": ([_I, _I, _I, _I, _LLP, _LLP], _I),
+    "mt_w4a16_pack": ([_P, _P, _P, _I, _I, _I, _P, _P], _I),
+    "mt_w4a16_linear_packed": ([_P, _P, _P, _F, _P, _P, _I, _P, _I, _I, _I, _P, _I, _P], _I),
     "mt_bf16_linear": ([_P, _P, _P, _F, _P, _P, _P, _I, _I, _I, _I, _I, _P], _I),
     "mt_rmsnorm": ([_P, _P, _P, _P, _P, _I, _I, _F, _I, _P], _I),
     "mt_silu_mul": ([_P, _P, _I, _I, _I, _P], _I),
@@ -67,6 +71,13 @@ def error_word(clear: bool = False) -> int:
     v = ctypes.c_int(0)
     call("mt_read_error_word", ctypes.byref(v), 1 if clear else 0)
     return v.value
+
+
+def w4a16_packed_size(n: int, k: int, has_zeros: bool, mode: int) -> tuple[int, int]:
+    """(packed weight bytes, workspace bytes) of an [n, k] projection in the packed layout."""
+    pb, wb = ctypes.c_longlong(0), ctypes.c_longlong(0)
+    call("mt_w4a16_packed_size", n, k, 1 if has_zeros else 0, mode, ctypes.byref(pb), ctypes.byref(wb))
+    return pb.value, wb.value
 
 
 def ptr(t) -> int | None:

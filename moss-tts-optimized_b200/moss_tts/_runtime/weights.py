@@ -43,10 +43,27 @@ class Projection:
     scales: torch.Tensor | None = None   # bf16 [N, K/32]
     qzeros: torch.Tensor | None = None   # uint8 [N, K/64] or None (z = 8)
     weight: torch.Tensor | None = None   # bf16 [N, K] (bf16 preset)
+    packed: dict = field(default_factory=dict, repr=False, compare=False)  # paired -> packed tiles
 
     @property
     def quantized(self) -> bool:
         return self.qweight is not None
+
+    def packed_tiles(self, paired: bool = False) -> torch.Tensor:
+        """Tile-major copy of the W4 weights for ``mt_w4a16_linear_packed``, made on first
+        use on the weights' device (the load-time repack; ``paired`` interleaves the gate
+        and up halves tile by tile)."""
+        key = bool(paired)
+        if key not in self.packed:
+            from . import native
+            mode = native.LINEAR_PAIRED if paired else 0
+            nbytes, _ = native.w4a16_packed_size(self.n, self.k, self.qzeros is not None, mode)
+            buf = torch.empty(nbytes, dtype=torch.uint8, device=self.qweight.device)
+            native.call("mt_w4a16_pack", self.qweight.data_ptr(), self.scales.data_ptr(),
+                        native.ptr(self.qzeros), self.n, self.k, mode, buf.data_ptr(),
+                        torch.cuda.current_stream(buf.device).cuda_stream)
+            self.packed[key] = buf
+        return self.packed[key]
 
     @classmethod
     def from_host(cls, p: dict, device) -> "Projection":

@@ -24,6 +24,8 @@ def header_prototypes():
         for a in args:
             if a.startswith("int*"):
                 kinds.append("ip")
+            elif a.startswith("long long*"):
+                kinds.append("llp")
             elif "*" in a:
                 kinds.append("p")
             elif a.startswith("float"):
@@ -61,7 +63,8 @@ def test_library_exports_every_declared_symbol(lib):
 
 def test_ctypes_signatures_match_header():
     from moss_tts._runtime import native
-    kind = {ctypes.c_void_p: "p", ctypes.c_int: "i", ctypes.c_float: "f", ctypes.POINTER(ctypes.c_int): "ip"}
+    kind = {ctypes.c_void_p: "p", ctypes.c_int: "i", ctypes.c_float: "f", ctypes.POINTER(ctypes.c_int): "ip",
+            ctypes.POINTER(ctypes.c_longlong): "llp"}
     protos = header_prototypes()
     assert set(native.SIGNATURES) == set(protos)
     for name, (args, res) in native.SIGNATURES.items():

@@ -248,8 +248,10 @@ def test_qk_norm_rope_matches_transformers(cuda_device):
     close(host_bits(kd)[0, :, 77], from_bf16_bits(g["rope_k"]))
 
 
-def test_attention_ragged_batch(cuda_device):
-    """Config 4 shape: several sequences with different live lengths in one launch."""
+@pytest.mark.parametrize("flags", [0, 2, 1])
+def test_attention_ragged_batch(cuda_device, flags):
+    """Config 4 shape: several sequences with different live lengths in one launch, through the
+    cluster kernel (default), the split-K kernel (flags bit 1) and with PDL (bit 0)."""
     from moss_tts._runtime import native
     g = golden("ops")
     lens = [256, 1000, 4095, 3]
@@ -268,7 +270,7 @@ def test_attention_ragged_batch(cuda_device):
     qn, kn = dev_bf16(g["rope_qn"], cuda_device), dev_bf16(g["rope_kn"], cuda_device)
     native.call("mt_attention_decode", dev_bf16(qkv, cuda_device).data_ptr(), qn.data_ptr(), kn.data_ptr(),
                 cos.data_ptr(), sin.data_ptr(), pos.data_ptr(), kd.data_ptr(), vd.data_ptr(), out.data_ptr(),
-                partial.data_ptr(), lse.data_ptr(), tickets.data_ptr(), B, 32, 8, L, splits, 1e-6, None, 0,
+                partial.data_ptr(), lse.data_ptr(), tickets.data_ptr(), B, 32, 8, L, splits, 1e-6, None, flags,
                 torch.cuda.current_stream().cuda_stream)
     assert int(tickets.abs().sum()) == 0
     c_all, s_all = ops.rope_table(lens)
@@ -322,10 +324,36 @@ def test_heads_greedy_against_oracle(cuda_device):
         assert int(best.abs().sum()) == 0 and int(ticket.item()) == 0
 
 
-# ------------------------------------------------------------------ streaming vs register kernels
+# ------------------------------------------------------------------ packed tensor-core GEMV
+def packed_linear(native, qw, sc, qz, n, k, mode, x, r, w, flags, device, ws=None, calls=1):
+    """Pack once, then run mt_w4a16_linear_packed `calls` times; returns (y bits, summed bits, ws)."""
+    nbytes, wbytes = native.w4a16_packed_size(n, k, qz is not None, mode & 4)
+    packed = torch.empty(nbytes, dtype=torch.uint8, device=device)
+    s = torch.cuda.current_stream().cuda_stream
+    native.call("mt_w4a16_pack", qw.data_ptr(), sc.data_ptr(), native.ptr(qz), n, k, mode & 4,
+                packed.data_ptr(), s)
+    if ws is None:
+        ws = torch.zeros(max(wbytes, 16), dtype=torch.uint8, device=device)
+    n_out = n // 2 if mode & 4 else n
+    outs = []
+    for _ in range(calls):
+        y = torch.empty((1, n_out), device=device, dtype=torch.bfloat16)
+        summed = torch.empty_like(x)
+        native.call("mt_w4a16_linear_packed", x.data_ptr(), r.data_ptr() if mode & 2 else None,
+                    w.data_ptr() if mode & 1 else None, 1e-6, summed.data_ptr() if mode & 2 else None,
+                    packed.data_ptr(), 1 if qz is not None else 0, y.data_ptr(), n, k, mode, ws.data_ptr(),
+                    flags, s)
+        outs.append((host_bits(y), host_bits(summed)))
+    return outs, ws
+
+
 @pytest.mark.parametrize("n,k,mode", [(6144, 4096, 1), (4096, 4096, 0), (24576, 4096, 7), (4096, 12288, 0),
-                                      (12288, 4096, 0), (1536, 3072, 3), (2048, 1024, 4), (768, 6144, 0)])
-def test_stream_kernel_matches_register_kernel_and_oracle(cuda_device, n, k, mode):
+                                      (12288, 4096, 0), (1536, 3072, 3), (2048, 1024, 4), (768, 6144, 0),
+                                      (300, 1024, 4), (40, 512, 2 | 1), (26, 256, 4), (1000, 2048, 0)])
+def test_packed_kernel_matches_oracle_and_register_kernel(cuda_device, n, k, mode):
+    """Split-K tensor-core GEMV over the packed layout: oracle parity (fixed tolerance), agreement
+    with the GPTQ-layout register kernel, PDL launch bitwise equal, repeat calls bitwise equal
+    (the workspace tickets return to zero), ragged tiles and single-slice K."""
     from moss_tts._runtime import native
     rng = np.random.Generator(np.random.PCG64(n + 3 * k + mode))
     p = synthetic.quantized(rng, n, k, 32, mode != 0)
@@ -333,22 +361,24 @@ def test_stream_kernel_matches_register_kernel_and_oracle(cuda_device, n, k, mod
     xb, rb = synthetic.activation(11 + n, (1, k)), synthetic.activation(12 + n, (1, k))
     nw = bf16_bits(from_bf16_bits(synthetic.activation(13, (k,), 0.02)) + 1.0)
     x, r, w = dev_bf16(xb, cuda_device), dev_bf16(rb, cuda_device), dev_bf16(nw, cuda_device)
+    ws = torch.zeros(native.w4a16_packed_size(n, k, qz is not None, mode & 4)[1], dtype=torch.uint8,
+                     device=cuda_device)
+    ws[:1024 * 128].fill_(0x7F)  # partial-row slots hold stale data between calls; only tickets must be zero
+    outs, ws = packed_linear(native, qw, sc, qz, n, k, mode, x, r, w, 0, cuda_device, ws=ws, calls=2)
+    pdl, _ = packed_linear(native, qw, sc, qz, n, k, mode, x, r, w, 1, cuda_device, ws=ws)
     n_out = n // 2 if mode & 4 else n
-    outs, sums = [], []
-    for flags in (0, 2, 1):  # streaming, register-pipelined, streaming with PDL
-        y = torch.empty((1, n_out), device=cuda_device, dtype=torch.bfloat16)
-        s = torch.empty_like(x)
+    yreg = None
+    if n % (8 if mode & 4 else 4) == 0:  # shapes the GPTQ-layout register kernel accepts
+        yreg = torch.empty((1, n_out), device=cuda_device, dtype=torch.bfloat16)
+        sreg = torch.empty_like(x)
         native.call("mt_w4a16_linear", x.data_ptr(), r.data_ptr() if mode & 2 else None,
-                    w.data_ptr() if mode & 1 else None, 1e-6, s.data_ptr() if mode & 2 else None,
-                    qw.data_ptr(), sc.data_ptr(), native.ptr(qz), y.data_ptr(), 1, n, k, 32, mode, flags,
+                    w.data_ptr() if mode & 1 else None, 1e-6, sreg.data_ptr() if mode & 2 else None,
+                    qw.data_ptr(), sc.data_ptr(), native.ptr(qz), yreg.data_ptr(), 1, n, k, 32, mode, 0,
                     torch.cuda.current_stream().cuda_stream)
-        outs.append(host_bits(y))
-        sums.append(host_bits(s))
     xin = from_bf16_bits(xb)
     if mode & 2:
         s_ref, h = ops.add_rmsnorm(xin, from_bf16_bits(rb), from_bf16_bits(nw), 1e-6)
-        for sm in sums:
-            assert np.array_equal(sm, bf16_bits(s_ref))
+        assert np.array_equal(outs[0][1], bf16_bits(s_ref))
     elif mode & 1:
         h = ops.rmsnorm(xin, from_bf16_bits(nw), 1e-6)
     else:
@@ -356,14 +386,26 @@ def test_stream_kernel_matches_register_kernel_and_oracle(cuda_device, n, k, mod
     ref = ops.linear(h, quant.dequantize_w4(p["qweight"], p["scales"], p["qzeros"]))
     if mode & 4:
         ref = ops.silu_mul(ref)
-    for o in outs:
-        close(o, ref)
-    # streaming and register kernels sum in different orders; a one-ulp change of the bf16
-    # gate can move bf16(silu(gate)) * up by two ulps, so allow two
-    a, b = from_bf16_bits(outs[0]), from_bf16_bits(outs[1])
-    assert np.all(np.abs(a - b) <= 2.0 ** -6 * np.maximum(np.abs(a), np.abs(b)) + 2.0 ** -14)
-    assert np.array_equal(outs[0], outs[2])
+    close(outs[0][0], ref)
+    # the two kernels sum in different orders; a one-ulp change of the bf16 gate can move
+    # bf16(silu(gate)) * up by two ulps, so allow two
+    if yreg is not None:
+        a, b = from_bf16_bits(outs[0][0]), from_bf16_bits(host_bits(yreg))
+        assert np.all(np.abs(a - b) <= 2.0 ** -6 * np.maximum(np.abs(a), np.abs(b)) + 2.0 ** -14)
+    assert np.array_equal(outs[0][0], outs[1][0]) and np.array_equal(outs[0][0], pdl[0][0])
+    # workspace: [1024 CTA boundaries][2][16] f32 partial rows, then [1024] i32 tickets
+    assert int(ws[1024 * 128:].view(torch.int32).abs().sum()) == 0
     assert native.error_word() == 0
+
+
+def test_packed_size_and_bad_arguments(cuda_device):
+    from moss_tts._runtime import native
+    assert native.w4a16_packed_size(4096, 4096, True, 0) == (256 * 16 * 2368, 1024 * (128 + 4))
+    assert native.w4a16_packed_size(24576, 4096, False, 4) == (1536 * 16 * 2304, 1024 * (128 + 4))
+    with pytest.raises(RuntimeError):
+        native.w4a16_packed_size(64, 1000, True, 0)  # K not a multiple of 256
+    with pytest.raises(RuntimeError):  # null workspace
+        native.call("mt_w4a16_linear_packed", 16, None, None, 0.0, None, 16, 1, 16, 64, 1024, 0, None, 0, None)
 
 
 def test_heads_tensor_parallel_shard_writes_only_its_codebooks(cuda_device):
