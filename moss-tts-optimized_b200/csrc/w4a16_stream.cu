@@ -118,6 +118,7 @@ struct StreamArgs {
   float* ws;      // [CTA boundary][2][16] partial rows of the tile two neighbouring CTAs share
   int* tickets;   // [CTA boundary], zero between launches
   int n, k, zeros;
+  int tile_aligned;  // CTA ranges on whole tiles (no tile shared between CTAs)
   float eps;
 };
 
@@ -216,7 +217,10 @@ __global__ void __launch_bounds__(kWarps * 32 + 32, 1) w4a16_packed(StreamArgs a
   const int n_out = PAIRED ? a.n / 2 : a.n;
   const int T = (n_out + RT - 1) / RT;
   const int NB = T * S;  // < 2^31 for every accepted shape (n < 2^24, S <= 64)
-  const int b0 = (int)((long long)blockIdx.x * NB / gridDim.x), b1 = (int)((long long)(blockIdx.x + 1) * NB / gridDim.x);
+  const int b0 = a.tile_aligned ? (int)((long long)blockIdx.x * T / gridDim.x) * S
+                                : (int)((long long)blockIdx.x * NB / gridDim.x);
+  const int b1 = a.tile_aligned ? (int)((long long)(blockIdx.x + 1) * T / gridDim.x) * S
+                                : (int)((long long)(blockIdx.x + 1) * NB / gridDim.x);
   const int nblk = b1 - b0;
   const int stages = (nblk + SB - 1) / SB;
   const int t_first = b0 / S, t_last = (b1 - 1) / S;
@@ -508,13 +512,27 @@ static size_t packed_smem(int ns, int bpw, int k, bool zeros, int max_tiles) {
          (size_t)kWarps * max_tiles * 16 * 4;
 }
 
+// MT_W4_SPLIT = 1 forces split-K ranges, 2 whole-tile ranges (default: whole tiles when
+// there are at least as many tiles as SMs, where the exchange of a split tile costs more
+// than the imbalance of whole tiles; split-K otherwise).
+static int split_mode() {
+  static int m = -1;
+  if (m < 0) {
+    const char* e = getenv("MT_W4_SPLIT");
+    m = (e && (e[0] == '1' || e[0] == '2') && e[1] == 0) ? e[0] - '0' : 0;
+  }
+  return m;
+}
+
 template <int NS, int BPW, bool NORM, bool ADD, bool PAIRED>
-static cudaError_t go(const StreamArgs& a, cudaStream_t s, int flags) {
+static cudaError_t go(StreamArgs a, cudaStream_t s, int flags) {
   const PackGeom pg(a.n, a.k, a.zeros != 0, PAIRED);
   int grid = sm_count();
   if (grid > pg.tiles) grid = pg.tiles;  // >= one tile of blocks per CTA: a tile spans at most two CTAs
   if (grid > PackGeom::kMaxCtas) grid = PackGeom::kMaxCtas;
-  const long long max_blocks = (pg.blocks + grid - 1) / grid;
+  a.tile_aligned = split_mode() == 2 || (split_mode() == 0 && pg.tiles >= sm_count());
+  const long long max_blocks = a.tile_aligned ? (long long)((pg.tiles + grid - 1) / grid) * pg.slices
+                                              : (pg.blocks + grid - 1) / grid;
   const int max_tiles = (int)((max_blocks + pg.slices - 1) / pg.slices) + 1;
   const size_t smem = packed_smem(NS, BPW, a.k, a.zeros != 0, max_tiles);
   if (smem > 227 * 1024) return cudaErrorInvalidValue;
