@@ -45,6 +45,9 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--layers", type=int, default=36, help=argparse.SUPPRESS)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile-kernel", action="store_true",
+                    help="only launch the dominant kernel (packed add+norm+gate/up+SiLU GEMV), once per "
+                         "layer per step, for an ncu capture; prints its mean launch time")
     return ap.parse_args()
 
 
@@ -167,6 +170,55 @@ def run_reference(args, rank):
 
 
 # ---------------------------------------------------------------------------- GPU leg
+def packed_gate_up(native, lw, x, r, summed, mid, workspace, flags, stream_ptr):
+    """One launch of the decode step's dominant kernel: add + RMSNorm + gate/up + SiLU over the
+    packed W4 tiles (what DecodeEngine runs)."""
+    p = lw.gate_up
+    native.call("mt_w4a16_linear_packed", x.data_ptr(), r.data_ptr(), lw.post_norm.data_ptr(), 1e-6,
+                summed.data_ptr(), p.packed_tiles(True).data_ptr(), 1 if p.qzeros is not None else 0,
+                mid.data_ptr(), p.n, p.k, 7, workspace.data_ptr(), flags, stream_ptr)
+
+
+def profile_kernel(args):
+    """Eager launches of the dominant kernel over each layer's weights (no graph, so every
+    launch is visible to a profiler); inputs larger than L2 once there are 3+ layers."""
+    import torch
+
+    from moss_tts._runtime import native
+    from moss_tts._runtime.config import DecoderConfig
+    from moss_tts._runtime.weights import DecoderWeights
+
+    dev = torch.device("cuda", 0)
+    cfg = DecoderConfig().with_(num_layers=args.layers)
+    with torch.inference_mode():
+        w = DecoderWeights.random(cfg, dev, seed=0, preset="gptq", full_text_head=False)
+        for lw in w.layers:
+            lw.gate_up.packed_tiles(True)
+        x = torch.randn(cfg.hidden_size, device=dev).bfloat16()
+        r = torch.randn(cfg.hidden_size, device=dev).bfloat16()
+        summed = torch.empty_like(x)
+        mid = torch.empty(cfg.intermediate_size, device=dev, dtype=torch.bfloat16)
+        ws = torch.zeros(native.w4a16_packed_size(2 * cfg.intermediate_size, cfg.hidden_size, True, 4)[1],
+                         device=dev, dtype=torch.uint8)
+        s = torch.cuda.current_stream(dev)
+        for _ in range(args.warmup):
+            for lw in w.layers:
+                packed_gate_up(native, lw, x, r, summed, mid, ws, native.FLAG_PDL, s.cuda_stream)
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(s)
+        for _ in range(args.steps):
+            for lw in w.layers:
+                packed_gate_up(native, lw, x, r, summed, mid, ws, native.FLAG_PDL, s.cuda_stream)
+        e1.record(s)
+        torch.cuda.synchronize(dev)
+        us = e0.elapsed_time(e1) * 1000 / (args.steps * len(w.layers))
+    print(json.dumps({"kernel": "mt_w4a16_linear_packed gate/up (N=%d K=%d)" % (2 * cfg.intermediate_size,
+                                                                            cfg.hidden_size),
+                      "launches": args.steps * len(w.layers), "eager_launch_us": round(us, 3),
+                      "bytes_per_launch": gate_up_bytes(cfg.hidden_size, 2 * cfg.intermediate_size)}), flush=True)
+
+
 def main():
     args = parse()
     rank = int(os.environ.get("RANK", "0"))
@@ -174,6 +226,9 @@ def main():
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         run_reference(args, rank)
+        return
+    if args.profile_kernel:
+        profile_kernel(args)
         return
     import torch
     import torch.distributed as dist
@@ -255,23 +310,18 @@ def main():
             dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
         e2e_value = args.steps / (float(e2e_ms.item()) / 1000.0)
 
-        # ---------------- dominant kernel: fused add+norm+gate/up+SiLU W4A16 GEMV, one
-        # launch per layer (each layer's 58 MB of weights: cold in L2), CUDA events
+        # ---------------- dominant kernel: fused add+norm+gate/up+SiLU W4A16 GEMV on the packed
+        # tiles, one launch per layer (each layer's 58 MB of weights: cold in L2), CUDA events
         lw0 = weights.layers[0].gate_up
         x = torch.randn(cfg.hidden_size, device=dev).bfloat16()
         r = torch.randn(cfg.hidden_size, device=dev).bfloat16()
         summed = torch.empty_like(x)
         mid = torch.empty(lw0.n // 2, device=dev, dtype=torch.bfloat16)
-        s_ptr = stream.cuda_stream
-
-        def gate_up(lw):
-            p = lw.gate_up
-            native.call("mt_w4a16_linear", x.data_ptr(), r.data_ptr(), lw.post_norm.data_ptr(), 1e-6,
-                        summed.data_ptr(), p.qweight.data_ptr(), p.scales.data_ptr(), native.ptr(p.qzeros),
-                        mid.data_ptr(), 1, p.n, p.k, 32, 7, native.FLAG_PDL, s_ptr)
         # captured in a CUDA graph (as inside the decode step) so host launch overhead is not timed
         side = torch.cuda.Stream(dev)
-        s_ptr = side.cuda_stream
+
+        def gate_up(lw):
+            packed_gate_up(native, lw, x, r, summed, mid, eng.w4_workspace, native.FLAG_PDL, side.cuda_stream)
         with torch.cuda.stream(side):
             for lw in weights.layers:
                 gate_up(lw)
@@ -322,7 +372,7 @@ def main():
                    "hbm_roofline_frac": round(step_bytes / (ms / args.steps * 1e-3) / 1e9 / peak, 4)},
         "e2e": {"value": round(e2e_value, 3), "unit": UNIT, "h2d_bytes_per_step": 36 * 8,
                 "d2h_bytes_per_step": 33 * 8},
-        "roofline": {"bound": "hbm", "kernel": "mt_w4a16_linear (add+RMSNorm+gate/up+SiLU, N=%d K=%d)" % (lw0.n, lw0.k),
+        "roofline": {"bound": "hbm", "kernel": "mt_w4a16_linear_packed (add+RMSNorm+gate/up+SiLU, N=%d K=%d)" % (lw0.n, lw0.k),
                      "achieved": round(achieved, 1), "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "traffic": traffic, "bytes_per_launch": gu_bytes,
                      "launch_us": round(kernel_us, 3)},

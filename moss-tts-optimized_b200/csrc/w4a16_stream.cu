@@ -204,6 +204,7 @@ __global__ void __launch_bounds__(kWarps * 32 + 32, 1) w4a16_packed(StreamArgs a
   __shared__ __align__(8) uint64_t empty[NS];
   __shared__ float red[kWarps];
   __shared__ float redmax[kWarps];
+  __shared__ float redw[kWarps];
   __shared__ __align__(16) uint4 zero16[4];
   __shared__ int failed;
   constexpr int RT = PAIRED ? 8 : 16;  // output rows per tile
@@ -284,18 +285,20 @@ __global__ void __launch_bounds__(kWarps * 32 + 32, 1) w4a16_packed(StreamArgs a
   }
   pdl_wait();
   pdl_trigger();
+  const uint4* xsrc = reinterpret_cast<const uint4*>(a.x);
+  const uint4* rsrc = reinterpret_cast<const uint4*>(a.residual);
   float v[4][8];
-  float ss = 0.f;
+  float ss = 0.f, mv = 0.f, mw = 0.f;
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
     const int word = tid + j * consumers;
     if (j >= wpt || word >= K / 8) continue;
-    const uint4 xw = reinterpret_cast<const uint4*>(a.x)[word];
+    const uint4 xw = xsrc[word];
     const uint32_t xa[4] = {xw.x, xw.y, xw.z, xw.w};
 #pragma unroll
     for (int i = 0; i < 4; ++i) { v[j][2 * i] = bf16_lo(xa[i]); v[j][2 * i + 1] = bf16_hi(xa[i]); }
     if (ADD) {
-      const uint4 rw = reinterpret_cast<const uint4*>(a.residual)[word];
+      const uint4 rw = rsrc[word];
       const uint32_t ra[4] = {rw.x, rw.y, rw.z, rw.w};
       uint32_t o[4];
 #pragma unroll
@@ -307,19 +310,33 @@ __global__ void __launch_bounds__(kWarps * 32 + 32, 1) w4a16_packed(StreamArgs a
       }
       if (a.summed && blockIdx.x == 0) reinterpret_cast<uint4*>(a.summed)[word] = make_uint4(o[0], o[1], o[2], o[3]);
     }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) mv = fmaxf(mv, fabsf(v[j][i]));
     if (NORM) {
 #pragma unroll
       for (int i = 0; i < 8; ++i) ss += v[j][i] * v[j][i];
+      const uint32_t na[4] = {nwv[j].x, nwv[j].y, nwv[j].z, nwv[j].w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) mw = fmaxf(mw, fmaxf(fabsf(bf16_lo(na[i])), fabsf(bf16_hi(na[i]))));
     }
   }
-  if (NORM) {
-    ss = warp_sum(ss);
-    if (lane == 0) red[warp] = ss;
-    named_sync(1, consumers);
-    float tot = 0.f;
+  // One reduction: sum of squares (RMSNorm), max |x| and, with the norm, max |w|.
+  if (NORM) ss = warp_sum(ss);
+  mv = warp_max(mv);
+  if (NORM) mw = warp_max(mw);
+  if (lane == 0) { red[warp] = ss; redmax[warp] = mv; redw[warp] = mw; }
+  named_sync(1, consumers);
+  float tot = 0.f, mx = 0.f, mxw = 0.f;
 #pragma unroll
-    for (int w = 0; w < kWarps; ++w) tot += red[w];
+  for (int w = 0; w < kWarps; ++w) {
+    tot += red[w];
+    mx = fmaxf(mx, redmax[w]);
+    mxw = fmaxf(mxw, redw[w]);
+  }
+  if (NORM) {
     const float inv = 1.0f / sqrtf(tot / (float)K + a.eps);
+    // |bf16(bf16(x inv) w)| <= max|x| inv max|w| (1 + 2^-8)^2: a bound is enough for the scale
+    mx = mx * inv * mxw * 1.0079f;
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       if (j >= wpt || tid + j * consumers >= K / 8) continue;
@@ -331,22 +348,10 @@ __global__ void __launch_bounds__(kWarps * 32 + 32, 1) w4a16_packed(StreamArgs a
       }
     }
   }
-  // Activation scale c = 2^(9 - e), e the exponent of max |x|: |x| c < 2^10, so c sum(x) over a
-  // group of 32 stays below 2^15 (fp16 range), and x c (x c / 16) is an exact fp16 normal for
-  // every |x| >= 2^-23 max |x| (2^-19 max |x|); smaller values keep their fp16 subnormal bits.
-  float mx = 0.f;
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    if (j >= wpt || tid + j * consumers >= K / 8) continue;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) mx = fmaxf(mx, fabsf(v[j][i]));
-  }
-  mx = warp_max(mx);
-  if (lane == 0) redmax[warp] = mx;
-  named_sync(1, consumers);
-  mx = 0.f;
-#pragma unroll
-  for (int w = 0; w < kWarps; ++w) mx = fmaxf(mx, redmax[w]);
+  // Activation scale c = 2^(9 - e), e the exponent of (a bound on) max |x|: |x| c < 2^10, so
+  // c sum(x) over a group of 32 stays below 2^15 (fp16 range), and x c (x c / 16) is an exact
+  // fp16 normal for every |x| >= 2^-23 max |x| (2^-19 max |x|); smaller values keep their
+  // fp16 subnormal bits.
   const int ex = mx > 0.f ? min(max((int)((__float_as_uint(mx) >> 23) & 0xFF) - 127, -100), 100) : 0;
   const float cs = __uint_as_float((uint32_t)(127 + 9 - ex) << 23);           // c
   const float inv_c = __uint_as_float((uint32_t)(127 + 24 - 9 + ex) << 23);   // 2^24 / c
