@@ -274,21 +274,29 @@ __global__ void __launch_bounds__(128) attention_decode(AttnArgs a) {
 // Cluster decode attention: one thread-block cluster of kClusterCtas CTAs per (sequence,
 // KV head). CTA r of the cluster owns tokens [r*span, (r+1)*span), span = ceil(len / C),
 // streams them in kChunk-token chunks (K and V rows are contiguous in the cache: two bulk
-// copies per chunk, double-buffered, the first two issued before the dependency wait),
-// and keeps an online softmax per query head. The CTAs then merge through distributed
-// shared memory (cluster rank 0 reads every peer's running max, sum and unnormalised
-// output), so no global scratch, atomics or memory fences are involved.
+// copies per chunk, double-buffered, the first two issued before the dependency wait) and
+// keeps an online softmax per query head. Everything independent of the previous kernel
+// (position, RoPE rows, norm weights) is read before the wait. Per chunk:
+//   logits  - item (token, head, quarter of the 128 dims) per thread, quarters combined by
+//             two lane shuffles (q in shared memory padded per quarter: conflict free);
+//   softmax - one warp per query head (max, exp, sum, running rescale);
+//   P.V     - thread (pair of dims, token group of four) accumulates all query heads.
+// The CTAs then merge through distributed shared memory: each pushes its running max, sum
+// and the 16-dim slice of its unnormalised output owned by rank s into rank s's inbox,
+// one cluster barrier publishes them, and every rank finishes its 16 dims locally.
 constexpr int kClusterCtas = 8;
-constexpr int kChunk = 64;
+constexpr int kChunk = 128;
 
 template <int REP>
 __global__ void __launch_bounds__(256) attention_cluster(AttnArgs a) {
   extern __shared__ __align__(128) uint8_t sm[];  // 2 slots x {K[kChunk][128], V[kChunk][128]} bf16
-  __shared__ __align__(16) float qs[REP][kHeadDim];
-  __shared__ float lg[REP][kChunk];
-  __shared__ float cmax[REP][2], csum[REP][2];
+  constexpr int kQStride = 36;                     // floats per 32-dim quarter of q (+4 pad)
+  __shared__ __align__(16) float qs[REP * 4 * kQStride];
+  __shared__ __align__(16) float pr[kChunk][REP];  // logits, then probabilities
+  __shared__ __align__(16) float red[4][REP][kHeadDim];
+  __shared__ __align__(16) float inbox[kClusterCtas][REP][16];
+  __shared__ float minbox[kClusterCtas][REP], linbox[kClusterCtas][REP];
   __shared__ float m_run[REP], l_run[REP], scale[REP];
-  __shared__ float accsm[REP][kHeadDim];
   __shared__ __align__(8) uint64_t full[2];
   __shared__ int failed;
   cg::cluster_group cluster = cg::this_cluster();
@@ -307,6 +315,7 @@ __global__ void __launch_bounds__(256) attention_cluster(AttnArgs a) {
   const int n = t1 > t0 ? t1 - t0 : 0;
   const int chunks = (n + kChunk - 1) / kChunk;
   const size_t kv_base = ((size_t)b * a.nkv + kh) * a.max_len * kHeadDim;
+  const bool owner = t0 <= p && p < t1;
 
   auto issue = [&](int c) {
     const int slot = c & 1, cs = t0 + c * kChunk, rows = min(kChunk, t1 - cs);
@@ -340,44 +349,61 @@ __global__ void __launch_bounds__(256) attention_cluster(AttnArgs a) {
     for (int c = 0; c < 2 && c < chunks; ++c) issue(c);
   }
   if (tid < REP) { m_run[tid] = -INFINITY; l_run[tid] = 0.f; }
+  // Inputs that do not depend on the previous kernel: this row's RoPE factors and the
+  // head-norm weights, for warps that rotate a head (q heads: warps < REP; k: warp REP).
+  const bool rotates = warp < REP || (warp == REP && owner);
+  uint2 cw = make_uint2(0, 0), sw = make_uint2(0, 0), nw = make_uint2(0, 0);
+  if (rotates) {
+    cw = *reinterpret_cast<const uint2*>(a.cos_tab + (size_t)p * kHeadDim + 4 * lane);
+    sw = *reinterpret_cast<const uint2*>(a.sin_tab + (size_t)p * kHeadDim + 4 * lane);
+    nw = *reinterpret_cast<const uint2*>((warp < REP ? a.q_norm : a.k_norm) + 4 * lane);
+  }
   __syncthreads();
   pdl_wait();
   pdl_trigger();
   if (bad_pos && a.status && tid == 0 && rank == 0) atomicExch(a.status, 1);
   const __nv_bfloat16* src = a.qkv + (size_t)b * qkv_w;
 
-  // Query heads (warp w < REP handles head kh*REP + w), rounded to bf16 as stored by the
-  // reference (kernels.py:165), kept as fp32 for the dot products.
-  if (warp < REP) {
-    const int h = kh * REP + warp;
-    float x[4];
-    const uint2 r = *reinterpret_cast<const uint2*>(src + h * kHeadDim + 4 * lane);
-    x[0] = bf16_lo(r.x); x[1] = bf16_hi(r.x); x[2] = bf16_lo(r.y); x[3] = bf16_hi(r.y);
-    norm_rope_head(x, a.q_norm, a.cos_tab + (size_t)p * kHeadDim, a.sin_tab + (size_t)p * kHeadDim, a.eps, lane);
-    *reinterpret_cast<float4*>(&qs[warp][4 * lane]) = make_float4(x[0], x[1], x[2], x[3]);
-  }
-  const bool owner = t0 <= p && p < t1;
+  // Head RMSNorm + rotate-half RoPE (kernels.py:158-163); q rounded to bf16 as the reference
+  // stores it (kernels.py:165), kept as fp32 for the dot products.
   uint2 krow = make_uint2(0, 0), vrow = make_uint2(0, 0);
-  if (owner && warp == 0) {
-    float x[4];
-    const uint2 r = *reinterpret_cast<const uint2*>(src + (a.nq + kh) * kHeadDim + 4 * lane);
-    x[0] = bf16_lo(r.x); x[1] = bf16_hi(r.x); x[2] = bf16_lo(r.y); x[3] = bf16_hi(r.y);
-    norm_rope_head(x, a.k_norm, a.cos_tab + (size_t)p * kHeadDim, a.sin_tab + (size_t)p * kHeadDim, a.eps, lane);
-    __nv_bfloat162 lo = __floats2bfloat162_rn(x[0], x[1]), hi = __floats2bfloat162_rn(x[2], x[3]);
-    krow.x = *reinterpret_cast<uint32_t*>(&lo);
-    krow.y = *reinterpret_cast<uint32_t*>(&hi);
-    vrow = *reinterpret_cast<const uint2*>(src + (a.nq + a.nkv + kh) * kHeadDim + 4 * lane);
-    *reinterpret_cast<uint2*>(a.k_cache + kv_base + (size_t)p * kHeadDim + 4 * lane) = krow;
-    *reinterpret_cast<uint2*>(a.v_cache + kv_base + (size_t)p * kHeadDim + 4 * lane) = vrow;
+  if (rotates) {
+    const int row = warp < REP ? kh * REP + warp : a.nq + kh;
+    const uint2 r = *reinterpret_cast<const uint2*>(src + (size_t)row * kHeadDim + 4 * lane);
+    if (warp == REP) vrow = *reinterpret_cast<const uint2*>(src + (size_t)(a.nq + a.nkv + kh) * kHeadDim + 4 * lane);
+    float x[4] = {bf16_lo(r.x), bf16_hi(r.x), bf16_lo(r.y), bf16_hi(r.y)};
+    const float wv[4] = {bf16_lo(nw.x), bf16_hi(nw.x), bf16_lo(nw.y), bf16_hi(nw.y)};
+    const float cv[4] = {bf16_lo(cw.x), bf16_hi(cw.x), bf16_lo(cw.y), bf16_hi(cw.y)};
+    const float sv[4] = {bf16_lo(sw.x), bf16_hi(sw.x), bf16_lo(sw.y), bf16_hi(sw.y)};
+    float ss = x[0] * x[0] + x[1] * x[1] + x[2] * x[2] + x[3] * x[3];
+    ss = warp_sum(ss);
+    const float inv = 1.0f / sqrtf(ss / 128.f + a.eps);
+    float y[4], part[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) y[i] = round_bf16(round_bf16(x[i] * inv) * wv[i]);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) part[i] = __shfl_xor_sync(0xffffffffu, y[i], 16);  // partner d +- 64
+    const float sign = lane < 16 ? -1.f : 1.f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) x[i] = round_bf16(round_bf16(y[i] * cv[i]) + round_bf16(sign * part[i] * sv[i]));
+    if (warp < REP) {
+      // dims 4 lane .. +3 sit in quarter lane / 8
+      *reinterpret_cast<float4*>(&qs[(warp * 4 + (lane >> 3)) * kQStride + 4 * (lane & 7)]) =
+          make_float4(x[0], x[1], x[2], x[3]);
+    } else {
+      __nv_bfloat162 lo = __floats2bfloat162_rn(x[0], x[1]), hi = __floats2bfloat162_rn(x[2], x[3]);
+      krow.x = *reinterpret_cast<uint32_t*>(&lo);
+      krow.y = *reinterpret_cast<uint32_t*>(&hi);
+      *reinterpret_cast<uint2*>(a.k_cache + kv_base + (size_t)p * kHeadDim + 4 * lane) = krow;
+      *reinterpret_cast<uint2*>(a.v_cache + kv_base + (size_t)p * kHeadDim + 4 * lane) = vrow;
+    }
   }
 
-  // V accumulation layout: thread (d = tid % 128, half = tid / 128) owns heads half*HPT ...
-  constexpr int HPT = REP >= 2 ? REP / 2 : 1;
-  const int d = tid & 127, half = tid >> 7;
-  const bool vlive = half * HPT < REP;
-  float acc[HPT];
+  // P.V accumulators: thread (pair of dims dp, token group tg), all query heads.
+  const int dp = tid & 63, tg = tid >> 6;
+  float acc[REP][2];
 #pragma unroll
-  for (int j = 0; j < HPT; ++j) acc[j] = 0.f;
+  for (int h = 0; h < REP; ++h) acc[h][0] = acc[h][1] = 0.f;
   __syncthreads();
 
   int c = 0;
@@ -386,24 +412,26 @@ __global__ void __launch_bounds__(256) attention_cluster(AttnArgs a) {
     const int slot = c & 1, cs = t0 + c * kChunk, rows = min(kChunk, t1 - cs);
     const __nv_bfloat16* ks = reinterpret_cast<const __nv_bfloat16*>(sm + (size_t)slot * kSlotBytes);
     const __nv_bfloat16* vs = ks + (size_t)kChunk * kHeadDim;
-    if (owner && warp == 0 && p >= cs && p < cs + rows) {  // this step's row, fresh
+    if (owner && warp == REP && p >= cs && p < cs + rows) {  // this step's row, fresh
       *reinterpret_cast<uint2*>(const_cast<__nv_bfloat16*>(ks) + (size_t)(p - cs) * kHeadDim + 4 * lane) = krow;
       *reinterpret_cast<uint2*>(const_cast<__nv_bfloat16*>(vs) + (size_t)(p - cs) * kHeadDim + 4 * lane) = vrow;
+      __syncwarp();
     }
     __syncthreads();
-    // logits: item (head h, token t); a warp covers 32 tokens of one head
-    for (int item = tid; item < REP * kChunk; item += 256) {
-      const int h = item / kChunk, t = item - h * kChunk;
-      float v = -INFINITY;
-      if (t < rows) {
-        const uint4* krow4 = reinterpret_cast<const uint4*>(ks + (size_t)t * kHeadDim);
-        const float4* q4 = reinterpret_cast<const float4*>(&qs[h][0]);
-        float d0 = 0.f, d1 = 0.f;
+    // logits: item = ((t * REP) + h) * 4 + quarter; four consecutive lanes share (t, h)
+    const int items = rows * REP * 4;
+    for (int base = 0; base < items; base += 256) {
+      const int item = base + tid;
+      const int qt = item & 3, h = (item >> 2) % REP, t = (item >> 2) / REP;
+      float d0 = 0.f, d1 = 0.f;
+      if (item < items) {
+        const uint4* k4 = reinterpret_cast<const uint4*>(ks + (size_t)t * kHeadDim + qt * 32);
+        const float4* q4 = reinterpret_cast<const float4*>(&qs[(h * 4 + qt) * kQStride]);
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          const int cc = rot(j, t);
-          const uint4 kk = krow4[cc];
-          const float4 qa = q4[2 * cc], qb = q4[2 * cc + 1];
+        for (int jj = 0; jj < 4; ++jj) {
+          const int j = (jj + qt) & 3;  // quarters 0 / 2 (1 / 3) share banks: rotate the order
+          const uint4 kk = k4[j];
+          const float4 qa = q4[2 * j], qb = q4[2 * j + 1];
           d0 = fmaf(qa.x, bf16_lo(kk.x), d0);
           d1 = fmaf(qa.y, bf16_hi(kk.x), d1);
           d0 = fmaf(qa.z, bf16_lo(kk.y), d0);
@@ -413,48 +441,55 @@ __global__ void __launch_bounds__(256) attention_cluster(AttnArgs a) {
           d0 = fmaf(qb.z, bf16_lo(kk.w), d0);
           d1 = fmaf(qb.w, bf16_hi(kk.w), d1);
         }
-        v = (d0 + d1) * kScale;
       }
-      lg[h][t] = v;
+      float v = d0 + d1;
+      v += __shfl_xor_sync(0xffffffffu, v, 1);
+      v += __shfl_xor_sync(0xffffffffu, v, 2);
+      if (item < items && qt == 0) pr[t][h] = v * kScale;
     }
     __syncthreads();
-    // online softmax: warps 2h and 2h+1 reduce head h's 64 logits
-    if (warp < 2 * REP) {
-      const int h = warp >> 1, hf = warp & 1;
-      const float v = lg[h][hf * 32 + lane];
-      const float m = warp_max(v);
-      if (lane == 0) cmax[h][hf] = m;
-    }
-    __syncthreads();
-    if (warp < 2 * REP) {
-      const int h = warp >> 1, hf = warp & 1;
-      const float mnew = fmaxf(m_run[h], fmaxf(cmax[h][0], cmax[h][1]));
-      const float e = expf(lg[h][hf * 32 + lane] - mnew);
-      lg[h][hf * 32 + lane] = e;
-      const float sum = warp_sum(e);
-      if (lane == 0) csum[h][hf] = sum;
-    }
-    __syncthreads();
-    if (tid < REP) {
-      const float mnew = fmaxf(m_run[tid], fmaxf(cmax[tid][0], cmax[tid][1]));
-      const float sc = expf(m_run[tid] - mnew);
-      scale[tid] = sc;
-      l_run[tid] = l_run[tid] * sc + csum[tid][0] + csum[tid][1];
-      m_run[tid] = mnew;
-    }
-    __syncthreads();
-    if (vlive) {
-      const __nv_bfloat16* vcol = vs + d;
-#pragma unroll
-      for (int j = 0; j < HPT; ++j) acc[j] *= scale[half * HPT + j];
-#pragma unroll 8
-      for (int t = 0; t < rows; ++t) {
-        const float v = bf16f(vcol[(size_t)t * kHeadDim]);
-#pragma unroll
-        for (int j = 0; j < HPT; ++j) acc[j] = fmaf(lg[half * HPT + j][t], v, acc[j]);
+    // online softmax: warp h owns query head h
+    if (warp < REP) {
+      const int h = warp;
+      float m = -INFINITY;
+      for (int t = lane; t < rows; t += 32) m = fmaxf(m, pr[t][h]);
+      m = warp_max(m);
+      const float mnew = fmaxf(m_run[h], m);
+      float s = 0.f;
+      for (int t = lane; t < rows; t += 32) {
+        const float e = expf(pr[t][h] - mnew);
+        pr[t][h] = e;
+        s += e;
+      }
+      s = warp_sum(s);
+      if (lane == 0) {
+        const float sc = expf(m_run[h] - mnew);
+        scale[h] = sc;
+        l_run[h] = l_run[h] * sc + s;
+        m_run[h] = mnew;
       }
     }
-    __syncthreads();  // every thread is done with this slot
+    __syncthreads();
+    {
+      float scl[REP];
+#pragma unroll
+      for (int h = 0; h < REP; ++h) scl[h] = scale[h];
+#pragma unroll
+      for (int h = 0; h < REP; ++h) { acc[h][0] *= scl[h]; acc[h][1] *= scl[h]; }
+      const uint32_t* v2 = reinterpret_cast<const uint32_t*>(vs) + dp;
+#pragma unroll 4
+      for (int t = tg; t < rows; t += 4) {
+        const uint32_t vv = v2[(size_t)t * (kHeadDim / 2)];
+        const float va = bf16_lo(vv), vb = bf16_hi(vv);
+#pragma unroll
+        for (int h = 0; h < REP; ++h) {
+          const float ph = pr[t][h];
+          acc[h][0] = fmaf(ph, va, acc[h][0]);
+          acc[h][1] = fmaf(ph, vb, acc[h][1]);
+        }
+      }
+    }
+    __syncthreads();  // every thread is done with this slot and with pr
     if (tid == 0 && c + 2 < chunks) issue(c + 2);
   }
   if (c < chunks) {  // a copy did not land within the bound
@@ -465,27 +500,36 @@ __global__ void __launch_bounds__(256) attention_cluster(AttnArgs a) {
     }
     __syncthreads();
   }
-  if (vlive) {
+  // sum the four token groups, push each 16-dim slice to its owner rank's inbox
 #pragma unroll
-    for (int j = 0; j < HPT; ++j) accsm[half * HPT + j][d] = acc[j];
+  for (int h = 0; h < REP; ++h) *reinterpret_cast<float2*>(&red[tg][h][2 * dp]) = make_float2(acc[h][0], acc[h][1]);
+  __syncthreads();
+  for (int item = tid; item < REP * kHeadDim; item += 256) {
+    const int h = item / kHeadDim, d = item - h * kHeadDim;
+    const float o = (red[0][h][d] + red[1][h][d]) + (red[2][h][d] + red[3][h][d]);
+    *cluster.map_shared_rank(&inbox[rank][h][d & 15], d >> 4) = o;
   }
-  cluster.sync();
-  if (rank == 0) {
-    for (int item = tid; item < REP * kHeadDim; item += 256) {
-      const int h = item / kHeadDim, dd = item - h * kHeadDim;
-      float M = -INFINITY;
-      for (int r = 0; r < kClusterCtas; ++r) M = fmaxf(M, *cluster.map_shared_rank(&m_run[h], r));
-      float S = 0.f, O = 0.f;
-      for (int r = 0; r < kClusterCtas; ++r) {
-        const float mr = *cluster.map_shared_rank(&m_run[h], r);
-        const float w = mr == -INFINITY ? 0.f : expf(mr - M);
-        S = fmaf(w, *cluster.map_shared_rank(&l_run[h], r), S);
-        O = fmaf(w, *cluster.map_shared_rank(&accsm[h][dd], r), O);
-      }
-      a.out[(size_t)b * a.nq * kHeadDim + (kh * REP + h) * kHeadDim + dd] = to_bf16(O / S);
+  if (tid < REP * kClusterCtas) {
+    const int h = tid % REP, dst = tid / REP;
+    *cluster.map_shared_rank(&minbox[rank][h], dst) = m_run[h];
+    *cluster.map_shared_rank(&linbox[rank][h], dst) = l_run[h];
+  }
+  cluster.sync();  // publishes every push; afterwards only local shared memory is read
+  if (tid < REP * 16) {
+    const int h = tid >> 4, dd = tid & 15;
+    float M = -INFINITY;
+#pragma unroll
+    for (int r = 0; r < kClusterCtas; ++r) M = fmaxf(M, minbox[r][h]);
+    float S = 0.f, O = 0.f;
+#pragma unroll
+    for (int r = 0; r < kClusterCtas; ++r) {
+      const float mr = minbox[r][h];
+      const float w = mr == -INFINITY ? 0.f : expf(mr - M);
+      S = fmaf(w, linbox[r][h], S);
+      O = fmaf(w, inbox[r][h][dd], O);
     }
+    a.out[(size_t)b * a.nq * kHeadDim + (kh * REP + h) * kHeadDim + 16 * rank + dd] = to_bf16(O / S);
   }
-  cluster.sync();  // peers keep their shared memory until rank 0 has read it
 }
 
 static cudaError_t launch_cluster_attention(const AttnArgs& a, int batch, int rep, cudaStream_t s, int flags) {
