@@ -119,6 +119,7 @@ struct StreamArgs {
   int* tickets;   // [CTA boundary], zero between launches
   int n, k, zeros;
   int tile_aligned;  // CTA ranges on whole tiles (no tile shared between CTAs)
+  int pre_issue;     // stages copied before the dependency wait (the rest right after it)
   float eps;
 };
 
@@ -197,6 +198,11 @@ constexpr int kWarps = 16;  // consumer warps per CTA
 
 // NS ring stages of kWarps * BPW slice blocks; consumer warp w takes blocks w + 16 m
 // (m < BPW) of every stage, which share one slice when S divides 16.
+#ifndef MT_PREFETCH_ACT
+#define MT_PREFETCH_ACT 1
+#endif
+__device__ __forceinline__ bool prefetch_act() { return MT_PREFETCH_ACT; }
+
 template <int NS, int BPW, bool NORM, bool ADD, bool PAIRED>
 __global__ void __launch_bounds__(kWarps * 32 + 32, 1) w4a16_packed(StreamArgs a, int max_tiles) {
   extern __shared__ __align__(128) uint8_t smem[];
@@ -250,7 +256,7 @@ __global__ void __launch_bounds__(kWarps * 32 + 32, 1) w4a16_packed(StreamArgs a
     failed = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     // weights never depend on the previous kernel: start streaming before the PDL wait
-    for (int st = 0; st < NS && st < stages; ++st) issue(st);
+    for (int st = 0; st < a.pre_issue && st < NS && st < stages; ++st) issue(st);
   }
   if (tid < 4) zero16[tid] = make_uint4(0, 0, 0, 0);
   for (int i = tid; i < kWarps * max_tiles * 16; i += blockDim.x) partial[i] = 0.f;
@@ -259,6 +265,10 @@ __global__ void __launch_bounds__(kWarps * 32 + 32, 1) w4a16_packed(StreamArgs a
   if (warp == kWarps) {  // producer warp
     pdl_trigger();
     if (lane == 0) {
+      if (a.pre_issue < NS) {
+        pdl_wait();
+        for (int st = a.pre_issue; st < NS && st < stages; ++st) issue(st);
+      }
       int st = NS;
       for (; st < stages; ++st) {
         const int slot = st % NS;
@@ -282,6 +292,18 @@ __global__ void __launch_bounds__(kWarps * 32 + 32, 1) w4a16_packed(StreamArgs a
 #pragma unroll
     for (int j = 0; j < 4; ++j)
       if (j < wpt && tid + j * consumers < K / 8) nwv[j] = reinterpret_cast<const uint4*>(a.norm_w)[tid + j * consumers];
+  }
+  // Warm the activation's address translation and L2 lines before the wait (a prefetch is
+  // not a read of the data: the loads after the wait see the previous kernel's writes).
+  if (prefetch_act() && (lane & 7) == 0) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int word = tid + j * consumers;
+      if (j < wpt && word < K / 8) {
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(reinterpret_cast<const uint4*>(a.x) + word));
+        if (ADD) asm volatile("prefetch.global.L2 [%0];" ::"l"(reinterpret_cast<const uint4*>(a.residual) + word));
+      }
+    }
   }
   pdl_wait();
   pdl_trigger();
@@ -529,6 +551,16 @@ static int split_mode() {
   return m;
 }
 
+// MT_W4_PREISSUE = stages copied before the dependency wait (0..9, default all).
+static int pre_issue_stages() {
+  static int m = -1;
+  if (m < 0) {
+    const char* e = getenv("MT_W4_PREISSUE");
+    m = (e && e[0] >= '0' && e[0] <= '9' && e[1] == 0) ? e[0] - '0' : 9;
+  }
+  return m;
+}
+
 template <int NS, int BPW, bool NORM, bool ADD, bool PAIRED>
 static cudaError_t go(StreamArgs a, cudaStream_t s, int flags) {
   const PackGeom pg(a.n, a.k, a.zeros != 0, PAIRED);
@@ -539,6 +571,7 @@ static cudaError_t go(StreamArgs a, cudaStream_t s, int flags) {
   const long long max_blocks = a.tile_aligned ? (long long)((pg.tiles + grid - 1) / grid) * pg.slices
                                               : (pg.blocks + grid - 1) / grid;
   const int max_tiles = (int)((max_blocks + pg.slices - 1) / pg.slices) + 1;
+  a.pre_issue = pre_issue_stages();
   const size_t smem = packed_smem(NS, BPW, a.k, a.zeros != 0, max_tiles);
   if (smem > 227 * 1024) return cudaErrorInvalidValue;
   return launch(w4a16_packed<NS, BPW, NORM, ADD, PAIRED>, dim3(grid), dim3(kWarps * 32 + 32), smem, s, flags, a,
