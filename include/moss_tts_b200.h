@@ -107,6 +107,35 @@ int mt_w4a16_linear_packed(const void* x, const void* residual, const void* norm
                            int mode, void* workspace, int flags, void* stream);
 
 /*
+ * Tensor-parallel exchange over peer memory (NVLink), replacing the NCCL all-reduce after a
+ * row-parallel projection for mt_w4a16_linear_packed_tp. Every rank owns a receive area of
+ * [slots][world][slot_elems / 2] 8-byte cells {bf16 pair, uint32 flag}, mapped on every rank
+ * (the caller's symmetric allocation); `recv` lists the areas by rank. Each cell is written
+ * with one 8-byte store, which is single-copy atomic, so a reader that sees this step's flag
+ * sees this step's data: no fences, counters or atomics.
+ *   out_slot >= 0: the producer writes its output rows into recv[r][out_slot][rank] of every
+ *                  rank r (flag = low 32 bits of *epoch) -- plain stores, no TMA multicast;
+ *   in_slot >= 0:  the consumer polls its recv[rank][in_slot][r] cells until every flag equals
+ *                  *epoch (bounded), and uses x = bf16(sum over ranks r in order) in place of `x`.
+ * `epoch` is the caller's device step counter, incremented once per step on every rank before
+ * the step's first exchange. No reference counterpart: the reference is single-GPU; this is
+ * the all-reduce of its tensor-parallel row (SURVEY's TP row).
+ */
+#define MT_TP_MAX_RANKS 8
+typedef struct mt_tp_exchange {
+  void* recv[MT_TP_MAX_RANKS];
+  const long long* epoch;
+  int world, rank;
+  int in_slot, out_slot, slot_elems;
+} mt_tp_exchange;
+
+/* mt_w4a16_linear_packed with the peer-memory exchange `tp` (see mt_tp_exchange). */
+int mt_w4a16_linear_packed_tp(const void* x, const void* residual, const void* norm_w, float eps,
+                              void* summed, const void* packed, int has_zeros, void* y, int n, int k,
+                              int mode, void* workspace, const mt_tp_exchange* tp, int flags,
+                              void* stream);
+
+/*
  * bf16-weight decode GEMV with the same modes as mt_w4a16_linear (w bf16 [n, k]).
  * Replaces linear_decode (src/moss_tts/_runtime/kernels.py:93-108) and the paired gate/up
  * SiLU GEMV fp8_silu_decode (src/moss_tts/_runtime/fused_mlp.py:7-30).

@@ -121,6 +121,11 @@ struct StreamArgs {
   int tile_aligned;  // CTA ranges on whole tiles (no tile shared between CTAs)
   int pre_issue;     // stages copied before the dependency wait (the rest right after it)
   float eps;
+  // tensor-parallel exchange over peer memory (mt_tp_exchange), 8-byte cells {bf16 pair, flag}
+  const uint2* tp_in;           // this rank's [world][k / 2] cells of the input slot, or null
+  const long long* tp_epoch;    // device step counter: this step's flag
+  int tp_world;
+  uint2* tp_out[MT_TP_MAX_RANKS];  // rank r's [n_out / 2] cells for this rank's output, or null
 };
 
 // Codes as fp16 subnormals: (w & 0x000F000F) is the fp16 pair (q_j, q_{j+4}) * 2^-24 and
@@ -295,7 +300,7 @@ __global__ void __launch_bounds__(kWarps * 32 + 32, 1) w4a16_packed(StreamArgs a
   }
   // Warm the activation's address translation and L2 lines before the wait (a prefetch is
   // not a read of the data: the loads after the wait see the previous kernel's writes).
-  if (prefetch_act() && (lane & 7) == 0) {
+  if (prefetch_act() && !a.tp_in && (lane & 7) == 0) {
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const int word = tid + j * consumers;
@@ -307,6 +312,7 @@ __global__ void __launch_bounds__(kWarps * 32 + 32, 1) w4a16_packed(StreamArgs a
   }
   pdl_wait();
   pdl_trigger();
+  const uint32_t tp_flag = a.tp_epoch ? (uint32_t)*a.tp_epoch : 0u;
   const uint4* xsrc = reinterpret_cast<const uint4*>(a.x);
   const uint4* rsrc = reinterpret_cast<const uint4*>(a.residual);
   float v[4][8];
@@ -315,7 +321,36 @@ __global__ void __launch_bounds__(kWarps * 32 + 32, 1) w4a16_packed(StreamArgs a
   for (int j = 0; j < 4; ++j) {
     const int word = tid + j * consumers;
     if (j >= wpt || word >= K / 8) continue;
-    const uint4 xw = xsrc[word];
+    uint4 xw;
+    if (a.tp_in) {  // x = bf16(sum over ranks), ranks in order, fp32 sum; cells polled (bounded)
+      float acc8[8] = {};
+      for (int r = 0; r < a.tp_world; ++r) {
+        const uint2* cell = a.tp_in + (size_t)r * (K / 2) + (size_t)word * 4;
+        uint32_t pa[4];
+        bool fresh = false;
+        for (long it = 0; it < kSpinLimit && !fresh; ++it) {
+          uint32_t c0[4], c1[4];
+          asm volatile("ld.relaxed.sys.global.v4.u32 {%0, %1, %2, %3}, [%4];"
+                       : "=r"(c0[0]), "=r"(c0[1]), "=r"(c0[2]), "=r"(c0[3]) : "l"(cell) : "memory");
+          asm volatile("ld.relaxed.sys.global.v4.u32 {%0, %1, %2, %3}, [%4];"
+                       : "=r"(c1[0]), "=r"(c1[1]), "=r"(c1[2]), "=r"(c1[3]) : "l"(cell + 2) : "memory");
+          pa[0] = c0[0]; pa[1] = c0[2]; pa[2] = c1[0]; pa[3] = c1[2];
+          fresh = c0[1] == tp_flag && c0[3] == tp_flag && c1[1] == tp_flag && c1[3] == tp_flag;
+        }
+        if (!fresh) atomicExch(&g_error_word, 2);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) { acc8[2 * i] += bf16_lo(pa[i]); acc8[2 * i + 1] += bf16_hi(pa[i]); }
+      }
+      uint32_t o4[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        __nv_bfloat162 pr2 = __floats2bfloat162_rn(acc8[2 * i], acc8[2 * i + 1]);
+        o4[i] = *reinterpret_cast<uint32_t*>(&pr2);
+      }
+      xw = make_uint4(o4[0], o4[1], o4[2], o4[3]);
+    } else {
+      xw = xsrc[word];
+    }
     const uint32_t xa[4] = {xw.x, xw.y, xw.z, xw.w};
 #pragma unroll
     for (int i = 0; i < 4; ++i) { v[j][2 * i] = bf16_lo(xa[i]); v[j][2 * i + 1] = bf16_hi(xa[i]); }
@@ -484,11 +519,28 @@ __global__ void __launch_bounds__(kWarps * 32 + 32, 1) w4a16_packed(StreamArgs a
   }
   named_sync(1, consumers);
   // tiles wholly inside this CTA's range
+  __nv_bfloat16* ystage = reinterpret_cast<__nv_bfloat16*>(partial + (size_t)kWarps * max_tiles * 16);
   for (int i = tid; i < ntiles * RT; i += consumers) {
     const int lt = i / RT, tr = i - lt * RT, tq = t_first + lt;
     if (tq * S < b0 || (tq + 1) * S > b1) continue;
     const int o = tq * RT + tr;
-    if (o < n_out) a.y[o] = to_bf16(finish_row<PAIRED>(partial[lt * 16 + tr], partial[lt * 16 + 8 + tr]));
+    if (o < n_out) {
+      const __nv_bfloat16 yv = to_bf16(finish_row<PAIRED>(partial[lt * 16 + tr], partial[lt * 16 + 8 + tr]));
+      a.y[o] = yv;
+      ystage[i] = yv;
+    }
+  }
+  if (a.tp_out[0]) {
+    // Push this CTA's rows (whole tiles) to every rank's receive area over NVLink: one 8-byte
+    // store {bf16 pair, this step's flag} per row pair and rank.
+    named_sync(1, consumers);
+    const int o0 = t_first * RT, rows = min(ntiles * RT, n_out - o0);
+    for (int i = tid; i < rows / 2; i += consumers) {
+      const uint32_t pair = reinterpret_cast<const uint32_t*>(ystage)[i];
+      for (int r = 0; r < a.tp_world; ++r)
+        asm volatile("st.relaxed.sys.global.v2.u32 [%0], {%1, %2};" ::"l"(a.tp_out[r] + o0 / 2 + i), "r"(pair),
+                     "r"(tp_flag) : "memory");
+    }
   }
   // Tiles shared with a neighbouring CTA. Every range holds at least S blocks, so only the
   // first tile can miss its head (shared with CTA - 1, boundary slot CTA - 1) and only the
@@ -536,7 +588,7 @@ __global__ void __launch_bounds__(kWarps * 32 + 32, 1) w4a16_packed(StreamArgs a
 static size_t packed_smem(int ns, int bpw, int k, bool zeros, int max_tiles) {
   const int block_b = kCodeBytes + kScaleBytes + (zeros ? kZeroBytes : 0);
   return (size_t)ns * kWarps * bpw * block_b + (size_t)k / 8 * 16 + (size_t)k / 32 * 4 +
-         (size_t)kWarps * max_tiles * 16 * 4;
+         (size_t)kWarps * max_tiles * 16 * 4 + (size_t)max_tiles * 16 * 2;  // + staged output rows
 }
 
 // MT_W4_SPLIT = 1 forces split-K ranges, 2 whole-tile ranges (default: whole tiles when
@@ -567,7 +619,7 @@ static cudaError_t go(StreamArgs a, cudaStream_t s, int flags) {
   int grid = sm_count();
   if (grid > pg.tiles) grid = pg.tiles;  // >= one tile of blocks per CTA: a tile spans at most two CTAs
   if (grid > PackGeom::kMaxCtas) grid = PackGeom::kMaxCtas;
-  a.tile_aligned = split_mode() == 2 || (split_mode() == 0 && pg.tiles >= sm_count());
+  a.tile_aligned = split_mode() == 2 || (split_mode() == 0 && pg.tiles >= sm_count()) || a.tp_out[0] != nullptr;
   const long long max_blocks = a.tile_aligned ? (long long)((pg.tiles + grid - 1) / grid) * pg.slices
                                               : (pg.blocks + grid - 1) / grid;
   const int max_tiles = (int)((max_blocks + pg.slices - 1) / pg.slices) + 1;
@@ -631,16 +683,18 @@ MT_API int mt_w4a16_pack(const void* qweight, const void* scales, const void* qz
   return (int)cudaGetLastError();
 }
 
-MT_API int mt_w4a16_linear_packed(const void* x, const void* residual, const void* norm_w, float eps, void* summed,
-                                  const void* packed, int has_zeros, void* y, int n, int k, int mode,
-                                  void* workspace, int flags, void* stream) {
-  if (!x || !packed || !y || !workspace || !packed_shape_ok(n, k, mode)) return kBadArgument;
+static int linear_packed(const void* x, const void* residual, const void* norm_w, float eps, void* summed,
+                         const void* packed, int has_zeros, void* y, int n, int k, int mode, void* workspace,
+                         const mt_tp_exchange* tp, int flags, void* stream) {
+  if (!packed || !y || !workspace || !packed_shape_ok(n, k, mode)) return kBadArgument;
   if ((mode & 2) && (!(mode & 1) || !residual)) return kBadArgument;
   if ((mode & 1) && !norm_w) return kBadArgument;
-  if (!aligned(x, 16) || !aligned(packed, 16) || !aligned(workspace, 16) || (residual && !aligned(residual, 16)) ||
+  const bool tp_in = tp && tp->in_slot >= 0, tp_out = tp && tp->out_slot >= 0;
+  if (!tp_in && !x) return kBadArgument;
+  if ((x && !aligned(x, 16)) || !aligned(packed, 16) || !aligned(workspace, 16) || (residual && !aligned(residual, 16)) ||
       (summed && !aligned(summed, 16)) || (norm_w && !aligned(norm_w, 16)))
     return kBadArgument;
-  StreamArgs a;
+  StreamArgs a = {};
   a.x = (const __nv_bfloat16*)x;
   a.residual = (const __nv_bfloat16*)residual;
   a.norm_w = (const __nv_bfloat16*)norm_w;
@@ -653,12 +707,48 @@ MT_API int mt_w4a16_linear_packed(const void* x, const void* residual, const voi
   a.k = k;
   a.zeros = has_zeros ? 1 : 0;
   a.eps = eps;
+  if (tp) {
+    const int w = tp->world, r = tp->rank, n_out = (mode & 4) ? n / 2 : n;
+    if (w < 1 || w > MT_TP_MAX_RANKS || r < 0 || r >= w || tp->slot_elems < 16 || tp->slot_elems % 16 || !tp->epoch)
+      return kBadArgument;
+    a.tp_world = w;
+    a.tp_epoch = tp->epoch;
+    const size_t cells = (size_t)tp->slot_elems / 2;  // cells of one (slot, source rank) row
+    if (tp_in) {
+      if (tp->slot_elems != k || !tp->recv[r] || !aligned(tp->recv[r], 16)) return kBadArgument;
+      a.tp_in = (const uint2*)tp->recv[r] + (size_t)tp->in_slot * w * cells;
+    }
+    if (tp_out) {
+      if (tp->slot_elems != n_out) return kBadArgument;
+      for (int q = 0; q < w; ++q) {
+        if (!tp->recv[q] || !aligned(tp->recv[q], 16)) return kBadArgument;
+        a.tp_out[q] = (uint2*)tp->recv[q] + ((size_t)tp->out_slot * w + r) * cells;
+      }
+    }
+  }
   cudaStream_t s = (cudaStream_t)stream;
   flags &= kFlagPdl;
   const bool paired = mode & 4;
   if (mode & 2) return (int)(paired ? go_ns<true, true, true>(a, s, flags) : go_ns<true, true, false>(a, s, flags));
   if (mode & 1) return (int)(paired ? go_ns<true, false, true>(a, s, flags) : go_ns<true, false, false>(a, s, flags));
   return (int)(paired ? go_ns<false, false, true>(a, s, flags) : go_ns<false, false, false>(a, s, flags));
+}
+
+MT_API int mt_w4a16_linear_packed(const void* x, const void* residual, const void* norm_w, float eps, void* summed,
+                                  const void* packed, int has_zeros, void* y, int n, int k, int mode,
+                                  void* workspace, int flags, void* stream) {
+  if (!x) return kBadArgument;
+  return linear_packed(x, residual, norm_w, eps, summed, packed, has_zeros, y, n, k, mode, workspace, nullptr,
+                       flags, stream);
+}
+
+MT_API int mt_w4a16_linear_packed_tp(const void* x, const void* residual, const void* norm_w, float eps,
+                                     void* summed, const void* packed, int has_zeros, void* y, int n, int k,
+                                     int mode, void* workspace, const mt_tp_exchange* tp, int flags,
+                                     void* stream) {
+  if (!tp) return kBadArgument;
+  return linear_packed(x, residual, norm_w, eps, summed, packed, has_zeros, y, n, k, mode, workspace, tp, flags,
+                       stream);
 }
 
 // Diagnostic read of the library's error word on the current device (1 after a kernel

@@ -18,6 +18,9 @@ KV heads, intermediate columns and codebooks; partial o_proj/down outputs are su
 NCCL all-reduce, and each rank writes only its own codebooks' ids (zeros elsewhere), summed
 by one int64 all-reduce.
 """
+import ctypes
+import os
+
 import torch
 
 from . import native
@@ -47,6 +50,37 @@ class TensorParallel:
         if self.world > 1:
             import torch.distributed as dist
             dist.all_reduce(t, group=self.group)
+
+
+class PeerExchange:
+    """Peer-memory exchange of the row-parallel projections' partial rows (``mt_tp_exchange``).
+
+    One symmetric allocation per rank (``torch.distributed._symmetric_memory``, mapped on every
+    rank of the group) of 8-byte cells ``[slots][world][width / 2]``, each {bf16 pair, uint32
+    flag}. The producer GEMV writes its rows into every rank's cells with this step's flag;
+    the consumer GEMV polls its own cells for the flag and sums the ranks' rows.
+    """
+
+    def __init__(self, tp: TensorParallel, slots: int, width: int, device):
+        import torch.distributed as dist
+        import torch.distributed._symmetric_memory as symm_mem
+
+        self.world, self.rank, self.slots, self.width = tp.world, tp.rank, slots, width
+        self.buf = symm_mem.empty(slots * tp.world * width * 4, dtype=torch.uint8, device=device)
+        self.buf.zero_()
+        self.handle = symm_mem.rendezvous(self.buf, tp.group or dist.group.WORLD)
+        self.ptrs = [int(p) for p in self.handle.buffer_ptrs]
+        self.epoch = torch.zeros(1, device=device, dtype=torch.long)  # steps started on this rank
+        torch.cuda.synchronize(device)
+        dist.barrier(group=tp.group)
+
+    def desc(self, in_slot: int = -1, out_slot: int = -1) -> "native.TpExchange":
+        d = native.TpExchange()
+        for r, p in enumerate(self.ptrs):
+            d.recv[r] = p
+        d.epoch = self.epoch.data_ptr()
+        d.world, d.rank, d.in_slot, d.out_slot, d.slot_elems = self.world, self.rank, in_slot, out_slot, self.width
+        return d
 
 
 def shard_weights(w: DecoderWeights, rank: int, world: int) -> DecoderWeights:
@@ -148,18 +182,29 @@ class DecodeEngine:
                     ws = max(ws, native.w4a16_packed_size(p.n, p.k, p.qzeros is not None,
                                                           native.LINEAR_PAIRED if paired else 0)[1])
         self.w4_workspace = torch.zeros(max(ws, 16), device=dev, dtype=torch.uint8)
+        # Tensor parallelism: the row-parallel partials travel through peer memory (o_proj and
+        # every down but the last; that one feeds the heads through an NCCL all-reduce).
+        self.exchange = None
+        if world > 1 and os.environ.get("MT_TP_EXCHANGE", "p2p") != "nccl" and weights.layers[0].out.quantized \
+                and all(self._packed_ok(p, False) for lw in weights.layers for p in (lw.out, lw.down)):
+            self.exchange = PeerExchange(self.tp, 2 * len(weights.layers), h, dev)
 
     # ------------------------------------------------------------------ kernels
     @staticmethod
     def _packed_ok(p: Projection, paired: bool) -> bool:
         return p.quantized and p.k % 256 == 0 and 256 <= p.k <= 16384 and (not paired or p.n % 2 == 0)
 
-    def _linear(self, p: Projection, x, y, *, residual=None, norm=None, summed=None, paired=False):
+    def _linear(self, p: Projection, x, y, *, residual=None, norm=None, summed=None, paired=False, tp=None):
         mode = (native.LINEAR_NORM if norm is not None else 0) | (native.LINEAR_ADD if residual is not None else 0)
         mode |= native.LINEAR_PAIRED if paired else 0
         eps = float(self.cfg.rms_norm_eps)
         s = torch.cuda.current_stream(self.device).cuda_stream
-        if self._packed_ok(p, paired):
+        if tp is not None:
+            native.call("mt_w4a16_linear_packed_tp", x.data_ptr(), native.ptr(residual), native.ptr(norm), eps,
+                        native.ptr(summed), p.packed_tiles(paired).data_ptr(), 1 if p.qzeros is not None else 0,
+                        y.data_ptr(), p.n, p.k, mode, self.w4_workspace.data_ptr(), ctypes.byref(tp),
+                        self.flags, s)
+        elif self._packed_ok(p, paired):
             native.call("mt_w4a16_linear_packed", x.data_ptr(), native.ptr(residual), native.ptr(norm), eps,
                         native.ptr(summed), p.packed_tiles(paired).data_ptr(), 1 if p.qzeros is not None else 0,
                         y.data_ptr(), p.n, p.k, mode, self.w4_workspace.data_ptr(), self.flags, s)
@@ -182,12 +227,16 @@ class DecodeEngine:
         res = self.emb
         nxt = 0
         eps = float(cfg.rms_norm_eps)
+        ex, last = self.exchange, len(w.layers) - 1
+        if ex is not None:
+            ex.epoch.add_(1)  # one step: every exchange slot is expected once more
         for i, lw in enumerate(w.layers):
             if i == 0:
                 self._linear(lw.qkv, self.emb, self.qkv, norm=lw.input_norm)
             else:
                 out = self.res[nxt]
-                self._linear(lw.qkv, self.mlp, self.qkv, residual=res, norm=lw.input_norm, summed=out)
+                tp_in = ex.desc(in_slot=2 * (i - 1) + 1) if ex is not None else None
+                self._linear(lw.qkv, self.mlp, self.qkv, residual=res, norm=lw.input_norm, summed=out, tp=tp_in)
                 res, nxt = out, 1 - nxt
             k, v = self.kv[i, 0], self.kv[i, 1]
             native.call("mt_attention_decode", self.qkv.data_ptr(), lw.q_norm.data_ptr(), lw.k_norm.data_ptr(),
@@ -195,13 +244,21 @@ class DecodeEngine:
                         v.data_ptr(), self.attn.data_ptr(), self.partial.data_ptr(), self.lse.data_ptr(),
                         self.tickets.data_ptr(), 1, self.nq, self.nkv, self.max_length, self.splits, eps,
                         self.status.data_ptr(), self.flags, s)
-            self._linear(lw.out, self.attn, self.proj)
-            self.tp.all_reduce(self.proj)
+            if ex is not None:
+                self._linear(lw.out, self.attn, self.proj, tp=ex.desc(out_slot=2 * i))
+            else:
+                self._linear(lw.out, self.attn, self.proj)
+                self.tp.all_reduce(self.proj)
             out = self.res[nxt]
-            self._linear(lw.gate_up, self.proj, self.mid, residual=res, norm=lw.post_norm, summed=out, paired=True)
+            tp_in = ex.desc(in_slot=2 * i) if ex is not None else None
+            self._linear(lw.gate_up, self.proj, self.mid, residual=res, norm=lw.post_norm, summed=out, paired=True,
+                         tp=tp_in)
             res, nxt = out, 1 - nxt
-            self._linear(lw.down, self.mid, self.mlp)
-            self.tp.all_reduce(self.mlp)
+            if ex is not None and i < last:
+                self._linear(lw.down, self.mid, self.mlp, tp=ex.desc(out_slot=2 * i + 1))
+            else:
+                self._linear(lw.down, self.mid, self.mlp)
+                self.tp.all_reduce(self.mlp)
         native.call("mt_heads_greedy", self.mlp.data_ptr(), res.data_ptr(), w.final_norm.data_ptr(), eps,
                     self.hidden.data_ptr(), w.head_text_rows.data_ptr(), w.head_audio.data_ptr(),
                     self.text_logits.data_ptr(), self.audio_logits.data_ptr(), self.text_ids.data_ptr(),

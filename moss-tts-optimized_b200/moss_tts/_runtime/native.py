@@ -28,6 +28,7 @@ SIGNATURES = {
     "mt_w4a16_packed_size": ([_I, _I, _I, _I, _LLP, _LLP], _I),
     "mt_w4a16_pack": ([_P, _P, _P, _I, _I, _I, _P, _P], _I),
     "mt_w4a16_linear_packed": ([_P, _P, _P, _F, _P, _P, _I, _P, _I, _I, _I, _P, _I, _P], _I),
+    "mt_w4a16_linear_packed_tp": ([_P, _P, _P, _F, _P, _P, _I, _P, _I, _I, _I, _P, _P, _I, _P], _I),
     "mt_bf16_linear": ([_P, _P, _P, _F, _P, _P, _P, _I, _I, _I, _I, _I, _P], _I),
     "mt_rmsnorm": ([_P, _P, _P, _P, _P, _I, _I, _F, _I, _P], _I),
     "mt_silu_mul": ([_P, _P, _I, _I, _I, _P], _I),
@@ -37,6 +38,16 @@ SIGNATURES = {
     "mt_attention_decode_noalloc": ([_P] * 9 + [_I] * 5 + [_F, _P, _I, _P], _I),
     "mt_heads_greedy": ([_P, _P, _P, _F] + [_P] * 11 + [_I] * 11 + [_P], _I),
 }
+
+
+TP_MAX_RANKS = 8
+
+
+class TpExchange(ctypes.Structure):
+    """``mt_tp_exchange`` of include/moss_tts_b200.h."""
+    _fields_ = [("recv", ctypes.c_void_p * TP_MAX_RANKS), ("epoch", ctypes.c_void_p),
+                ("world", ctypes.c_int), ("rank", ctypes.c_int), ("in_slot", ctypes.c_int),
+                ("out_slot", ctypes.c_int), ("slot_elems", ctypes.c_int)]
 
 
 class NativeLibraryError(RuntimeError):

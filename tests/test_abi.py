@@ -26,6 +26,8 @@ def header_prototypes():
                 kinds.append("ip")
             elif a.startswith("long long*"):
                 kinds.append("llp")
+            elif a.startswith("const mt_tp_exchange*"):
+                kinds.append("p")
             elif "*" in a:
                 kinds.append("p")
             elif a.startswith("float"):
