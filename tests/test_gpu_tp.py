@@ -1,6 +1,6 @@
-"""Tensor parallelism on real GPUs: TP=2 decode steps against the unsharded model.
+"""Tensor parallelism on real GPUs: TP=2/4/8 decode steps against the unsharded model.
 
-Skipped unless at least two GPUs are visible. The worker (tests/tp_worker.py) runs under
+Each world size is skipped unless that many GPUs are visible. The worker (tests/tp_worker.py) runs under
 torchrun with one rank per GPU; NCCL all-reduces after o_proj and down are captured in the
 decode graph. Hidden states must agree within max-abs 5e-2 + 2e-2 |ref| (bf16 partial sums
 reduced in a different order); greedy ids may differ only at near-ties, so at least 97% of
@@ -19,11 +19,14 @@ from conftest import REPO
 pytestmark = pytest.mark.gpu
 
 
-@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_tp2_decode_matches_single_gpu(tmp_path):
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_tp_decode_matches_single_gpu(tmp_path, world):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     out = tmp_path / "tp.json"
-    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node=2",
-           "--master-addr=127.0.0.1", "--master-port=29631", str(REPO / "tests" / "tp_worker.py"), str(out)]
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={world}",
+           "--master-addr=127.0.0.1", f"--master-port={29631 + world}", str(REPO / "tests" / "tp_worker.py"),
+           str(out)]
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
     r = subprocess.run(["timeout", "-k", "30", "300"] + cmd, env=env, capture_output=True, text=True)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
