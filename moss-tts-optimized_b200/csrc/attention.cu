@@ -286,14 +286,16 @@ __global__ void __launch_bounds__(128) attention_decode(AttnArgs a) {
 // one cluster barrier publishes them, and every rank finishes its 16 dims locally.
 constexpr int kClusterCtas = 8;
 constexpr int kChunk = 128;
+constexpr int kAttnThreads = 256;               // 8 warps per CTA (16 measured no faster)
+constexpr int kTokenGroups = kAttnThreads / 64;  // P.V token groups of 64 dim-pair threads
 
 template <int REP>
-__global__ void __launch_bounds__(256) attention_cluster(AttnArgs a) {
+__global__ void __launch_bounds__(kAttnThreads) attention_cluster(AttnArgs a) {
   extern __shared__ __align__(128) uint8_t sm[];  // 2 slots x {K[kChunk][128], V[kChunk][128]} bf16
   constexpr int kQStride = 36;                     // floats per 32-dim quarter of q (+4 pad)
   __shared__ __align__(16) float qs[REP * 4 * kQStride];
   __shared__ __align__(16) float pr[kChunk][REP];  // logits, then probabilities
-  __shared__ __align__(16) float red[4][REP][kHeadDim];
+  __shared__ __align__(16) float red[kTokenGroups][REP][kHeadDim];
   __shared__ __align__(16) float inbox[kClusterCtas][REP][16];
   __shared__ float minbox[kClusterCtas][REP], linbox[kClusterCtas][REP];
   __shared__ float m_run[REP], l_run[REP], scale[REP];
@@ -420,7 +422,7 @@ __global__ void __launch_bounds__(256) attention_cluster(AttnArgs a) {
     __syncthreads();
     // logits: item = ((t * REP) + h) * 4 + quarter; four consecutive lanes share (t, h)
     const int items = rows * REP * 4;
-    for (int base = 0; base < items; base += 256) {
+    for (int base = 0; base < items; base += kAttnThreads) {
       const int item = base + tid;
       const int qt = item & 3, h = (item >> 2) % REP, t = (item >> 2) / REP;
       float d0 = 0.f, d1 = 0.f;
@@ -478,7 +480,7 @@ __global__ void __launch_bounds__(256) attention_cluster(AttnArgs a) {
       for (int h = 0; h < REP; ++h) { acc[h][0] *= scl[h]; acc[h][1] *= scl[h]; }
       const uint32_t* v2 = reinterpret_cast<const uint32_t*>(vs) + dp;
 #pragma unroll 4
-      for (int t = tg; t < rows; t += 4) {
+      for (int t = tg; t < rows; t += kTokenGroups) {
         const uint32_t vv = v2[(size_t)t * (kHeadDim / 2)];
         const float va = bf16_lo(vv), vb = bf16_hi(vv);
 #pragma unroll
@@ -500,13 +502,15 @@ __global__ void __launch_bounds__(256) attention_cluster(AttnArgs a) {
     }
     __syncthreads();
   }
-  // sum the four token groups, push each 16-dim slice to its owner rank's inbox
+  // sum the token groups, push each 16-dim slice to its owner rank's inbox
 #pragma unroll
   for (int h = 0; h < REP; ++h) *reinterpret_cast<float2*>(&red[tg][h][2 * dp]) = make_float2(acc[h][0], acc[h][1]);
   __syncthreads();
-  for (int item = tid; item < REP * kHeadDim; item += 256) {
+  for (int item = tid; item < REP * kHeadDim; item += kAttnThreads) {
     const int h = item / kHeadDim, d = item - h * kHeadDim;
-    const float o = (red[0][h][d] + red[1][h][d]) + (red[2][h][d] + red[3][h][d]);
+    float o = 0.f;
+#pragma unroll
+    for (int g = 0; g < kTokenGroups; ++g) o += red[g][h][d];
     *cluster.map_shared_rank(&inbox[rank][h][d & 15], d >> 4) = o;
   }
   if (tid < REP * kClusterCtas) {
@@ -535,7 +539,7 @@ __global__ void __launch_bounds__(256) attention_cluster(AttnArgs a) {
 static cudaError_t launch_cluster_attention(const AttnArgs& a, int batch, int rep, cudaStream_t s, int flags) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(kClusterCtas * a.nkv, 1, batch);
-  cfg.blockDim = dim3(256);
+  cfg.blockDim = dim3(kAttnThreads);
   cfg.dynamicSmemBytes = 2 * (size_t)kChunk * kHeadDim * 2 * 2;
   cfg.stream = s;
   cudaLaunchAttribute attr[2];

@@ -208,7 +208,9 @@ constexpr int kWarps = 16;  // consumer warps per CTA
 #endif
 __device__ __forceinline__ bool prefetch_act() { return MT_PREFETCH_ACT; }
 
-template <int NS, int BPW, bool NORM, bool ADD, bool PAIRED>
+// TPM: tensor-parallel exchange compiled in (bit 0: input from peer cells, bit 1: output
+// pushed to peer cells); the single-GPU instantiations carry no exchange code.
+template <int NS, int BPW, bool NORM, bool ADD, bool PAIRED, int TPM>
 __global__ void __launch_bounds__(kWarps * 32 + 32, 1) w4a16_packed(StreamArgs a, int max_tiles) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ __align__(8) uint64_t full[NS];
@@ -300,7 +302,7 @@ __global__ void __launch_bounds__(kWarps * 32 + 32, 1) w4a16_packed(StreamArgs a
   }
   // Warm the activation's address translation and L2 lines before the wait (a prefetch is
   // not a read of the data: the loads after the wait see the previous kernel's writes).
-  if (prefetch_act() && !a.tp_in && (lane & 7) == 0) {
+  if (prefetch_act() && !(TPM & 1) && (lane & 7) == 0) {
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const int word = tid + j * consumers;
@@ -312,7 +314,7 @@ __global__ void __launch_bounds__(kWarps * 32 + 32, 1) w4a16_packed(StreamArgs a
   }
   pdl_wait();
   pdl_trigger();
-  const uint32_t tp_flag = a.tp_epoch ? (uint32_t)*a.tp_epoch : 0u;
+  const uint32_t tp_flag = TPM ? (uint32_t)*a.tp_epoch : 0u;
   const uint4* xsrc = reinterpret_cast<const uint4*>(a.x);
   const uint4* rsrc = reinterpret_cast<const uint4*>(a.residual);
   float v[4][8];
@@ -322,7 +324,7 @@ __global__ void __launch_bounds__(kWarps * 32 + 32, 1) w4a16_packed(StreamArgs a
     const int word = tid + j * consumers;
     if (j >= wpt || word >= K / 8) continue;
     uint4 xw;
-    if (a.tp_in) {  // x = bf16(sum over ranks), ranks in order, fp32 sum; cells polled (bounded)
+    if (TPM & 1) {  // x = bf16(sum over ranks), ranks in order, fp32 sum; cells polled (bounded)
       float acc8[8] = {};
       for (int r = 0; r < a.tp_world; ++r) {
         const uint2* cell = a.tp_in + (size_t)r * (K / 2) + (size_t)word * 4;
@@ -527,10 +529,10 @@ __global__ void __launch_bounds__(kWarps * 32 + 32, 1) w4a16_packed(StreamArgs a
     if (o < n_out) {
       const __nv_bfloat16 yv = to_bf16(finish_row<PAIRED>(partial[lt * 16 + tr], partial[lt * 16 + 8 + tr]));
       a.y[o] = yv;
-      ystage[i] = yv;
+      if (TPM & 2) ystage[i] = yv;
     }
   }
-  if (a.tp_out[0]) {
+  if (TPM & 2) {
     // Push this CTA's rows (whole tiles) to every rank's receive area over NVLink: one 8-byte
     // store {bf16 pair, this step's flag} per row pair and rank.
     named_sync(1, consumers);
@@ -613,7 +615,7 @@ static int pre_issue_stages() {
   return m;
 }
 
-template <int NS, int BPW, bool NORM, bool ADD, bool PAIRED>
+template <int NS, int BPW, bool NORM, bool ADD, bool PAIRED, int TPM>
 static cudaError_t go(StreamArgs a, cudaStream_t s, int flags) {
   const PackGeom pg(a.n, a.k, a.zeros != 0, PAIRED);
   int grid = sm_count();
@@ -626,7 +628,7 @@ static cudaError_t go(StreamArgs a, cudaStream_t s, int flags) {
   a.pre_issue = pre_issue_stages();
   const size_t smem = packed_smem(NS, BPW, a.k, a.zeros != 0, max_tiles);
   if (smem > 227 * 1024) return cudaErrorInvalidValue;
-  return launch(w4a16_packed<NS, BPW, NORM, ADD, PAIRED>, dim3(grid), dim3(kWarps * 32 + 32), smem, s, flags, a,
+  return launch(w4a16_packed<NS, BPW, NORM, ADD, PAIRED, TPM>, dim3(grid), dim3(kWarps * 32 + 32), smem, s, flags, a,
                 max_tiles);
 }
 
@@ -641,13 +643,13 @@ static int stream_pipe() {
   return p;
 }
 
-template <bool NORM, bool ADD, bool PAIRED>
+template <bool NORM, bool ADD, bool PAIRED, int TPM = 0>
 static cudaError_t go_ns(const StreamArgs& a, cudaStream_t s, int flags) {
   switch (stream_pipe()) {
-    case 21: return go<2, 1, NORM, ADD, PAIRED>(a, s, flags);
-    case 31: return go<3, 1, NORM, ADD, PAIRED>(a, s, flags);
-    case 41: return go<4, 1, NORM, ADD, PAIRED>(a, s, flags);
-    default: return go<2, 2, NORM, ADD, PAIRED>(a, s, flags);
+    case 21: return go<2, 1, NORM, ADD, PAIRED, TPM>(a, s, flags);
+    case 31: return go<3, 1, NORM, ADD, PAIRED, TPM>(a, s, flags);
+    case 41: return go<4, 1, NORM, ADD, PAIRED, TPM>(a, s, flags);
+    default: return go<2, 2, NORM, ADD, PAIRED, TPM>(a, s, flags);
   }
 }
 
@@ -729,6 +731,16 @@ static int linear_packed(const void* x, const void* residual, const void* norm_w
   cudaStream_t s = (cudaStream_t)stream;
   flags &= kFlagPdl;
   const bool paired = mode & 4;
+  // The exchange variants the tensor-parallel decode step uses: input into the add + norm
+  // projections (q|k|v, gate/up; RMSNorm-only for a first layer), output from plain ones.
+  if (tp_in && tp_out) return kBadArgument;
+  if (tp_in) {
+    if (mode == 3) return (int)go_ns<true, true, false, 1>(a, s, flags);
+    if (mode == 7) return (int)go_ns<true, true, true, 1>(a, s, flags);
+    if (mode == 1) return (int)go_ns<true, false, false, 1>(a, s, flags);
+    return kBadArgument;
+  }
+  if (tp_out) return mode == 0 ? (int)go_ns<false, false, false, 2>(a, s, flags) : kBadArgument;
   if (mode & 2) return (int)(paired ? go_ns<true, true, true>(a, s, flags) : go_ns<true, true, false>(a, s, flags));
   if (mode & 1) return (int)(paired ? go_ns<true, false, true>(a, s, flags) : go_ns<true, false, false>(a, s, flags));
   return (int)(paired ? go_ns<false, false, true>(a, s, flags) : go_ns<false, false, false>(a, s, flags));
