@@ -45,6 +45,7 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--layers", type=int, default=36, help=argparse.SUPPRESS)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-bf16", action="store_true", help="skip the BF16-preset step timing")
     ap.add_argument("--profile-kernel", action="store_true",
                     help="only launch the dominant kernel (packed add+norm+gate/up+SiLU GEMV), once per "
                          "layer per step, for an ncu capture; prints its mean launch time")
@@ -219,6 +220,50 @@ def profile_kernel(args):
                       "bytes_per_launch": gate_up_bytes(cfg.hidden_size, 2 * cfg.intermediate_size)}), flush=True)
 
 
+def bf16_step_rate(args, cfg, dev, rank, world, group, max_length):
+    """Device-resident steps/s of the same decode step with the BF16 preset (config 3 is timed in
+    both formats): random bf16 weights drawn on the device, the same graph replay and timing."""
+    import torch
+    import torch.distributed as dist
+
+    from moss_tts._runtime.engine import DecodeEngine, TensorParallel, shard_weights
+    from moss_tts._runtime.weights import DecoderWeights
+
+    with torch.inference_mode():
+        full = DecoderWeights.random(cfg, dev, seed=1, preset="bf16", full_text_head=False)
+        w = shard_weights(full, rank, world)
+        del full
+        torch.cuda.empty_cache()
+        eng = DecodeEngine(w, max_length=max_length, tp=TensorParallel(rank, world, group))
+        ids0 = torch.full((33,), 17, dtype=torch.long)
+        ids0[0] = cfg.audio_assistant_gen_slot_token_id
+        eng.set_inputs(ids0, PROMPT, 1, -1)
+        eng.capture(advance=True)
+        stream = torch.cuda.current_stream(dev)
+        for _ in range(args.warmup):
+            eng.run(advance=True)
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            eng.run(advance=True)
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        ms = torch.tensor([e0.elapsed_time(e1)], device=dev)
+        if world > 1:
+            dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+        ms = float(ms.item())
+        step_bytes = w.layer_bytes() + w.head_audio.numel() * 2 + 2 * cfg.hidden_size * 2 \
+            + 147456 // world * (PROMPT + args.warmup + args.steps // 2) * args.layers // 36
+        status = int(eng.status.item())
+        eng.graph = eng.graph_advance = None
+        del eng, w
+        torch.cuda.empty_cache()
+    return args.steps / (ms / 1000.0), ms / args.steps, step_bytes, status
+
+
 def main():
     args = parse()
     rank = int(os.environ.get("RANK", "0"))
@@ -341,6 +386,16 @@ def main():
         torch.cuda.synchronize(dev)
         kernel_us = k0.elapsed_time(k1) * 1000 / (reps * len(weights.layers))
         del kgraph
+    # the BF16 preset (config 3 is timed in both formats), after releasing the W4A16 engine's graphs
+    bf16 = None
+    if not args.no_bf16:
+        llm.graph = None
+        eng.graph = eng.graph_advance = None
+        torch.cuda.synchronize(dev)
+        b_val, b_ms, b_bytes, b_status = bf16_step_rate(args, cfg, dev, rank, world, group, max_length)
+        pk, _ = measured_peaks()
+        bf16 = {"value": round(b_val, 3), "unit": UNIT, "ms_per_step": round(b_ms, 4), "status": b_status,
+                "step_bytes_per_gpu": b_bytes, "hbm_roofline_frac": round(b_bytes / (b_ms * 1e-3) / 1e9 / pk, 4)}
     peak, peak_kind = measured_peaks()
     gu_bytes = gate_up_bytes(lw0.k, lw0.n)
     achieved = gu_bytes / (kernel_us * 1e-6) / 1e9
@@ -377,6 +432,7 @@ def main():
                      "frac": round(achieved / peak, 4), "traffic": traffic, "bytes_per_launch": gu_bytes,
                      "launch_us": round(kernel_us, 3)},
         "cpu_baseline": cpu,
+        "bf16": bf16,
         "clocks": clocks.summary(),
         "gpu_launches": launches * args.steps,
         "status": status,
