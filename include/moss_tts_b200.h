@@ -33,7 +33,8 @@ extern "C" {
 #endif
 
 #define MT_FLAG_PDL 1
-#define MT_FLAG_REGISTER_PIPELINE 2 /* alternative kernels: split-K attention, register-pipelined heads */
+#define MT_FLAG_REGISTER_PIPELINE 2 /* alternative kernels: split-K attention, register-pipelined heads
+                                      and bf16 GEMV */
 #define MT_LINEAR_NORM 1   /* RMSNorm prologue over each activation row            */
 #define MT_LINEAR_ADD 2    /* bf16 residual add before the norm (requires NORM)    */
 #define MT_LINEAR_PAIRED 4 /* rows [0,N/2) gate, [N/2,N) up; y = bf16(silu(g)) * u */
@@ -138,7 +139,9 @@ int mt_w4a16_linear_packed_tp(const void* x, const void* residual, const void* n
 /*
  * bf16-weight decode GEMV with the same modes as mt_w4a16_linear (w bf16 [n, k]).
  * Replaces linear_decode (src/moss_tts/_runtime/kernels.py:93-108) and the paired gate/up
- * SiLU GEMV fp8_silu_decode (src/moss_tts/_runtime/fused_mlp.py:7-30).
+ * SiLU GEMV fp8_silu_decode (src/moss_tts/_runtime/fused_mlp.py:7-30). Batch 1 with
+ * k <= 12288 streams the rows through shared memory (one CTA per SM); other batches, and
+ * MT_FLAG_REGISTER_PIPELINE, use the register-pipelined kernel.
  */
 int mt_bf16_linear(const void* x, const void* residual, const void* norm_w, float eps,
                    void* summed, const void* w, void* y, int batch, int n, int k, int mode,

@@ -321,6 +321,18 @@ static cudaError_t bf16_mode(const Bf16Args& a, int mode, cudaStream_t s, int fl
 }
 
 cudaError_t heads_stream_dispatch(const struct HeadsArgs& a, int flags, cudaStream_t s);
+struct Bf16StreamArgs {  // bf16_stream.cu; field order and types match it
+  const __nv_bfloat16* x;
+  const __nv_bfloat16* residual;
+  const __nv_bfloat16* norm_w;
+  __nv_bfloat16* summed;
+  const __nv_bfloat16* w;
+  __nv_bfloat16* y;
+  int n, k;
+  float eps;
+  int unit0, units;
+};
+bool bf16_stream_linear(const Bf16StreamArgs& args, int mode, int flags, cudaStream_t s, cudaError_t* err);
 bool heads_stream_supported(int hidden_size, int n_text, int n_cb, int vocab, int text_owner);
 
 }  // namespace mt
@@ -348,6 +360,22 @@ MT_API int mt_bf16_linear(const void* x, const void* residual, const void* norm_
   if ((size_t)k * 4 > 200 * 1024) return kBadArgument;
   const int n_out = paired ? n / 2 : n;
   cudaStream_t s = (cudaStream_t)stream;
+  if (batch == 1 && !(flags & 2)) {
+    Bf16StreamArgs sa;
+    sa.x = (const __nv_bfloat16*)x;
+    sa.residual = (const __nv_bfloat16*)residual;
+    sa.norm_w = (const __nv_bfloat16*)norm_w;
+    sa.summed = (__nv_bfloat16*)summed;
+    sa.w = (const __nv_bfloat16*)w;
+    sa.y = (__nv_bfloat16*)y;
+    sa.n = n;
+    sa.k = k;
+    sa.eps = eps;
+    sa.unit0 = 0;
+    sa.units = n_out;
+    cudaError_t e = cudaSuccess;
+    if (bf16_stream_linear(sa, mode, flags & kFlagPdl, s, &e)) return (int)e;
+  }
   for (int b0 = 0; b0 < batch; b0 += chunk) {
     Bf16Args a;
     a.x = (const __nv_bfloat16*)x + (size_t)b0 * k;

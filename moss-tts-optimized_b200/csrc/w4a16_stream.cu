@@ -767,6 +767,7 @@ MT_API int mt_w4a16_linear_packed_tp(const void* x, const void* residual, const 
 // abandoned a bounded wait); optionally clears it. Synchronous, unlike every other call.
 namespace mt {
 cudaError_t heads_error_word(int* value, bool clear);
+cudaError_t bf16_error_word(int* value, bool clear);
 }
 
 MT_API int mt_read_error_word(int* value, int clear) {
@@ -777,5 +778,6 @@ MT_API int mt_read_error_word(int* value, int clear) {
     e = cudaMemcpyToSymbol(g_error_word, &zero, sizeof(int));
   }
   if (e == cudaSuccess) e = heads_error_word(value, clear != 0);
+  if (e == cudaSuccess) e = bf16_error_word(value, clear != 0);
   return (int)e;
 }

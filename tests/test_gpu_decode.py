@@ -112,3 +112,35 @@ def test_pinned_host_roundtrip(model):
     out = eng.read_next_ids()
     assert out.device.type == "cpu" and out.is_pinned()
     assert out.shape == (1, 1, 33)
+
+
+def test_bf16_preset_decode_matches_oracle(cuda_device):
+    """The BF16 preset (bf16 projections, streamed bf16 GEMVs) of the same 2-layer full-width
+    model against the oracle decoder: 16 greedy steps fed the oracle's own ids; hidden states
+    within max-abs 5e-2 / rel 2e-2, ids identical except on near-ties of the oracle's top two."""
+    from oracle import model as omodel
+    dc = small_vocab(DecoderConfig(), vocab=2048, layers=2)
+    host = synthetic.decoder_weights(dc, seed=9, preset="bf16")
+    w = DecoderWeights.from_host(dc, host, cuda_device, preset="bf16")
+    eng = DecodeEngine(w, max_length=64)
+    dec = omodel.Decoder(host, dc.as_dict(), max_length=64)
+    ids = np.zeros(1 + dc.n_vq, dtype=np.int64)
+    ids[0] = dc.audio_assistant_gen_slot_token_id
+    mismatched = 0
+    for step in range(16):
+        alen, delay = schedule(step)
+        want, text, audio, h_ref = dec.step(ids, step, alen, delay)
+        got = eng.step(torch.from_numpy(ids), step, alen, delay).reshape(-1).cpu().numpy()
+        h = from_bf16_bits(host_bits(eng.hidden)).astype(np.float64).reshape(-1)
+        ref = np.asarray(h_ref, dtype=np.float64).reshape(-1)
+        assert np.all(np.abs(h - ref) <= 5e-2 + 2e-2 * np.abs(ref)), (step, np.abs(h - ref).max())
+        bad = got != want
+        if bad.any():
+            assert not bad[0] or abs(float(text[0] - text[1])) <= 0.0625, step
+            top2 = np.sort(np.asarray(audio, dtype=np.float64), axis=-1)[:, -2:]
+            margins = (top2[:, 1] - top2[:, 0])[bad[1:]]
+            assert np.all(margins <= 0.0625), (step, margins)
+            mismatched += int(bad.sum())
+        ids = want
+    assert int(eng.status.item()) == 0
+    assert mismatched <= 0.02 * 16 * (1 + dc.n_vq), mismatched

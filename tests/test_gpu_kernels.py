@@ -176,6 +176,51 @@ def test_linear_decode_bf16(cuda_device):
         close(host_bits(y), ops.linear(from_bf16_bits(x), from_bf16_bits(w)))
 
 
+@pytest.mark.parametrize("n,k,mode", [(6144, 4096, 1), (4096, 4096, 3), (24576, 4096, 7), (4096, 12288, 0),
+                                      (4096, 6144, 0), (4096, 1536, 0), (3072, 4096, 5), (4096, 512, 0),
+                                      (1032, 2048, 4), (80000, 512, 0), (20, 256, 1)])
+def test_bf16_linear_batch1_matches_oracle(cuda_device, n, k, mode):
+    """Batch-1 bf16 GEMV streamed through shared memory (every (rows per stage, chunks per thread)
+    variant, each prologue mode, ragged last stages, fewer rows than SMs, and a matrix large
+    enough to need two launches): oracle parity, summed output exact, PDL and repeat calls
+    bitwise equal, and agreement with the register-pipelined kernel (flag bit 1)."""
+    from moss_tts._runtime import native
+    rng = np.random.Generator(np.random.PCG64(7 * n + k + mode))
+    wb = synthetic._normal_bf16(rng, (n, k))
+    xb, rb = synthetic.activation(21 + n, (1, k)), synthetic.activation(22 + n, (1, k))
+    nw = bf16_bits(from_bf16_bits(synthetic.activation(23, (k,), 0.02)) + 1.0)
+    x, r, w, g = (dev_bf16(a, cuda_device) for a in (xb, rb, wb, nw))
+    n_out = n // 2 if mode & 4 else n
+    s = torch.cuda.current_stream().cuda_stream
+
+    def run(flags):
+        y = torch.empty((1, n_out), device=cuda_device, dtype=torch.bfloat16)
+        summed = torch.zeros_like(x)
+        native.call("mt_bf16_linear", x.data_ptr(), r.data_ptr() if mode & 2 else None,
+                    g.data_ptr() if mode & 1 else None, 1e-6, summed.data_ptr() if mode & 2 else None,
+                    w.data_ptr(), y.data_ptr(), 1, n, k, mode, flags, s)
+        return host_bits(y), host_bits(summed)
+
+    y0, s0 = run(0)
+    y1, _ = run(0)
+    ypdl, _ = run(1)
+    yreg, _ = run(2)
+    xin = from_bf16_bits(xb)
+    if mode & 2:
+        s_ref, h = ops.add_rmsnorm(xin, from_bf16_bits(rb), from_bf16_bits(nw), 1e-6)
+        assert np.array_equal(s0, bf16_bits(s_ref))
+    elif mode & 1:
+        h = ops.rmsnorm(xin, from_bf16_bits(nw), 1e-6)
+    else:
+        h = xin
+    ref = ops.linear(h, from_bf16_bits(wb))
+    if mode & 4:
+        ref = ops.silu_mul(ref)
+    close(y0, ref)
+    close(yreg, ref)
+    assert np.array_equal(y0, y1) and np.array_equal(y0, ypdl)
+
+
 # ------------------------------------------------------------------ attention
 class _Cache:
     class _Layer:
