@@ -137,6 +137,21 @@ int mt_w4a16_linear_packed_tp(const void* x, const void* residual, const void* n
                               void* stream);
 
 /*
+ * Batched W4A16 G32 projection on the tcgen05 tensor cores (batch 1..128, meant for the
+ * batched decode sweep at 16 and up, where the CUDA-core GEMVs fall behind the weight
+ * stream): y[b, :] = bf16(x[b, :] . W^T) with W = bf16((q - z) * s) dequantised exactly as
+ * calibrated_quant.dequantize (src/moss_tts/_runtime/calibrated_quant.py:41-42) and fp32
+ * accumulation — the projection of dp4a_packing.linear (dp4a_packing.py:94-125) at batch > 8.
+ * mode 0, or MT_LINEAR_PAIRED (y = bf16(silu(bf16 gate)) * bf16 up, n/2 columns). GPTQ
+ * layout as mt_w4a16_linear; requires n % 128 == 0, k % 256 == 0, 16-byte aligned x and
+ * qweight. `workspace` (mt_w4a16_gemm_workspace bytes, 256-byte aligned) is zero-filled once
+ * and left with its tickets zero; calls sharing it must be ordered on one stream.
+ */
+int mt_w4a16_gemm_workspace(int batch, int n, int k, int mode, long long* bytes);
+int mt_w4a16_gemm(const void* x, const void* qweight, const void* scales, const void* qzeros, void* y,
+                  int batch, int n, int k, int mode, void* workspace, int flags, void* stream);
+
+/*
  * bf16-weight decode GEMV with the same modes as mt_w4a16_linear (w bf16 [n, k]).
  * Replaces linear_decode (src/moss_tts/_runtime/kernels.py:93-108) and the paired gate/up
  * SiLU GEMV fp8_silu_decode (src/moss_tts/_runtime/fused_mlp.py:7-30). Batch 1 with

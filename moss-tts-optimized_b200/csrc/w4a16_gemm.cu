@@ -1,0 +1,592 @@
+// W4A16 G32 skinny GEMM on the fifth-generation tensor cores (sm_100a): the batched decode
+// projections y[B, N] = x[B, K] . W^T, B = 9..128, with W = bf16((q - z) * s), the
+// reference's dequantize-then-matmul (src/moss_tts/_runtime/calibrated_quant.py:41-42 and
+// the projection of dp4a_packing.py:94-125), with fp32 accumulation; optional fused gate/up
+// pair with bf16(silu(bf16 gate)) * bf16 up (fused_mlp.py:18-23).
+//
+// Batch-1..8 decode streams weights far below the tensor-core crossover and stays on the
+// CUDA-core / mma.sync GEMV kernels; at B >= 16 one weight byte feeds 4B multiply-adds and
+// only tcgen05 keeps the dequantised stream fed at HBM speed. Design:
+//
+// * A tile is 128 weight rows (the 128 TMEM lanes). One persistent CTA per SM owns a
+//   balanced contiguous range of the (tile, 256-wide K chunk) work list, so every SM streams
+//   the same number of weight bytes; a range cuts at most two tiles (its first and last).
+// * Two loader warps fill a ring of up to eight shared-memory stages with TMA tensor loads:
+//   the chunk's 4-bit codes (128 rows x 128 bytes, 128-byte swizzle) and the activation chunk
+//   (B x 256 bf16 in four 64-column boxes with the 128-byte swizzle: the canonical K-major
+//   SWIZZLE_128B operand layout; rows past B read as zeros). The code loads do not depend
+//   on the previous kernel and start before griddepcontrol.wait.
+// * The dequantised weights never touch shared memory: sixteen dequantisation warps (warp w
+//   owns TMEM lanes 32 (w % 4) .. +31, one weight row per thread, and one quarter of each K
+//   chunk) read their row's codes from the stage (conflict-free thanks to the swizzle), their
+//   scales and zero points from L1-cached loads issued three chunks ahead, turn each code pair
+//   into an exact bf16 pair (bf16(128 + q) by bit insertion, minus bf16(128 + z) exactly,
+//   times the bf16 scale with one round to nearest: the oracle's bf16((q - z) * s) bit for
+//   bit) and store them into one of two or three TMEM slots with tcgen05.st.
+// * One thread issues tcgen05.mma.kind::f16 with A in TMEM and B in shared memory into one
+//   of two fp32 accumulators D[128, B] in TMEM (alternating per tile segment); tcgen05.commit
+//   frees a stage of the four-deep ring and hands a finished accumulator to four epilogue
+//   warps, which read it with tcgen05.ld while the next segment accumulates.
+// * A tile cut between CTAs is finished by the last contributor (ticket), which sums the
+//   contributions in CTA order, so results are deterministic.
+// Every mbarrier wait is bounded; an expired wait sets an error word and the kernel still
+// drains, releases its TMEM and returns.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include "stream_pipeline.cuh"
+
+namespace mt {
+
+__device__ int g_gemm_error;  // set when a bounded wait expired (read through mt_read_error_word)
+
+namespace tc {
+
+using namespace pipe;
+
+constexpr int kTileM = 128;        // weight rows per tile = TMEM lanes
+constexpr int kChunk = 256;        // K elements per pipeline stage
+constexpr int kMaxSlots = 3;       // TMEM A slots (3 when the batch fits 64 columns, else 2)
+constexpr int kMaxStages = 8;      // shared-memory stages (codes + activations) in flight
+constexpr int kDequantWarps = 16;  // warp w: TMEM lane quarter w % 4, K quarter w / 4
+constexpr int kMmaWarp = 16;
+constexpr int kEpiWarp0 = 17;      // warps 17..20 read the accumulators
+constexpr int kCodeWarp = 21;      // TMA loads of the 4-bit codes
+constexpr int kActWarp = 22;       // TMA loads of the activation chunks
+constexpr int kThreads = 23 * 32;
+constexpr int kMaxBatch = 128;
+constexpr int kSlotCols = kChunk / 2;  // TMEM columns of one A slot (two bf16 per column)
+constexpr uint32_t kCodeBytes = kTileM * kChunk / 2;  // codes of one chunk of one tile
+constexpr int kTmemCols = 512;
+
+struct GemmArgs {
+  const __nv_bfloat16* x;        // [batch, K]
+  const uint8_t* qweight;        // [N, K/2]
+  const __nv_bfloat16* scales;   // [N, K/32]
+  const uint8_t* qzeros;         // [N, K/64] or null (z = 8)
+  __nv_bfloat16* y;              // [batch, N] or [batch, N/2] (paired)
+  float* partial;                // [2 * grid][batch][128] contributions to cut tiles
+  unsigned* tickets;             // [tiles], zero on entry and exit
+  int batch, n, k, n_mma, tiles, chunks, stages;
+  int d_cols, slots;  // accumulator columns (64 or 128) and TMEM A slots after the two accumulators
+};
+
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+  uint32_t d;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
+  return d;
+}
+__device__ __forceinline__ uint32_t bf16x2_sub(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+__device__ __forceinline__ uint32_t bf16x2_mul(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+
+// One lane of a converged warp (PTX elect.sync): the issuing lane of a warp-uniform loop.
+__device__ __forceinline__ bool elect_one() {
+  uint32_t pred = 0;
+  asm volatile(
+      "{\n .reg .pred p;\n elect.sync _|p, 0xffffffff;\n selp.u32 %0, 1, 0, p;\n}"
+      : "=r"(pred));
+  return pred != 0;
+}
+// Bounded wait for a phase that is usually far off: back off between polls so that waiting
+// warps leave the issue slots to the dequantisation warps.
+__device__ __forceinline__ bool mbar_wait_idle(uint64_t* bar, unsigned parity) {
+  for (long i = 0; i < (1L << 22); ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    __nanosleep(64);
+  }
+  return false;
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* v) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
+      "%14, %15, %16};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+      "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr)
+      : "memory");
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// D[128, N] (+)= A[128, 16] (TMEM) . B[N, 16]^T (shared memory descriptor), bf16 in, fp32 out.
+__device__ __forceinline__ void mma_ts(uint32_t d_taddr, uint32_t a_taddr, uint64_t bdesc, uint32_t idesc,
+                                       uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, {%5, %5, %5, %5}, p;\n}" ::"r"(d_taddr),
+      "r"(a_taddr), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(0u)
+      : "memory");
+}
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+// Shared-memory matrix descriptor, K-major, no swizzle: core matrices of 8 rows x 16 bytes;
+// `lbo` = byte distance between the two K-adjacent core matrices of one K=16 step, `sbo` =
+// byte distance between 8-row groups; bit 46 = descriptor version of sm_100.
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+  return (uint64_t)((addr >> 4) & 0x3FFF) | ((uint64_t)((lbo >> 4) & 0x3FFF) << 16) |
+         ((uint64_t)((sbo >> 4) & 0x3FFF) << 32) | (1ull << 46);
+}
+// K-major, 128-byte swizzle (layout type 2): rows of 64 bf16 (128 bytes), 8-row atoms of
+// 1024 bytes at a stride of 1024; a K=16 step inside the atom advances the start by 32 bytes.
+__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t addr) {
+  return smem_desc(addr, 16, 1024) | (2ull << 61);
+}
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+
+struct RowLoads {
+  uint32_t s;     // two bf16 scales (groups 2j, 2j + 1)
+  uint32_t z;     // zero-point byte (low nibble group 2j)
+};
+
+__device__ __forceinline__ int range_start(int b, long work, int ctas) { return (int)((long)b * work / ctas); }
+// The CTA whose work range holds item w.
+__device__ __forceinline__ int owner_of(int w, long work, int ctas) {
+  int b = (int)((long)w * ctas / work);
+  while (b + 1 < ctas && range_start(b + 1, work, ctas) <= w) ++b;
+  while (b > 0 && range_start(b, work, ctas) > w) --b;
+  return b;
+}
+
+template <bool PAIRED>
+__global__ void __launch_bounds__(kThreads, 1)
+    w4a16_gemm_tc(GemmArgs a, const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap wmap) {
+  // dynamic shared memory, from the first 1024-byte boundary: [stages] x {codes [128][128 B]
+  // (128-byte swizzle), activations [4][n_mma][64] bf16 (128-byte swizzle)}, then [16][64] f32
+  // for the paired epilogue
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  __shared__ __align__(8) uint64_t full[kMaxSlots];    // dequantised chunk in TMEM slot
+  __shared__ __align__(8) uint64_t aempty[kMaxSlots];  // MMAs done with TMEM slot
+  __shared__ __align__(8) uint64_t wfull[kMaxStages];  // codes landed
+  __shared__ __align__(8) uint64_t xfull[kMaxStages];  // activations landed
+  __shared__ __align__(8) uint64_t sempty[kMaxStages];  // MMAs done with the stage
+  __shared__ __align__(8) uint64_t dfull[2];
+  __shared__ __align__(8) uint64_t dfree[2];
+  __shared__ uint32_t tmem_base_s;
+  __shared__ int abort_s;
+  __shared__ unsigned last_s;
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int K = a.k, n_mma = a.n_mma, B = a.batch, chunks = a.chunks, ctas = gridDim.x, nst = a.stages;
+  const int n_out = PAIRED ? a.n / 2 : a.n;
+  const long work = (long)a.tiles * chunks;
+  const int w0 = range_start(blockIdx.x, work, ctas), w1 = range_start(blockIdx.x + 1, work, ctas);
+  const int nwork = w1 - w0;
+  const int t_first = w0 / chunks;
+  const int nseg = nwork > 0 ? (w1 - 1) / chunks - t_first + 1 : 0;
+  const int nslot = a.slots, a_col0 = 2 * a.d_cols;
+  const uint32_t x_bytes = (uint32_t)n_mma * kChunk * 2, x_box = (uint32_t)n_mma * 128;  // 64-column boxes
+  const uint32_t stage_bytes = kCodeBytes + x_bytes;
+  uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
+  float* exch = reinterpret_cast<float*>(smem + nst * stage_bytes);
+
+  if (warp == kMmaWarp) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base_s)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    if (lane == 0) {
+      for (int i = 0; i < kMaxSlots; ++i) {
+        mbar_init(&full[i], kDequantWarps * 32);
+        mbar_init(&aempty[i], 1);
+      }
+      for (int i = 0; i < kMaxStages; ++i) {
+        mbar_init(&wfull[i], 1);
+        mbar_init(&xfull[i], 1);
+        mbar_init(&sempty[i], 1);
+      }
+      for (int i = 0; i < 2; ++i) {
+        mbar_init(&dfull[i], 1);
+        mbar_init(&dfree[i], 128);
+      }
+      abort_s = 0;
+      asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_base_s;
+  pdl_trigger();
+
+  if (warp < kDequantWarps) {
+    const int q = warp & 3, h = warp >> 2, m = 32 * q + lane;
+    // scales and zero points: L1-cached loads three chunks ahead (a 32-byte sector serves 4 / 16 chunks)
+    auto load = [&](int j, RowLoads& r) {
+      if (j < nwork) {
+        const int w = w0 + j, tile = w / chunks, c = w - tile * chunks;
+        const int row = PAIRED ? (m < 64 ? tile * 64 + m : n_out + tile * 64 + (m - 64)) : tile * kTileM + m;
+        r.s = __ldg(reinterpret_cast<const uint32_t*>(a.scales + (size_t)row * (K / 32) + c * 8 + h * 2));
+        r.z = a.qzeros ? (uint32_t)__ldg(a.qzeros + (size_t)row * (K / 64) + c * 4 + h) : 0x88u;
+      }
+    };
+    RowLoads buf[4];
+    load(0, buf[0]);
+    load(1, buf[1]);
+    load(2, buf[2]);
+    // weights are never written by a predecessor: no dependency wait before streaming them
+    const uint32_t t_lane = (uint32_t)(32 * q) << 16;
+    const int sw = m & 7;  // 128-byte swizzle of row m: 16-byte piece p sits at p ^ sw
+    const uint32_t code_off = (uint32_t)m * 128;
+
+    auto process = [&](int j, const RowLoads& r) {
+      const int slot = j % nslot, st = j % nst;
+      bool ok = true;
+      if (j >= nslot) {  // the MMAs of chunk j - nslot have released this TMEM slot
+        ok = mbar_wait_bounded(&aempty[slot], (unsigned)(((j / nslot) - 1) & 1));
+        tc_fence_after();
+      }
+      ok = mbar_wait_bounded(&wfull[st], (unsigned)((j / nst) & 1)) && ok;
+      if (!ok) abort_s = 1;
+      const uint8_t* cs = smem + st * stage_bytes + code_off;
+      const uint4 c0 = *reinterpret_cast<const uint4*>(cs + (((2 * h) ^ sw) << 4));
+      const uint4 c1 = *reinterpret_cast<const uint4*>(cs + (((2 * h + 1) ^ sw) << 4));
+      // dequantise 64 codes -> 32 bf16 pairs: code word i holds k = 8i .. 8i + 7
+      const uint32_t zlo = r.z & 0xF, zhi = (r.z >> 4) & 0xF;
+      const uint32_t zz0 = (0x4300u + zlo) * 0x10001u, zz1 = (0x4300u + zhi) * 0x10001u;
+      const uint32_t s0 = (r.s & 0xFFFFu) * 0x10001u, s1 = (r.s >> 16) * 0x10001u;
+      const uint32_t cw[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+      uint32_t v[32];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const uint32_t u = cw[i], hi = u >> 4;
+        const uint32_t zz = i < 4 ? zz0 : zz1, ss = i < 4 ? s0 : s1;
+#pragma unroll
+        for (int b = 0; b < 4; ++b) {
+          const uint32_t t = (prmt(u, hi, 0x0400u + 0x0101u * b) & 0x000F000Fu) | 0x43004300u;
+          v[4 * i + b] = bf16x2_mul(bf16x2_sub(t, zz), ss);
+        }
+      }
+      const uint32_t ta = tmem + t_lane + (uint32_t)(a_col0 + slot * kSlotCols + h * 32);
+      __syncwarp();
+      tmem_st16(ta, v);
+      tmem_st16(ta + 16, v + 16);
+      asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+      tc_fence_before();
+      mbar_arrive(&full[slot]);
+    };
+#pragma unroll 1
+    for (int j = 0; j < nwork; j += 4) {
+      load(j + 3, buf[3]);
+      process(j, buf[0]);
+      if (j + 1 < nwork) {
+        load(j + 4, buf[0]);
+        process(j + 1, buf[1]);
+      }
+      if (j + 2 < nwork) {
+        load(j + 5, buf[1]);
+        process(j + 2, buf[2]);
+      }
+      if (j + 3 < nwork) {
+        load(j + 6, buf[2]);
+        process(j + 3, buf[3]);
+      }
+    }
+  } else if (warp == kMmaWarp) {
+    // warp-uniform loop; one elected lane issues the MMAs and commits
+    const uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n_mma >> 3) << 17) |
+                           ((uint32_t)(kTileM >> 4) << 24);
+    const uint32_t b0 = smem_u32(smem) + kCodeBytes;
+    int seg = -1;
+    for (int j = 0; j < nwork; ++j) {
+      const int w = w0 + j, c = w % chunks;
+      const bool first = j == 0 || c == 0, last = j == nwork - 1 || c == chunks - 1;
+      if (first) {
+        ++seg;
+        if (seg >= 2) {  // the epilogue must have read this accumulator's previous segment
+          if (!mbar_wait_bounded(&dfree[seg & 1], (unsigned)(((seg >> 1) - 1) & 1))) abort_s = 1;
+          tc_fence_after();
+        }
+      }
+      const int slot = j % nslot, st = j % nst;
+      const bool ok = mbar_wait_bounded(&xfull[st], (unsigned)((j / nst) & 1)) &&
+                      mbar_wait_bounded(&full[slot], (unsigned)((j / nslot) & 1));
+      tc_fence_after();
+      if (!ok) abort_s = 1;
+      const uint32_t d = tmem + (uint32_t)((seg & 1) * a.d_cols);
+      const uint32_t a_col = tmem + (uint32_t)(a_col0 + slot * kSlotCols);
+      const uint32_t x0 = b0 + st * stage_bytes;
+      __syncwarp();
+      if (elect_one()) {
+        if (ok && !abort_s) {
+#pragma unroll
+          for (int kk = 0; kk < kChunk / 16; ++kk)
+            mma_ts(d, a_col + kk * 8, smem_desc_sw128(x0 + (kk >> 2) * x_box + (kk & 3) * 32), idesc,
+                   (first && kk == 0) ? 0u : 1u);
+        }
+        mma_commit(&aempty[slot]);
+        mma_commit(&sempty[st]);
+        if (last) mma_commit(&dfull[seg & 1]);
+      }
+      __syncwarp();
+    }
+  } else if (warp == kCodeWarp || warp == kActWarp) {
+    // codes (independent of the previous kernel) and activations; warp-uniform loops, one
+    // elected lane issues each stage's TMA loads
+    const bool codes = warp == kCodeWarp;
+    if (!codes) pdl_wait();
+    const uint32_t b0 = smem_u32(smem);
+    for (int j = 0; j < nwork; ++j) {
+      const int st = j % nst;
+      if (j >= nst && !mbar_wait_idle(&sempty[st], (unsigned)(((j / nst) - 1) & 1))) abort_s = 1;
+      const int w = w0 + j, tile = w / chunks, c = w - tile * chunks;
+      const uint32_t base = b0 + st * stage_bytes;
+      __syncwarp();
+      if (elect_one()) {
+        if (codes) {
+          const int r0 = PAIRED ? tile * 64 : tile * kTileM, r1 = PAIRED ? n_out + tile * 64 : r0 + 64;
+          mbar_expect_tx(&wfull[st], kCodeBytes);
+          tma_load_2d(base, &wmap, c * (kChunk / 2), r0, &wfull[st]);
+          tma_load_2d(base + kCodeBytes / 2, &wmap, c * (kChunk / 2), r1, &wfull[st]);
+        } else {
+          mbar_expect_tx(&xfull[st], x_bytes);
+#pragma unroll
+          for (int bx = 0; bx < kChunk / 64; ++bx)
+            tma_load_2d(base + kCodeBytes + bx * x_box, &xmap, c * kChunk + 64 * bx, 0, &xfull[st]);
+        }
+      }
+      __syncwarp();
+    }
+  } else {
+    // Epilogue warps: lane quarter warp % 4; e = 0..127 indexes the named barrier group.
+    const int q = warp & 3, m = 32 * q + lane, e = tid - kEpiWarp0 * 32;
+    const uint32_t t_lane = (uint32_t)(32 * q) << 16;
+    pdl_wait();
+    auto emit = [&](int tile, int cb, const float* v) {
+      if (PAIRED) {  // fused_mlp.py:18-23: rows < 64 gate, rows >= 64 the matching up rows
+        if (m >= 64)
+#pragma unroll
+          for (int t = 0; t < 16; ++t) exch[t * 64 + (m - 64)] = v[t];
+        named_sync(1, 128);
+        if (m < 64) {
+#pragma unroll
+          for (int t = 0; t < 16; ++t) {
+            if (cb + t < B) {
+              const float gate = round_bf16(v[t]), up = round_bf16(exch[t * 64 + m]);
+              a.y[(size_t)(cb + t) * n_out + tile * 64 + m] = to_bf16(round_bf16(gate / (1.0f + expf(-gate))) * up);
+            }
+          }
+        }
+        named_sync(1, 128);
+      } else {
+#pragma unroll
+        for (int t = 0; t < 16; ++t)
+          if (cb + t < B) a.y[(size_t)(cb + t) * n_out + tile * kTileM + m] = to_bf16(v[t]);
+      }
+    };
+    for (int s = 0; s < nseg; ++s) {
+      const int tile = t_first + s;
+      const int ca = max(w0, tile * chunks) - tile * chunks, ce = min(w1, (tile + 1) * chunks) - tile * chunks;
+      const bool whole = ca == 0 && ce == chunks;
+      if (!mbar_wait_idle(&dfull[s & 1], (unsigned)((s >> 1) & 1))) abort_s = 1;
+      tc_fence_after();
+      const uint32_t d = tmem + t_lane + (uint32_t)((s & 1) * a.d_cols);
+      float* mine = a.partial + (size_t)(2 * blockIdx.x + (s == 0 ? 0 : 1)) * B * kTileM;
+      for (int cb = 0; cb < n_mma; cb += 16) {
+        float v[16];
+        __syncwarp();
+        tmem_ld16(d + (uint32_t)cb, v);
+        if (whole) {
+          emit(tile, cb, v);
+        } else {
+#pragma unroll
+          for (int t = 0; t < 16; ++t)
+            if (cb + t < B) mine[(size_t)(cb + t) * kTileM + m] = v[t];
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&dfree[s & 1]);
+      if (whole) continue;
+      // A cut tile: the last contributor sums the contributions in CTA order.
+      const int b_first = owner_of(tile * chunks, work, ctas), b_last = owner_of(tile * chunks + chunks - 1, work, ctas);
+      __threadfence();
+      named_sync(1, 128);
+      if (e == 0) last_s = atomicAdd(a.tickets + tile, 1u) == (unsigned)(b_last - b_first) ? 1u : 0u;
+      named_sync(1, 128);
+      if (last_s) {
+        __threadfence();
+        for (int cb = 0; cb < n_mma; cb += 16) {
+          float v[16];
+#pragma unroll
+          for (int t = 0; t < 16; ++t) v[t] = 0.f;
+          for (int b = b_first; b <= b_last; ++b) {
+            const int slot = 2 * b + (range_start(b, work, ctas) / chunks == tile ? 0 : 1);
+            const float* src = a.partial + (size_t)slot * B * kTileM;
+#pragma unroll
+            for (int t = 0; t < 16; ++t)
+              if (cb + t < B) v[t] += __ldcg(src + (size_t)(cb + t) * kTileM + m);
+          }
+          emit(tile, cb, v);
+        }
+        if (e == 0) a.tickets[tile] = 0u;
+      }
+      named_sync(1, 128);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (abort_s && tid == 0) atomicExch(&g_gemm_error, 1);
+  if (warp == kMmaWarp) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+  }
+}
+
+struct Plan {
+  int tiles, chunks, n_mma, ctas, stages, d_cols, slots;
+  size_t smem, partial_bytes, ticket_bytes;
+};
+
+static bool make_plan(int batch, int n, int k, int mode, Plan* p) {
+  const bool paired = mode & 4;
+  if (batch < 1 || batch > kMaxBatch || k < kChunk || k % kChunk || n < kTileM || n % kTileM) return false;
+  p->tiles = paired ? (n / 2) / 64 : n / kTileM;
+  p->chunks = k / kChunk;
+  p->n_mma = (batch + 15) / 16 * 16;
+  p->d_cols = p->n_mma <= 64 ? 64 : 128;
+  p->slots = (kTmemCols - 2 * p->d_cols) / kSlotCols;
+  const long work = (long)p->tiles * p->chunks;
+  p->ctas = (int)(work < sm_count() ? work : sm_count());
+  const size_t stage = kCodeBytes + (size_t)p->n_mma * kChunk * 2, fixed = 1024 + 16 * 64 * sizeof(float);
+  p->stages = (int)((200 * 1024 - fixed) / stage);
+  if (p->stages > kMaxStages) p->stages = kMaxStages;
+  if (p->stages < 2) return false;
+  p->smem = fixed + (size_t)p->stages * stage;
+  p->ticket_bytes = ((size_t)p->tiles * sizeof(unsigned) + 255) / 256 * 256;
+  p->partial_bytes = (size_t)2 * p->ctas * batch * kTileM * sizeof(float);
+  return true;
+}
+
+static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
+  if (!encode) {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess && fn)
+      encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  }
+  return encode;
+}
+
+// TMA map of the 4-bit codes qweight [n, k/2] bytes: boxes of 128 bytes (one K chunk) x 64 rows
+// with the 128-byte swizzle.
+static bool code_map(CUtensorMap* map, const void* qweight, int n, int k) {
+  PFN_cuTensorMapEncodeTiled_v12000 encode = tensor_map_encoder();
+  if (!encode) return false;
+  const cuuint64_t dims[2] = {(cuuint64_t)k / 2, (cuuint64_t)n};
+  const cuuint64_t strides[1] = {(cuuint64_t)k / 2};
+  const cuuint32_t box[2] = {kChunk / 2, 64};
+  const cuuint32_t estr[2] = {1, 1};
+  return encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(qweight), dims, strides, box, estr,
+                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// TMA map of the activations x [batch, k] bf16: boxes of 64 columns x n_mma rows with the
+// 128-byte swizzle; rows past `batch` are out of bounds and read as zeros.
+static bool activation_map(CUtensorMap* map, const void* x, int batch, int k, int n_mma) {
+  PFN_cuTensorMapEncodeTiled_v12000 encode = tensor_map_encoder();
+  if (!encode) return false;
+  const cuuint64_t dims[2] = {(cuuint64_t)k, (cuuint64_t)batch};
+  const cuuint64_t strides[1] = {(cuuint64_t)k * 2};
+  const cuuint32_t box[2] = {64, (cuuint32_t)n_mma};
+  const cuuint32_t estr[2] = {1, 1};
+  return encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(x), dims, strides, box, estr,
+                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+}  // namespace tc
+
+cudaError_t gemm_error_word(int* value, bool clear) {
+  int v = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, g_gemm_error, sizeof(int));
+  if (e != cudaSuccess) return e;
+  *value |= v;
+  if (clear) {
+    const int zero = 0;
+    e = cudaMemcpyToSymbol(g_gemm_error, &zero, sizeof(int));
+  }
+  return e;
+}
+
+}  // namespace mt
+
+using namespace mt;
+
+// Workspace bytes of mt_w4a16_gemm on the current device for this shape (tickets first,
+// then the contributions to tiles cut between CTAs). The workspace must be zero-filled once; calls leave the tickets zero.
+MT_API int mt_w4a16_gemm_workspace(int batch, int n, int k, int mode, long long* bytes) {
+  tc::Plan p;
+  if (!bytes || (mode & ~4) || !tc::make_plan(batch, n, k, mode, &p)) return kBadArgument;
+  *bytes = (long long)(p.ticket_bytes + p.partial_bytes);
+  return 0;
+}
+
+// Batched W4A16 G32 projection on tcgen05 tensor cores: y[b, :] = bf16(x[b, :] . W^T) for
+// b < batch (1..128; meant for 16 and up), W = bf16((q - z) * s) from the GPTQ layout
+// (qweight uint8 [n, k/2], scales bf16 [n, k/32], qzeros uint8 [n, k/64] or NULL for z = 8).
+// mode 0, or MT_LINEAR_PAIRED (rows [0, n/2) gate, [n/2, n) up; y has n/2 columns).
+// Requires n % 128 == 0, k % 256 == 0, 16-byte aligned x / qweight / y.
+MT_API int mt_w4a16_gemm(const void* x, const void* qweight, const void* scales, const void* qzeros, void* y,
+                         int batch, int n, int k, int mode, void* workspace, int flags, void* stream) {
+  tc::Plan p;
+  if (!x || !qweight || !scales || !y || !workspace || (mode & ~4) || !tc::make_plan(batch, n, k, mode, &p))
+    return kBadArgument;
+  if (!aligned(x, 16) || !aligned(qweight, 16) || !aligned(scales, 4) || !aligned(workspace, 256)) return kBadArgument;
+  tc::GemmArgs a;
+  a.x = (const __nv_bfloat16*)x;
+  a.qweight = (const uint8_t*)qweight;
+  a.scales = (const __nv_bfloat16*)scales;
+  a.qzeros = (const uint8_t*)qzeros;
+  a.y = (__nv_bfloat16*)y;
+  a.tickets = (unsigned*)workspace;
+  a.partial = (float*)((uint8_t*)workspace + p.ticket_bytes);
+  a.batch = batch;
+  a.n = n;
+  a.k = k;
+  a.n_mma = p.n_mma;
+  a.tiles = p.tiles;
+  a.chunks = p.chunks;
+  a.stages = p.stages;
+  a.d_cols = p.d_cols;
+  a.slots = p.slots;
+  alignas(64) CUtensorMap xmap, wmap;
+  if (!tc::activation_map(&xmap, x, batch, k, p.n_mma) || !tc::code_map(&wmap, qweight, n, k))
+    return (int)cudaErrorNotSupported;
+  const dim3 grid(p.ctas), block(tc::kThreads);
+  cudaStream_t s = (cudaStream_t)stream;
+  if (mode & 4) return (int)launch(tc::w4a16_gemm_tc<true>, grid, block, p.smem, s, flags & kFlagPdl, a, xmap, wmap);
+  return (int)launch(tc::w4a16_gemm_tc<false>, grid, block, p.smem, s, flags & kFlagPdl, a, xmap, wmap);
+}

@@ -768,6 +768,7 @@ MT_API int mt_w4a16_linear_packed_tp(const void* x, const void* residual, const 
 namespace mt {
 cudaError_t heads_error_word(int* value, bool clear);
 cudaError_t bf16_error_word(int* value, bool clear);
+cudaError_t gemm_error_word(int* value, bool clear);
 }
 
 MT_API int mt_read_error_word(int* value, int clear) {
@@ -779,5 +780,6 @@ MT_API int mt_read_error_word(int* value, int clear) {
   }
   if (e == cudaSuccess) e = heads_error_word(value, clear != 0);
   if (e == cudaSuccess) e = bf16_error_word(value, clear != 0);
+  if (e == cudaSuccess) e = gemm_error_word(value, clear != 0);
   return (int)e;
 }

@@ -29,6 +29,8 @@ SIGNATURES = {
     "mt_w4a16_pack": ([_P, _P, _P, _I, _I, _I, _P, _P], _I),
     "mt_w4a16_linear_packed": ([_P, _P, _P, _F, _P, _P, _I, _P, _I, _I, _I, _P, _I, _P], _I),
     "mt_w4a16_linear_packed_tp": ([_P, _P, _P, _F, _P, _P, _I, _P, _I, _I, _I, _P, _P, _I, _P], _I),
+    "mt_w4a16_gemm_workspace": ([_I, _I, _I, _I, _LLP], _I),
+    "mt_w4a16_gemm": ([_P, _P, _P, _P, _P, _I, _I, _I, _I, _P, _I, _P], _I),
     "mt_bf16_linear": ([_P, _P, _P, _F, _P, _P, _P, _I, _I, _I, _I, _I, _P], _I),
     "mt_rmsnorm": ([_P, _P, _P, _P, _P, _I, _I, _F, _I, _P], _I),
     "mt_silu_mul": ([_P, _P, _I, _I, _I, _P], _I),
@@ -89,6 +91,13 @@ def w4a16_packed_size(n: int, k: int, has_zeros: bool, mode: int) -> tuple[int, 
     pb, wb = ctypes.c_longlong(0), ctypes.c_longlong(0)
     call("mt_w4a16_packed_size", n, k, 1 if has_zeros else 0, mode, ctypes.byref(pb), ctypes.byref(wb))
     return pb.value, wb.value
+
+
+def w4a16_gemm_workspace(batch: int, n: int, k: int, mode: int) -> int:
+    """Workspace bytes of mt_w4a16_gemm for this shape on the current device."""
+    b = ctypes.c_longlong(0)
+    call("mt_w4a16_gemm_workspace", batch, n, k, mode, ctypes.byref(b))
+    return b.value
 
 
 def ptr(t) -> int | None:

@@ -33,11 +33,28 @@ def _weights(packed, scales, zeros, group):
     return packed, n, k
 
 
+_WORKSPACES: dict = {}
+
+
+def gemm_workspace(device, batch: int, n: int, k: int, paired: bool = False) -> torch.Tensor:
+    """Zero-filled workspace of ``mt_w4a16_gemm`` for this shape, cached per device and grown
+    on demand (the kernel leaves its tickets zero, so calls ordered on one stream share it)."""
+    nbytes = native.w4a16_gemm_workspace(batch, n, k, native.LINEAR_PAIRED if paired else 0)
+    dev = torch.device(device)
+    ws = _WORKSPACES.get(dev)
+    if ws is None or ws.numel() < nbytes:
+        ws = torch.zeros(max(nbytes, 256), dtype=torch.uint8, device=dev)
+        _WORKSPACES[dev] = ws
+    return ws
+
+
 def linear(x, packed, scales, zeros=None, *, group=32, paired=False, prequantized=None, pdl=False):
-    """``y = x @ dequant(W).T`` in bf16 with fp32 accumulation, for 1..8 activation rows.
+    """``y = x @ dequant(W).T`` in bf16 with fp32 accumulation, for 1..128 activation rows.
 
     ``paired=True`` treats rows ``[0, N/2)`` as gate and ``[N/2, N)`` as up and returns
     ``bf16(bf16(silu(gate)) * up)`` with ``N/2`` columns (``dp4a_packing.py:85-89``).
+    Up to 8 rows run the CUDA-core GEMV; 9..128 rows run the
+    tcgen05 tensor-core GEMM (N % 128 == 0, K % 256 == 0) with a cached workspace.
     """
     if prequantized is not None:
         raise ValueError("W4A16 takes bf16 activations; int8 prequantized inputs are not used")
@@ -46,14 +63,22 @@ def linear(x, packed, scales, zeros=None, *, group=32, paired=False, prequantize
     _cuda(x, packed, scales, zeros)
     _bf16(x)
     rows = x.numel() // x.shape[-1]
-    if x.shape[-1] != k or not 1 <= rows <= 8:
-        raise ValueError("Expected 1..8 contiguous bf16 activation rows of width K")
+    if x.shape[-1] != k or not 1 <= rows <= 128:
+        raise ValueError("Expected 1..128 contiguous bf16 activation rows of width K")
     out_n = n // 2 if paired else n
     y = torch.empty((*x.shape[:-1], out_n), device=x.device, dtype=x.dtype)
-    native.call("mt_w4a16_linear", x.data_ptr(), None, None, 0.0, None, packed.data_ptr(),
-                scales.data_ptr(), native.ptr(zeros), y.data_ptr(), rows, n, k, group,
-                native.LINEAR_PAIRED if paired else 0, native.FLAG_PDL if pdl else 0,
-                native.stream_of(x))
+    mode = native.LINEAR_PAIRED if paired else 0
+    flags = native.FLAG_PDL if pdl else 0
+    if rows <= 8:
+        native.call("mt_w4a16_linear", x.data_ptr(), None, None, 0.0, None, packed.data_ptr(),
+                    scales.data_ptr(), native.ptr(zeros), y.data_ptr(), rows, n, k, group, mode, flags,
+                    native.stream_of(x))
+        return y
+    if n % 128 or k % 256:
+        raise ValueError("More than 8 rows need N a multiple of 128 and K a multiple of 256")
+    ws = gemm_workspace(x.device, rows, n, k, paired)
+    native.call("mt_w4a16_gemm", x.data_ptr(), packed.data_ptr(), scales.data_ptr(), native.ptr(zeros),
+                y.data_ptr(), rows, n, k, mode, ws.data_ptr(), flags, native.stream_of(x))
     return y
 
 

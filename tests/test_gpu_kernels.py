@@ -176,6 +176,53 @@ def test_linear_decode_bf16(cuda_device):
         close(host_bits(y), ops.linear(from_bf16_bits(x), from_bf16_bits(w)))
 
 
+@pytest.mark.parametrize("n,k,paired,zeros,batch", [
+    (6144, 4096, False, True, 16), (24576, 4096, True, True, 32), (4096, 12288, False, True, 64),
+    (4096, 4096, False, False, 48), (768, 4096, False, True, 9), (3072, 4096, True, False, 64),
+    (4096, 512, False, True, 128), (256, 256, True, True, 17), (4096, 1536, False, True, 33)])
+def test_tcgen05_gemm_matches_oracle(cuda_device, n, k, paired, zeros, batch):
+    """Batched W4A16 projection on the tcgen05 tensor cores: oracle parity (dequantise then
+    bf16 x bf16 with fp32 accumulation), split-K tickets back to zero, repeat calls bitwise
+    equal, ragged batches (padded MMA columns), with and without zero points, fused pair."""
+    from moss_tts._runtime import native
+    rng = np.random.Generator(np.random.PCG64(n + 7 * k + batch))
+    p = synthetic.quantized(rng, n, k, 32, zeros)
+    qw, sc, qz = upload_w4(p, cuda_device)
+    xb = synthetic.activation(31 + batch, (batch, k))
+    x = dev_bf16(xb, cuda_device)
+    mode = native.LINEAR_PAIRED if paired else 0
+    nbytes = native.w4a16_gemm_workspace(batch, n, k, mode)
+    ws = torch.zeros(nbytes, dtype=torch.uint8, device=cuda_device)
+    n_out = n // 2 if paired else n
+    outs = []
+    for flags in (0, 0, 1):
+        y = torch.empty((batch, n_out), device=cuda_device, dtype=torch.bfloat16)
+        native.call("mt_w4a16_gemm", x.data_ptr(), qw.data_ptr(), sc.data_ptr(), native.ptr(qz), y.data_ptr(),
+                    batch, n, k, mode, ws.data_ptr(), flags, torch.cuda.current_stream().cuda_stream)
+        outs.append(host_bits(y))
+    torch.cuda.synchronize()
+    assert native.error_word(clear=True) == 0
+    ntiles = n_out // 64 if paired else n // 128
+    assert int(ws[:ntiles * 4].view(torch.int32).abs().sum()) == 0
+    ref = ops.linear(from_bf16_bits(xb), quant.dequantize_w4(p["qweight"], p["scales"], p["qzeros"]))
+    if paired:
+        ref = ops.silu_mul(ref)
+    close(outs[0], ref)
+    assert np.array_equal(outs[0], outs[1]) and np.array_equal(outs[0], outs[2])
+
+
+def test_quantized_linear_routes_large_batches_to_tcgen05(cuda_device):
+    """quantized.linear keeps the reference signature for 9..128 rows (tcgen05 GEMM)."""
+    rng = np.random.Generator(np.random.PCG64(91))
+    p = synthetic.quantized(rng, 1024, 1024, 32, True)
+    qw, sc, qz = upload_w4(p, cuda_device)
+    xb = synthetic.activation(92, (2, 12, 1024))
+    y = quantized.linear(dev_bf16(xb, cuda_device), qw, sc, qz)
+    assert y.shape == (2, 12, 1024)
+    ref = ops.linear(from_bf16_bits(xb).reshape(24, 1024), quant.dequantize_w4(p["qweight"], p["scales"], p["qzeros"]))
+    close(host_bits(y).reshape(24, 1024), ref)
+
+
 @pytest.mark.parametrize("n,k,mode", [(6144, 4096, 1), (4096, 4096, 3), (24576, 4096, 7), (4096, 12288, 0),
                                       (4096, 6144, 0), (4096, 1536, 0), (3072, 4096, 5), (4096, 512, 0),
                                       (1032, 2048, 4), (80000, 512, 0), (20, 256, 1)])
