@@ -46,6 +46,9 @@ def parse():
     ap.add_argument("--layers", type=int, default=36, help=argparse.SUPPRESS)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-bf16", action="store_true", help="skip the BF16-preset step timing")
+    ap.add_argument("--batch-sweep", default=None, metavar="B,B,...",
+                    help="config 4: batched decode of B sequences with ragged contexts (uniform in "
+                         "[256, 4096], seeded) for each listed B; prints one JSON line per B")
     ap.add_argument("--profile-kernel", action="store_true",
                     help="only launch the dominant kernel (packed add+norm+gate/up+SiLU GEMV), once per "
                          "layer per step, for an ncu capture; prints its mean launch time")
@@ -264,6 +267,102 @@ def bf16_step_rate(args, cfg, dev, rank, world, group, max_length):
     return args.steps / (ms / 1000.0), ms / args.steps, step_bytes, status
 
 
+def batch_sweep(args, rank, world, local):
+    """Config 4: W4A16 decode of B independent sequences per step, each with its own context
+    length drawn uniformly from [256, 4096] (seeded), for every B of --batch-sweep. One step
+    advances every sequence by one token; the metric is tokens/s = B x steps/s (device-resident
+    inputs, CUDA graph with device-side advance, CUDA events, max over ranks). B = 1 runs the
+    batch-1 engine; larger B the batched engine (tcgen05 GEMM projections)."""
+    import torch
+    import torch.distributed as dist
+
+    from moss_tts._runtime.batch_engine import BatchDecodeEngine
+    from moss_tts._runtime.config import DecoderConfig
+    from moss_tts._runtime.engine import DecodeEngine, TensorParallel, shard_weights
+    from moss_tts._runtime import native
+    from moss_tts._runtime.weights import DecoderWeights
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    group = None
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+        group = dist.group.WORLD
+        dist.all_reduce(torch.ones(1, device=dev))
+    cfg = DecoderConfig().with_(num_layers=args.layers)
+    peak, peak_kind = measured_peaks()
+    batches = [int(b) for b in args.batch_sweep.split(",") if b]
+    max_length = ((4096 + args.warmup + args.steps + 1 + 127) // 128) * 128
+    with torch.inference_mode():
+        full = DecoderWeights.random(cfg, dev, seed=0, preset="gptq", full_text_head=False)
+        weights = shard_weights(full, rank, world)
+        del full
+        torch.cuda.empty_cache()
+        tp = TensorParallel(rank, world, group)
+        weight_bytes = weights.layer_bytes() + weights.head_audio.numel() * 2 + 2 * cfg.hidden_size * 2
+        kv_row = 2 * (cfg.num_kv_heads // world) * cfg.head_dim * 2 * args.layers  # bytes per token, all layers
+        for B in batches:
+            rng = torch.Generator().manual_seed(1000 + B)
+            ctx = torch.randint(256, 4097, (B,), generator=rng)
+            if B == 1:
+                eng = DecodeEngine(weights, max_length=max_length, tp=tp)
+                kv = eng.kv.unsqueeze(2)
+            else:
+                eng = BatchDecodeEngine(weights, B, max_length=max_length, tp=tp)
+                kv = eng.kv
+            g = torch.Generator(device=dev).manual_seed(100 + rank)
+            kv.normal_(generator=g)  # synthetic prompts: every cached row is N(0, 1)
+            ids = torch.full((B, 33), 17, dtype=torch.long)
+            ids[:, 0] = cfg.audio_assistant_gen_slot_token_id
+            if B == 1:
+                eng.set_inputs(ids[0], int(ctx[0]), 1, -1)
+            else:
+                eng.set_inputs(ids, ctx, torch.ones(B, dtype=torch.long), torch.full((B,), -1, dtype=torch.long))
+            eng.capture(advance=True)
+            for _ in range(args.warmup):
+                eng.run(advance=True)
+            if world > 1:
+                dist.barrier()
+            torch.cuda.synchronize(dev)
+            stream = torch.cuda.current_stream(dev)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            with ClockSampler(local) as clocks:
+                e0.record(stream)
+                for _ in range(args.steps):
+                    eng.run(advance=True)
+                e1.record(stream)
+                torch.cuda.synchronize(dev)
+            ms = torch.tensor([e0.elapsed_time(e1)], device=dev)
+            if world > 1:
+                dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+            ms = float(ms.item()) / args.steps
+            status = int(eng.status.item()) | native.error_word(clear=True)
+            # bytes one step must read per GPU: weights once + every sequence's KV rows (mid-run context)
+            mean_ctx = float(ctx.double().mean()) + args.warmup + args.steps / 2
+            step_bytes = weight_bytes + int(kv_row * mean_ctx * B)
+            if rank == 0:
+                print(json.dumps({
+                    "metric": "batched decode tokens/s (8B W4A16 G32, ragged contexts)", "value": round(B * 1000.0 / ms, 2),
+                    "unit": "tokens/s", "batch": B, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+                    "ms_per_step": round(ms, 4), "steps_per_s": round(1000.0 / ms, 2), "dtype": "bf16",
+                    "data": "synthetic", "scaling": "strong",
+                    "config": {"workload": "config4: 36-layer 8B-shaped decoder, W4A16 G32, batched greedy decode, "
+                                           "per-sequence context uniform in [256, 4096] (seeded)",
+                               "parallelism": f"tp{world}", "projections": "packed GEMV" if B == 1 else
+                               ("tcgen05 GEMM" if getattr(eng, "gemm", False) else "GPTQ-layout GEMV"),
+                               "mean_context": round(mean_ctx, 1)},
+                    "step_bytes_per_gpu": step_bytes,
+                    "hbm_roofline_frac": round(step_bytes / (ms * 1e-3) / 1e9 / peak, 4), "peak_gbs": peak,
+                    "peak_kind": peak_kind, "clocks": clocks.summary(), "status": status}), flush=True)
+            eng.graph = eng.graph_advance = None
+            del eng, kv
+            torch.cuda.empty_cache()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main():
     args = parse()
     rank = int(os.environ.get("RANK", "0"))
@@ -274,6 +373,9 @@ def main():
         return
     if args.profile_kernel:
         profile_kernel(args)
+        return
+    if args.batch_sweep:
+        batch_sweep(args, rank, world, local)
         return
     import torch
     import torch.distributed as dist

@@ -145,7 +145,8 @@ int mt_w4a16_linear_packed_tp(const void* x, const void* residual, const void* n
  * mode 0, or MT_LINEAR_PAIRED (y = bf16(silu(bf16 gate)) * bf16 up, n/2 columns). GPTQ
  * layout as mt_w4a16_linear; requires n % 128 == 0, k % 256 == 0, 16-byte aligned x and
  * qweight. `workspace` (mt_w4a16_gemm_workspace bytes, 256-byte aligned) is zero-filled once
- * and left with its tickets zero; calls sharing it must be ordered on one stream.
+ * and left with its tickets zero; calls of any shapes may share one workspace of the largest
+ * size when they are ordered on one stream.
  */
 int mt_w4a16_gemm_workspace(int batch, int n, int k, int mode, long long* bytes);
 int mt_w4a16_gemm(const void* x, const void* qweight, const void* scales, const void* qzeros, void* y,
@@ -244,6 +245,21 @@ int mt_heads_greedy(const void* x, const void* residual, const void* norm_w, flo
                     void* best, void* ticket, int hidden_size, int n_text, int n_cb, int vocab,
                     int cb_offset, int n_vq, int delay_slot_id, int audio_end_id, int pad_code,
                     int text_owner, int flags, void* stream);
+
+/*
+ * Greedy selection of `batch` decode steps from precomputed head logits (text bf16
+ * [batch, n_text], audio bf16 [batch, n_cb * vocab]): argmax per codebook with the
+ * first-index tie rule, the text token through text_ids, the delay-pattern masks with each
+ * sequence's audio_length / delay_length (int64 [batch]). Writes next_ids int64
+ * [batch, 1 + n_vq]: this shard's codebooks, zeros for the others, the text token when
+ * text_owner != 0 (else zero). Replaces the sampling half of FastLLM._decode with greedy=True
+ * (src/moss_tts/_runtime/llm.py:276-287) for the batched decode step, whose logits come from
+ * one plain bf16 GEMM per head as the reference's F.linear (llm.py:271-274).
+ */
+int mt_heads_select(const void* text_logits, const void* audio_logits, const void* text_ids,
+                    const void* audio_length, const void* delay_length, void* next_ids, int batch,
+                    int n_text, int n_cb, int vocab, int cb_offset, int n_vq, int delay_slot_id,
+                    int audio_end_id, int pad_code, int text_owner, int flags, void* stream);
 
 #ifdef __cplusplus
 }

@@ -55,6 +55,7 @@ constexpr int kCodeWarp = 21;      // TMA loads of the 4-bit codes
 constexpr int kActWarp = 22;       // TMA loads of the activation chunks
 constexpr int kThreads = 23 * 32;
 constexpr int kMaxBatch = 128;
+constexpr int kMaxTiles = 4096;    // 128-row tiles per projection (n <= 524288)
 constexpr int kSlotCols = kChunk / 2;  // TMEM columns of one A slot (two bf16 per column)
 constexpr uint32_t kCodeBytes = kTileM * kChunk / 2;  // codes of one chunk of one tile
 constexpr int kTmemCols = 512;
@@ -482,7 +483,10 @@ static bool make_plan(int batch, int n, int k, int mode, Plan* p) {
   if (p->stages > kMaxStages) p->stages = kMaxStages;
   if (p->stages < 2) return false;
   p->smem = fixed + (size_t)p->stages * stage;
-  p->ticket_bytes = ((size_t)p->tiles * sizeof(unsigned) + 255) / 256 * 256;
+  // a fixed ticket region, so that calls of different shapes can share one workspace: one
+  // call's partials never overlap another call's tickets
+  if (p->tiles > kMaxTiles) return false;
+  p->ticket_bytes = (size_t)kMaxTiles * sizeof(unsigned);
   p->partial_bytes = (size_t)2 * p->ctas * batch * kTileM * sizeof(float);
   return true;
 }
@@ -545,8 +549,9 @@ cudaError_t gemm_error_word(int* value, bool clear) {
 
 using namespace mt;
 
-// Workspace bytes of mt_w4a16_gemm on the current device for this shape (tickets first,
-// then the contributions to tiles cut between CTAs). The workspace must be zero-filled once; calls leave the tickets zero.
+// Workspace bytes of mt_w4a16_gemm on the current device for this shape: a fixed 16 KB ticket
+// region, then the contributions to tiles cut between CTAs. Calls of different shapes may
+// share one workspace of the largest size when they are ordered on one stream. The workspace must be zero-filled once; calls leave the tickets zero.
 MT_API int mt_w4a16_gemm_workspace(int batch, int n, int k, int mode, long long* bytes) {
   tc::Plan p;
   if (!bytes || (mode & ~4) || !tc::make_plan(batch, n, k, mode, &p)) return kBadArgument;

@@ -31,6 +31,7 @@ SIGNATURES = {
     "mt_w4a16_linear_packed_tp": ([_P, _P, _P, _F, _P, _P, _I, _P, _I, _I, _I, _P, _P, _I, _P], _I),
     "mt_w4a16_gemm_workspace": ([_I, _I, _I, _I, _LLP], _I),
     "mt_w4a16_gemm": ([_P, _P, _P, _P, _P, _I, _I, _I, _I, _P, _I, _P], _I),
+    "mt_heads_select": ([_P, _P, _P, _P, _P, _P] + [_I] * 11 + [_P], _I),
     "mt_bf16_linear": ([_P, _P, _P, _F, _P, _P, _P, _I, _I, _I, _I, _I, _P], _I),
     "mt_rmsnorm": ([_P, _P, _P, _P, _P, _I, _I, _F, _I, _P], _I),
     "mt_silu_mul": ([_P, _P, _I, _I, _I, _P], _I),
