@@ -16,9 +16,10 @@
 //   (B x 256 bf16 in four 64-column boxes with the 128-byte swizzle: the canonical K-major
 //   SWIZZLE_128B operand layout; rows past B read as zeros). The code loads do not depend
 //   on the previous kernel and start before griddepcontrol.wait.
-// * The dequantised weights never touch shared memory: sixteen dequantisation warps (warp w
-//   owns TMEM lanes 32 (w % 4) .. +31, one weight row per thread, and one quarter of each K
-//   chunk) read their row's codes from the stage (conflict-free thanks to the swizzle), their
+// * The dequantised weights never touch shared memory: sixteen dequantisation warps in two
+//   groups taking alternate chunks (so one group computes while the other waits; in a group
+//   warp w owns TMEM lanes 32 (w % 4) .. +31, one weight row per thread, and one half of the
+//   chunk's K) read their row's codes from the stage (conflict-free thanks to the swizzle), their
 //   scales and zero points from L1-cached loads issued three chunks ahead, turn each code pair
 //   into an exact bf16 pair (bf16(128 + q) by bit insertion, minus bf16(128 + z) exactly,
 //   times the bf16 scale with one round to nearest: the oracle's bf16((q - z) * s) bit for
@@ -48,7 +49,7 @@ constexpr int kTileM = 128;        // weight rows per tile = TMEM lanes
 constexpr int kChunk = 256;        // K elements per pipeline stage
 constexpr int kMaxSlots = 3;       // TMEM A slots (3 when the batch fits 64 columns, else 2)
 constexpr int kMaxStages = 8;      // shared-memory stages (codes + activations) in flight
-constexpr int kDequantWarps = 16;  // warp w: TMEM lane quarter w % 4, K quarter w / 4
+constexpr int kDequantWarps = 16;  // two groups of 8 (alternate chunks); lane quarter w % 4, K half (w / 4) % 2
 constexpr int kMmaWarp = 16;
 constexpr int kEpiWarp0 = 17;      // warps 17..20 read the accumulators
 constexpr int kCodeWarp = 21;      // TMA loads of the 4-bit codes
@@ -166,8 +167,8 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
 }
 
 struct RowLoads {
-  uint32_t s;     // two bf16 scales (groups 2j, 2j + 1)
-  uint32_t z;     // zero-point byte (low nibble group 2j)
+  uint2 s;        // four bf16 scales (the groups of half a chunk)
+  uint32_t z;     // two zero-point bytes (low nibble first)
 };
 
 __device__ __forceinline__ int range_start(int b, long work, int ctas) { return (int)((long)b * work / ctas); }
@@ -218,7 +219,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     if (lane == 0) {
       for (int i = 0; i < kMaxSlots; ++i) {
-        mbar_init(&full[i], kDequantWarps * 32);
+        mbar_init(&full[i], kDequantWarps / 2 * 32);  // one group's lanes
         mbar_init(&aempty[i], 1);
       }
       for (int i = 0; i < kMaxStages; ++i) {
@@ -241,20 +242,21 @@ __global__ void __launch_bounds__(kThreads, 1)
   pdl_trigger();
 
   if (warp < kDequantWarps) {
-    const int q = warp & 3, h = warp >> 2, m = 32 * q + lane;
-    // scales and zero points: L1-cached loads three chunks ahead (a 32-byte sector serves 4 / 16 chunks)
+    // Two groups of eight warps take alternate chunks (group g: chunks g, g + 2, ...), so one
+    // group dequantises while the other waits on its barriers; in a group, warp w covers TMEM
+    // lane quarter w % 4 (one weight row per thread) and half (w / 4) % 2 of the chunk's K.
+    const int q = warp & 3, h = (warp >> 2) & 1, grp = warp >> 3, m = 32 * q + lane;
+    // scales and zero points: L1-cached loads two of the group's chunks ahead
     auto load = [&](int j, RowLoads& r) {
       if (j < nwork) {
         const int w = w0 + j, tile = w / chunks, c = w - tile * chunks;
         const int row = PAIRED ? (m < 64 ? tile * 64 + m : n_out + tile * 64 + (m - 64)) : tile * kTileM + m;
-        r.s = __ldg(reinterpret_cast<const uint32_t*>(a.scales + (size_t)row * (K / 32) + c * 8 + h * 2));
-        r.z = a.qzeros ? (uint32_t)__ldg(a.qzeros + (size_t)row * (K / 64) + c * 4 + h) : 0x88u;
+        r.s = __ldg(reinterpret_cast<const uint2*>(a.scales + (size_t)row * (K / 32) + c * 8 + h * 4));
+        r.z = a.qzeros ? (uint32_t)__ldg(reinterpret_cast<const uint16_t*>(a.qzeros + (size_t)row * (K / 64) + c * 4 +
+                                                                           h * 2))
+                       : 0x8888u;
       }
     };
-    RowLoads buf[4];
-    load(0, buf[0]);
-    load(1, buf[1]);
-    load(2, buf[2]);
     // weights are never written by a predecessor: no dependency wait before streaming them
     const uint32_t t_lane = (uint32_t)(32 * q) << 16;
     const int sw = m & 7;  // 128-byte swizzle of row m: 16-byte piece p sits at p ^ sw
@@ -270,47 +272,50 @@ __global__ void __launch_bounds__(kThreads, 1)
       ok = mbar_wait_bounded(&wfull[st], (unsigned)((j / nst) & 1)) && ok;
       if (!ok) abort_s = 1;
       const uint8_t* cs = smem + st * stage_bytes + code_off;
-      const uint4 c0 = *reinterpret_cast<const uint4*>(cs + (((2 * h) ^ sw) << 4));
-      const uint4 c1 = *reinterpret_cast<const uint4*>(cs + (((2 * h + 1) ^ sw) << 4));
-      // dequantise 64 codes -> 32 bf16 pairs: code word i holds k = 8i .. 8i + 7
-      const uint32_t zlo = r.z & 0xF, zhi = (r.z >> 4) & 0xF;
-      const uint32_t zz0 = (0x4300u + zlo) * 0x10001u, zz1 = (0x4300u + zhi) * 0x10001u;
-      const uint32_t s0 = (r.s & 0xFFFFu) * 0x10001u, s1 = (r.s >> 16) * 0x10001u;
-      const uint32_t cw[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
-      uint32_t v[32];
+      const uint32_t ta = tmem + t_lane + (uint32_t)(a_col0 + slot * kSlotCols + h * 64);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const uint32_t u = cw[i], hi = u >> 4;
-        const uint32_t zz = i < 4 ? zz0 : zz1, ss = i < 4 ? s0 : s1;
+      for (int half = 0; half < 2; ++half) {  // 64 codes -> 32 bf16 pairs, twice
+        const int p0 = 4 * h + 2 * half;
+        const uint4 c0 = *reinterpret_cast<const uint4*>(cs + ((p0 ^ sw) << 4));
+        const uint4 c1 = *reinterpret_cast<const uint4*>(cs + (((p0 + 1) ^ sw) << 4));
+        const uint32_t zb = (r.z >> (8 * half)) & 0xFF;
+        const uint32_t zz0 = (0x4300u + (zb & 0xF)) * 0x10001u, zz1 = (0x4300u + (zb >> 4)) * 0x10001u;
+        const uint32_t sp = half ? r.s.y : r.s.x;
+        const uint32_t s0 = (sp & 0xFFFFu) * 0x10001u, s1 = (sp >> 16) * 0x10001u;
+        const uint32_t cw[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+        uint32_t v[32];
 #pragma unroll
-        for (int b = 0; b < 4; ++b) {
-          const uint32_t t = (prmt(u, hi, 0x0400u + 0x0101u * b) & 0x000F000Fu) | 0x43004300u;
-          v[4 * i + b] = bf16x2_mul(bf16x2_sub(t, zz), ss);
+        for (int i = 0; i < 8; ++i) {  // code word i holds k = 8i .. 8i + 7
+          const uint32_t u = cw[i], hi = u >> 4;
+          const uint32_t zz = i < 4 ? zz0 : zz1, ss = i < 4 ? s0 : s1;
+#pragma unroll
+          for (int b = 0; b < 4; ++b) {
+            const uint32_t t = (prmt(u, hi, 0x0400u + 0x0101u * b) & 0x000F000Fu) | 0x43004300u;
+            v[4 * i + b] = bf16x2_mul(bf16x2_sub(t, zz), ss);
+          }
         }
+        __syncwarp();
+        tmem_st16(ta + 32 * half, v);
+        tmem_st16(ta + 32 * half + 16, v + 16);
       }
-      const uint32_t ta = tmem + t_lane + (uint32_t)(a_col0 + slot * kSlotCols + h * 32);
-      __syncwarp();
-      tmem_st16(ta, v);
-      tmem_st16(ta + 16, v + 16);
       asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
       tc_fence_before();
       mbar_arrive(&full[slot]);
     };
+    RowLoads buf[3];
+    load(grp, buf[0]);
+    load(grp + 2, buf[1]);
 #pragma unroll 1
-    for (int j = 0; j < nwork; j += 4) {
-      load(j + 3, buf[3]);
+    for (int j = grp; j < nwork; j += 6) {
+      load(j + 4, buf[2]);
       process(j, buf[0]);
-      if (j + 1 < nwork) {
-        load(j + 4, buf[0]);
-        process(j + 1, buf[1]);
-      }
       if (j + 2 < nwork) {
-        load(j + 5, buf[1]);
-        process(j + 2, buf[2]);
+        load(j + 6, buf[0]);
+        process(j + 2, buf[1]);
       }
-      if (j + 3 < nwork) {
-        load(j + 6, buf[2]);
-        process(j + 3, buf[3]);
+      if (j + 4 < nwork) {
+        load(j + 8, buf[1]);
+        process(j + 4, buf[2]);
       }
     }
   } else if (warp == kMmaWarp) {
@@ -569,7 +574,9 @@ MT_API int mt_w4a16_gemm(const void* x, const void* qweight, const void* scales,
   tc::Plan p;
   if (!x || !qweight || !scales || !y || !workspace || (mode & ~4) || !tc::make_plan(batch, n, k, mode, &p))
     return kBadArgument;
-  if (!aligned(x, 16) || !aligned(qweight, 16) || !aligned(scales, 4) || !aligned(workspace, 256)) return kBadArgument;
+  if (!aligned(x, 16) || !aligned(qweight, 16) || !aligned(scales, 8) || (qzeros && !aligned(qzeros, 2)) ||
+      !aligned(workspace, 256))
+    return kBadArgument;
   tc::GemmArgs a;
   a.x = (const __nv_bfloat16*)x;
   a.qweight = (const uint8_t*)qweight;

@@ -308,12 +308,23 @@ def _rope(device, length):
 
 
 def test_rope_tables_match_transformers():
+    """Bit-exact against transformers' Qwen3 rotary embedding evaluated in this process (both
+    use torch's fp32 pow / cos / sin on this host's CPU, whose last bits can differ between
+    CPUs); against the fixture made on another host, at most one bf16 ulp anywhere."""
+    from transformers import Qwen3Config
+    from transformers.models.qwen3 import modeling_qwen3
     from moss_tts._runtime.engine import rope_tables
     g = golden("ops")
     cos, sin = rope_tables(4096)
     pos = torch.from_numpy(g["rope_positions"])
-    assert np.array_equal(cos[pos].view(torch.int16).numpy().view(np.uint16), g["rope_cos"])
-    assert np.array_equal(sin[pos].view(torch.int16).numpy().view(np.uint16), g["rope_sin"])
+    cfg = Qwen3Config(hidden_size=4096, intermediate_size=12288, num_hidden_layers=1, num_attention_heads=32,
+                      num_key_value_heads=8, head_dim=128, vocab_size=2048, rms_norm_eps=1e-6,
+                      rope_parameters={"rope_type": "default", "rope_theta": 1e6}, max_position_embeddings=8192)
+    c_ref, s_ref = modeling_qwen3.Qwen3RotaryEmbedding(cfg)(torch.zeros(1, dtype=torch.bfloat16), pos[None])
+    assert torch.equal(cos[pos], c_ref[0]) and torch.equal(sin[pos], s_ref[0])
+    for mine, fixture in ((cos[pos], g["rope_cos"]), (sin[pos], g["rope_sin"])):
+        ulps = np.abs(mine.view(torch.int16).numpy().astype(np.int32) - fixture.view(np.int16).astype(np.int32))
+        assert ulps.max() <= 1, ulps.max()
 
 
 @pytest.mark.parametrize("ctx", [0, 1, 31, 96, 777, 2048])
