@@ -49,6 +49,9 @@ def parse():
     ap.add_argument("--batch-sweep", default=None, metavar="B,B,...",
                     help="config 4: batched decode of B sequences with ragged contexts (uniform in "
                          "[256, 4096], seeded) for each listed B; prints one JSON line per B")
+    ap.add_argument("--profile-gemm", type=int, default=0, metavar="B",
+                    help="only launch the tcgen05 W4A16 GEMM on the fused gate/up shape with B rows "
+                         "(4 launches on random weights, for an ncu capture); prints its mean launch time")
     ap.add_argument("--profile-kernel", action="store_true",
                     help="only launch the dominant kernel (packed add+norm+gate/up+SiLU GEMV), once per "
                          "layer per step, for an ncu capture; prints its mean launch time")
@@ -267,6 +270,35 @@ def bf16_step_rate(args, cfg, dev, rank, world, group, max_length):
     return args.steps / (ms / 1000.0), ms / args.steps, step_bytes, status
 
 
+def profile_gemm(rows: int):
+    """The batched projection alone: mt_w4a16_gemm on gate/up (N = 24576, K = 4096, fused pair)
+    with `rows` activation rows, random codes / scales / zero points, 4 launches."""
+    import torch
+
+    from moss_tts._runtime import native
+
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(0)
+    n, k = 24576, 4096
+    qw = torch.randint(0, 256, (n, k // 2), dtype=torch.uint8, device=dev, generator=g)
+    sc = (torch.rand(n, k // 32, device=dev, generator=g) * 0.01 + 1e-4).to(torch.bfloat16)
+    qz = torch.randint(0, 256, (n, k // 64), dtype=torch.uint8, device=dev, generator=g)
+    x = torch.randn(rows, k, device=dev, generator=g).to(torch.bfloat16)
+    y = torch.empty(rows, n // 2, device=dev, dtype=torch.bfloat16)
+    ws = torch.zeros(native.w4a16_gemm_workspace(rows, n, k, native.LINEAR_PAIRED), dtype=torch.uint8, device=dev)
+    s = torch.cuda.current_stream(dev).cuda_stream
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    for i in range(4):
+        if i == 2:
+            e0.record()
+        native.call("mt_w4a16_gemm", x.data_ptr(), qw.data_ptr(), sc.data_ptr(), qz.data_ptr(), y.data_ptr(), rows,
+                    n, k, native.LINEAR_PAIRED, ws.data_ptr(), 0, s)
+    e1.record()
+    torch.cuda.synchronize(dev)
+    print(json.dumps({"kernel": "mt_w4a16_gemm gate/up", "rows": rows, "launch_us": round(e0.elapsed_time(e1) * 500, 2),
+                      "error_word": native.error_word(clear=True)}), flush=True)
+
+
 def batch_sweep(args, rank, world, local):
     """Config 4: W4A16 decode of B independent sequences per step, each with its own context
     length drawn uniformly from [256, 4096] (seeded), for every B of --batch-sweep. One step
@@ -376,6 +408,9 @@ def main():
         return
     if args.batch_sweep:
         batch_sweep(args, rank, world, local)
+        return
+    if args.profile_gemm:
+        profile_gemm(args.profile_gemm)
         return
     import torch
     import torch.distributed as dist

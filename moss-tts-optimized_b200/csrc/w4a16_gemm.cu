@@ -33,6 +33,7 @@
 // Every mbarrier wait is bounded; an expired wait sets an error word and the kernel still
 // drains, releases its TMEM and returns.
 #include <cuda.h>
+#include <string.h>
 #include <cudaTypedefs.h>
 
 #include "stream_pipeline.cuh"
@@ -59,6 +60,9 @@ constexpr int kMaxBatch = 128;
 constexpr int kMaxTiles = 4096;    // 128-row tiles per projection (n <= 524288)
 constexpr int kSlotCols = kChunk / 2;  // TMEM columns of one A slot (two bf16 per column)
 constexpr uint32_t kCodeBytes = kTileM * kChunk / 2;  // codes of one chunk of one tile
+constexpr uint32_t kScaleOff = kCodeBytes;            // [128 rows][8 bf16 scales]
+constexpr uint32_t kZeroOff = kScaleOff + kTileM * 16;  // [128 rows][16 zero-point bytes (4 chunks)]
+constexpr uint32_t kXOff = kZeroOff + kTileM * 16;      // activation boxes (1024-byte aligned)
 constexpr int kTmemCols = 512;
 
 struct GemmArgs {
@@ -70,6 +74,7 @@ struct GemmArgs {
   float* partial;                // [2 * grid][batch][128] contributions to cut tiles
   unsigned* tickets;             // [tiles], zero on entry and exit
   int batch, n, k, n_mma, tiles, chunks, stages;
+  int zt;             // zero points arrive by TMA with the codes ((k / 64) % 16 == 0), else per thread
   int d_cols, slots;  // accumulator columns (64 or 128) and TMEM A slots after the two accumulators
 };
 
@@ -167,8 +172,7 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
 }
 
 struct RowLoads {
-  uint2 s;        // four bf16 scales (the groups of half a chunk)
-  uint32_t z;     // two zero-point bytes (low nibble first)
+  uint32_t z;     // two zero-point bytes (low nibble first), when they do not arrive by TMA
 };
 
 __device__ __forceinline__ int range_start(int b, long work, int ctas) { return (int)((long)b * work / ctas); }
@@ -182,7 +186,8 @@ __device__ __forceinline__ int owner_of(int w, long work, int ctas) {
 
 template <bool PAIRED>
 __global__ void __launch_bounds__(kThreads, 1)
-    w4a16_gemm_tc(GemmArgs a, const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap wmap) {
+    w4a16_gemm_tc(GemmArgs a, const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap wmap,
+                  const __grid_constant__ CUtensorMap smap, const __grid_constant__ CUtensorMap zmap) {
   // dynamic shared memory, from the first 1024-byte boundary: [stages] x {codes [128][128 B]
   // (128-byte swizzle), activations [4][n_mma][64] bf16 (128-byte swizzle)}, then [16][64] f32
   // for the paired epilogue
@@ -208,7 +213,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int nseg = nwork > 0 ? (w1 - 1) / chunks - t_first + 1 : 0;
   const int nslot = a.slots, a_col0 = 2 * a.d_cols;
   const uint32_t x_bytes = (uint32_t)n_mma * kChunk * 2, x_box = (uint32_t)n_mma * 128;  // 64-column boxes
-  const uint32_t stage_bytes = kCodeBytes + x_bytes;
+  const uint32_t stage_bytes = kXOff + x_bytes;
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   float* exch = reinterpret_cast<float*>(smem + nst * stage_bytes);
 
@@ -251,10 +256,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (j < nwork) {
         const int w = w0 + j, tile = w / chunks, c = w - tile * chunks;
         const int row = PAIRED ? (m < 64 ? tile * 64 + m : n_out + tile * 64 + (m - 64)) : tile * kTileM + m;
-        r.s = __ldg(reinterpret_cast<const uint2*>(a.scales + (size_t)row * (K / 32) + c * 8 + h * 4));
-        r.z = a.qzeros ? (uint32_t)__ldg(reinterpret_cast<const uint16_t*>(a.qzeros + (size_t)row * (K / 64) + c * 4 +
-                                                                           h * 2))
-                       : 0x8888u;
+        if (a.qzeros && !a.zt)
+          r.z = (uint32_t)__ldg(reinterpret_cast<const uint16_t*>(a.qzeros + (size_t)row * (K / 64) + c * 4 + h * 2));
       }
     };
     // weights are never written by a predecessor: no dependency wait before streaming them
@@ -271,16 +274,23 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       ok = mbar_wait_bounded(&wfull[st], (unsigned)((j / nst) & 1)) && ok;
       if (!ok) abort_s = 1;
-      const uint8_t* cs = smem + st * stage_bytes + code_off;
+      const uint8_t* stage = smem + st * stage_bytes;
+      const uint8_t* cs = stage + code_off;
+      const uint2 sc = *reinterpret_cast<const uint2*>(stage + kScaleOff + m * 16 + h * 8);
+      uint32_t zpair = 0x8888u;
+      if (a.qzeros)
+        zpair = a.zt ? (uint32_t)*reinterpret_cast<const uint16_t*>(stage + kZeroOff + m * 16 +
+                                                                   (((w0 + j) % chunks) * 4 & 15) + h * 2)
+                     : r.z;
       const uint32_t ta = tmem + t_lane + (uint32_t)(a_col0 + slot * kSlotCols + h * 64);
 #pragma unroll
       for (int half = 0; half < 2; ++half) {  // 64 codes -> 32 bf16 pairs, twice
         const int p0 = 4 * h + 2 * half;
         const uint4 c0 = *reinterpret_cast<const uint4*>(cs + ((p0 ^ sw) << 4));
         const uint4 c1 = *reinterpret_cast<const uint4*>(cs + (((p0 + 1) ^ sw) << 4));
-        const uint32_t zb = (r.z >> (8 * half)) & 0xFF;
+        const uint32_t zb = (zpair >> (8 * half)) & 0xFF;
         const uint32_t zz0 = (0x4300u + (zb & 0xF)) * 0x10001u, zz1 = (0x4300u + (zb >> 4)) * 0x10001u;
-        const uint32_t sp = half ? r.s.y : r.s.x;
+        const uint32_t sp = half ? sc.y : sc.x;
         const uint32_t s0 = (sp & 0xFFFFu) * 0x10001u, s1 = (sp >> 16) * 0x10001u;
         const uint32_t cw[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
         uint32_t v[32];
@@ -322,7 +332,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // warp-uniform loop; one elected lane issues the MMAs and commits
     const uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n_mma >> 3) << 17) |
                            ((uint32_t)(kTileM >> 4) << 24);
-    const uint32_t b0 = smem_u32(smem) + kCodeBytes;
+    const uint32_t b0 = smem_u32(smem) + kXOff;
     int seg = -1;
     for (int j = 0; j < nwork; ++j) {
       const int w = w0 + j, c = w % chunks;
@@ -371,14 +381,20 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (elect_one()) {
         if (codes) {
           const int r0 = PAIRED ? tile * 64 : tile * kTileM, r1 = PAIRED ? n_out + tile * 64 : r0 + 64;
-          mbar_expect_tx(&wfull[st], kCodeBytes);
+          mbar_expect_tx(&wfull[st], kZeroOff + (a.zt ? kTileM * 16 : 0));
           tma_load_2d(base, &wmap, c * (kChunk / 2), r0, &wfull[st]);
           tma_load_2d(base + kCodeBytes / 2, &wmap, c * (kChunk / 2), r1, &wfull[st]);
+          tma_load_2d(base + kScaleOff, &smap, c * 8, r0, &wfull[st]);
+          tma_load_2d(base + kScaleOff + 64 * 16, &smap, c * 8, r1, &wfull[st]);
+          if (a.zt) {
+            tma_load_2d(base + kZeroOff, &zmap, (c * 4) & ~15, r0, &wfull[st]);
+            tma_load_2d(base + kZeroOff + 64 * 16, &zmap, (c * 4) & ~15, r1, &wfull[st]);
+          }
         } else {
           mbar_expect_tx(&xfull[st], x_bytes);
 #pragma unroll
           for (int bx = 0; bx < kChunk / 64; ++bx)
-            tma_load_2d(base + kCodeBytes + bx * x_box, &xmap, c * kChunk + 64 * bx, 0, &xfull[st]);
+            tma_load_2d(base + kXOff + bx * x_box, &xmap, c * kChunk + 64 * bx, 0, &xfull[st]);
         }
       }
       __syncwarp();
@@ -483,7 +499,7 @@ static bool make_plan(int batch, int n, int k, int mode, Plan* p) {
   p->slots = (kTmemCols - 2 * p->d_cols) / kSlotCols;
   const long work = (long)p->tiles * p->chunks;
   p->ctas = (int)(work < sm_count() ? work : sm_count());
-  const size_t stage = kCodeBytes + (size_t)p->n_mma * kChunk * 2, fixed = 1024 + 16 * 64 * sizeof(float);
+  const size_t stage = kXOff + (size_t)p->n_mma * kChunk * 2, fixed = 1024 + 16 * 64 * sizeof(float);
   p->stages = (int)((200 * 1024 - fixed) / stage);
   if (p->stages > kMaxStages) p->stages = kMaxStages;
   if (p->stages < 2) return false;
@@ -519,6 +535,21 @@ static bool code_map(CUtensorMap* map, const void* qweight, int n, int k) {
   const cuuint32_t estr[2] = {1, 1};
   return encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(qweight), dims, strides, box, estr,
                 CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// TMA map of a per-row table (scales [n, cols] bf16 or zero points [n, cols] bytes): boxes of
+// `box` elements (16 bytes) x 64 rows, no swizzle.
+static bool row_map(CUtensorMap* map, const void* base, CUtensorMapDataType type, int n, int cols, int elem,
+                    int box_cols) {
+  PFN_cuTensorMapEncodeTiled_v12000 encode = tensor_map_encoder();
+  if (!encode) return false;
+  const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)n};
+  const cuuint64_t strides[1] = {(cuuint64_t)cols * elem};
+  const cuuint32_t box[2] = {(cuuint32_t)box_cols, 64};
+  const cuuint32_t estr[2] = {1, 1};
+  return encode(map, type, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
@@ -574,7 +605,7 @@ MT_API int mt_w4a16_gemm(const void* x, const void* qweight, const void* scales,
   tc::Plan p;
   if (!x || !qweight || !scales || !y || !workspace || (mode & ~4) || !tc::make_plan(batch, n, k, mode, &p))
     return kBadArgument;
-  if (!aligned(x, 16) || !aligned(qweight, 16) || !aligned(scales, 8) || (qzeros && !aligned(qzeros, 2)) ||
+  if (!aligned(x, 16) || !aligned(qweight, 16) || !aligned(scales, 16) || (qzeros && !aligned(qzeros, 16)) ||
       !aligned(workspace, 256))
     return kBadArgument;
   tc::GemmArgs a;
@@ -594,11 +625,15 @@ MT_API int mt_w4a16_gemm(const void* x, const void* qweight, const void* scales,
   a.stages = p.stages;
   a.d_cols = p.d_cols;
   a.slots = p.slots;
-  alignas(64) CUtensorMap xmap, wmap;
-  if (!tc::activation_map(&xmap, x, batch, k, p.n_mma) || !tc::code_map(&wmap, qweight, n, k))
+  a.zt = qzeros && (k / 64) % 16 == 0;
+  alignas(64) CUtensorMap xmap, wmap, smap, zmap;
+  memset(&zmap, 0, sizeof(zmap));
+  if (!tc::activation_map(&xmap, x, batch, k, p.n_mma) || !tc::code_map(&wmap, qweight, n, k) ||
+      !tc::row_map(&smap, scales, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, n, k / 32, 2, 8) ||
+      (a.zt && !tc::row_map(&zmap, qzeros, CU_TENSOR_MAP_DATA_TYPE_UINT8, n, k / 64, 1, 16)))
     return (int)cudaErrorNotSupported;
   const dim3 grid(p.ctas), block(tc::kThreads);
   cudaStream_t s = (cudaStream_t)stream;
-  if (mode & 4) return (int)launch(tc::w4a16_gemm_tc<true>, grid, block, p.smem, s, flags & kFlagPdl, a, xmap, wmap);
-  return (int)launch(tc::w4a16_gemm_tc<false>, grid, block, p.smem, s, flags & kFlagPdl, a, xmap, wmap);
+  if (mode & 4) return (int)launch(tc::w4a16_gemm_tc<true>, grid, block, p.smem, s, flags & kFlagPdl, a, xmap, wmap, smap, zmap);
+  return (int)launch(tc::w4a16_gemm_tc<false>, grid, block, p.smem, s, flags & kFlagPdl, a, xmap, wmap, smap, zmap);
 }
