@@ -414,15 +414,18 @@ __global__ void __launch_bounds__(kAttnThreads) attention_cluster(AttnArgs a) {
   int c = 0;
   for (; c < chunks; ++c) {
     if (!__syncthreads_and(wait_slot(c) ? 1 : 0)) break;
+    // every thread is past chunk c - 1: its slot (and pr) may be reused
+    if (tid == 0 && c >= 1 && c + 1 < chunks) issue(c + 1);
     const int slot = c & 1, cs = t0 + c * kChunk, rows = min(kChunk, t1 - cs);
     const __nv_bfloat16* ks = reinterpret_cast<const __nv_bfloat16*>(sm + (size_t)slot * kSlotBytes);
     const __nv_bfloat16* vs = ks + (size_t)kChunk * kHeadDim;
-    if (owner && warp == REP && p >= cs && p < cs + rows) {  // this step's row, fresh
-      *reinterpret_cast<uint2*>(const_cast<__nv_bfloat16*>(ks) + (size_t)(p - cs) * kHeadDim + 4 * lane) = krow;
-      *reinterpret_cast<uint2*>(const_cast<__nv_bfloat16*>(vs) + (size_t)(p - cs) * kHeadDim + 4 * lane) = vrow;
-      __syncwarp();
+    if (owner && p >= cs && p < cs + rows) {  // the chunk holding this step's row (CTA-uniform)
+      if (warp == REP) {
+        *reinterpret_cast<uint2*>(const_cast<__nv_bfloat16*>(ks) + (size_t)(p - cs) * kHeadDim + 4 * lane) = krow;
+        *reinterpret_cast<uint2*>(const_cast<__nv_bfloat16*>(vs) + (size_t)(p - cs) * kHeadDim + 4 * lane) = vrow;
+      }
+      __syncthreads();
     }
-    __syncthreads();
     // logits: item = ((t * REP) + h) * 4 + quarter; four consecutive lanes share (t, h)
     const int items = rows * REP * 4;
     for (int base = 0; base < items; base += kAttnThreads) {
@@ -494,8 +497,6 @@ __global__ void __launch_bounds__(kAttnThreads) attention_cluster(AttnArgs a) {
         }
       }
     }
-    __syncthreads();  // every thread is done with this slot and with pr
-    if (tid == 0 && c + 2 < chunks) issue(c + 2);
   }
   if (c < chunks) {  // a copy did not land within the bound
     if (tid == 0) {

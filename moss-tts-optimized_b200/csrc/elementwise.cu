@@ -49,6 +49,79 @@ __global__ void __launch_bounds__(256) rmsnorm_rows(const __nv_bfloat16* __restr
     y[(size_t)row * n + i] = to_bf16(round_bf16(buf[i] * inv) * bf16f(w[i]));
 }
 
+// The same for rows of n % 8 == 0 elements (<= 256 * 8 * J): every thread issues all of its
+// 16-byte loads up front (x and residual) and keeps the row in registers, so a row costs one
+// memory round trip instead of one per element sweep.
+template <int J>
+__global__ void __launch_bounds__(256) rmsnorm_rows_v8(const __nv_bfloat16* __restrict__ x,
+                                                       const __nv_bfloat16* __restrict__ residual,
+                                                       const __nv_bfloat16* __restrict__ w,
+                                                       __nv_bfloat16* __restrict__ summed,
+                                                       __nv_bfloat16* __restrict__ y, int n, float eps) {
+  __shared__ float red[8];
+  const int row = blockIdx.x, tid = threadIdx.x, E = n >> 3;
+  pdl_wait();
+  pdl_trigger();
+  const uint4* xr = reinterpret_cast<const uint4*>(x + (size_t)row * n);
+  const uint4* rr = residual ? reinterpret_cast<const uint4*>(residual + (size_t)row * n) : nullptr;
+  uint4 xv[J], rv[J];
+#pragma unroll
+  for (int j = 0; j < J; ++j) {
+    const int e = tid + 256 * j;
+    xv[j] = e < E ? xr[e] : make_uint4(0, 0, 0, 0);
+    rv[j] = (rr && e < E) ? rr[e] : make_uint4(0, 0, 0, 0);
+  }
+  float v[J][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < J; ++j) {
+    const uint32_t xw[4] = {xv[j].x, xv[j].y, xv[j].z, xv[j].w}, rw[4] = {rv[j].x, rv[j].y, rv[j].z, rv[j].w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      v[j][2 * i] = bf16_lo(xw[i]);
+      v[j][2 * i + 1] = bf16_hi(xw[i]);
+      if (residual) {
+        v[j][2 * i] = round_bf16(v[j][2 * i] + bf16_lo(rw[i]));
+        v[j][2 * i + 1] = round_bf16(v[j][2 * i + 1] + bf16_hi(rw[i]));
+      }
+      ss += v[j][2 * i] * v[j][2 * i] + v[j][2 * i + 1] * v[j][2 * i + 1];
+    }
+    const int e = tid + 256 * j;
+    if (residual && summed && e < E) {
+      uint32_t o[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        __nv_bfloat162 p = __floats2bfloat162_rn(v[j][2 * i], v[j][2 * i + 1]);
+        o[i] = *reinterpret_cast<uint32_t*>(&p);
+      }
+      reinterpret_cast<uint4*>(summed + (size_t)row * n)[e] = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+  }
+  ss = warp_sum(ss);
+  if ((tid & 31) == 0) red[tid >> 5] = ss;
+  __syncthreads();
+  float tot = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) tot += red[i];
+  const float inv = 1.0f / sqrtf(tot / (float)n + eps);
+#pragma unroll
+  for (int j = 0; j < J; ++j) {
+    const int e = tid + 256 * j;
+    if (e >= E) continue;
+    const uint4 wv = reinterpret_cast<const uint4*>(w)[e];
+    const uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float a0 = round_bf16(round_bf16(v[j][2 * i] * inv) * bf16_lo(ww[i]));
+      const float a1 = round_bf16(round_bf16(v[j][2 * i + 1] * inv) * bf16_hi(ww[i]));
+      __nv_bfloat162 p = __floats2bfloat162_rn(a0, a1);
+      o[i] = *reinterpret_cast<uint32_t*>(&p);
+    }
+    reinterpret_cast<uint4*>(y + (size_t)row * n)[e] = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
 // SiLU(gate) rounded to bf16, times up (kernels.py:123-139); x is [rows, 2n].
 __global__ void silu_mul_rows(const __nv_bfloat16* __restrict__ x, __nv_bfloat16* __restrict__ y,
                               int rows, int n) {
@@ -135,6 +208,14 @@ MT_API int mt_abi_version(void) { return 1; }
 MT_API int mt_rmsnorm(const void* x, const void* residual, const void* weight, void* summed, void* y,
                       int rows, int n, float eps, int flags, void* stream) {
   if (!x || !weight || !y || rows < 1 || n < 1 || n > 16384) return kBadArgument;
+  const bool vec = n % 8 == 0 && aligned(x, 16) && aligned(weight, 16) && aligned(y, 16) &&
+                   (!residual || aligned(residual, 16)) && (!summed || aligned(summed, 16));
+  if (vec) {
+    auto k = n <= 256 * 8 * 2 ? rmsnorm_rows_v8<2> : rmsnorm_rows_v8<8>;
+    return launch(k, dim3(rows), dim3(256), 0, (cudaStream_t)stream, flags, (const __nv_bfloat16*)x,
+                  (const __nv_bfloat16*)residual, (const __nv_bfloat16*)weight, (__nv_bfloat16*)summed,
+                  (__nv_bfloat16*)y, n, eps);
+  }
   return launch(rmsnorm_rows, dim3(rows), dim3(256), (size_t)n * 4, (cudaStream_t)stream, flags,
                 (const __nv_bfloat16*)x, (const __nv_bfloat16*)residual, (const __nv_bfloat16*)weight,
                 (__nv_bfloat16*)summed, (__nv_bfloat16*)y, n, eps);

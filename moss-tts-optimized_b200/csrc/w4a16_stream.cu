@@ -643,9 +643,21 @@ static int stream_pipe() {
   return p;
 }
 
+// Pipeline shape of the small projections (at most 32 Mi weights: q|k|v and o_proj at
+// K = 4096): MT_W4_PIPE_SMALL, same values, default the shape of the large ones.
+static int stream_pipe_small() {
+  static int p = -1;
+  if (p < 0) {
+    const char* e = getenv("MT_W4_PIPE_SMALL");
+    p = (e && (!strcmp(e, "31") || !strcmp(e, "21") || !strcmp(e, "41") || !strcmp(e, "22"))) ? atoi(e)
+                                                                                              : stream_pipe();
+  }
+  return p;
+}
+
 template <bool NORM, bool ADD, bool PAIRED, int TPM = 0>
 static cudaError_t go_ns(const StreamArgs& a, cudaStream_t s, int flags) {
-  switch (stream_pipe()) {
+  switch ((long long)a.n * a.k <= (32LL << 20) ? stream_pipe_small() : stream_pipe()) {
     case 21: return go<2, 1, NORM, ADD, PAIRED, TPM>(a, s, flags);
     case 31: return go<3, 1, NORM, ADD, PAIRED, TPM>(a, s, flags);
     case 41: return go<4, 1, NORM, ADD, PAIRED, TPM>(a, s, flags);

@@ -1,4 +1,5 @@
-"""Tensor parallelism on real GPUs: TP=2/4/8 decode steps against the unsharded model.
+"""Tensor parallelism on real GPUs: TP=2/4/8 decode steps (batch 1 and a batch of 16 ragged
+sequences) against the unsharded model.
 
 Each world size is skipped unless that many GPUs are visible. The worker (tests/tp_worker.py) runs under
 torchrun with one rank per GPU; NCCL all-reduces after o_proj and down are captured in the
@@ -35,5 +36,7 @@ def test_tp_decode_matches_single_gpu(tmp_path, world):
     same = sum(s["ids_equal"] for s in rep["steps"])
     total = sum(s["ids"] for s in rep["steps"])
     assert same >= 0.97 * total, rep
-    for s in rep["steps"]:
+    for s in rep["steps"] + rep["batched"]:
         assert s["hidden_max_abs"] <= 5e-2 + 2e-2 * s["hidden_scale"], rep
+    same = sum(s["ids_equal"] for s in rep["batched"])
+    assert same >= 0.97 * sum(s["ids"] for s in rep["batched"]), rep

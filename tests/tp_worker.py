@@ -18,6 +18,7 @@ import torch.distributed as dist  # noqa: E402
 
 from moss_tts._runtime import synthetic  # noqa: E402
 from moss_tts._runtime.config import DecoderConfig, small_vocab  # noqa: E402
+from moss_tts._runtime.batch_engine import BatchDecodeEngine  # noqa: E402
 from moss_tts._runtime.engine import DecodeEngine, TensorParallel, shard_weights  # noqa: E402
 from moss_tts._runtime.weights import DecoderWeights  # noqa: E402
 
@@ -57,6 +58,33 @@ def main(out_path: str) -> None:
         ids = obj[0]
     report["status"] = int(eng.status.item())
     eng.graph = None  # graphs holding NCCL work go before the process group
+    # batched decode (tcgen05 GEMM projections, ragged contexts) through the same all-reduces
+    B, nkv = 16, cfg.num_kv_heads // world
+    beng = BatchDecodeEngine(shard_weights(full, rank, world), B, max_length=128, tp=tp)
+    bref = BatchDecodeEngine(full, B, max_length=128) if rank == 0 else None
+    g = torch.Generator(device=dev).manual_seed(11)
+    kv = torch.randn((2, 2, B, cfg.num_kv_heads, 128, 128), generator=g, device=dev).to(torch.bfloat16)
+    beng.kv.copy_(kv[:, :, :, rank * nkv:(rank + 1) * nkv])
+    if rank == 0:
+        bref.kv.copy_(kv)
+    pos = torch.arange(B) * 6 + 9
+    bids = torch.full((B, 33), 7, dtype=torch.long)
+    bids[:, 0] = 5
+    one, neg = torch.ones(B, dtype=torch.long), torch.full((B,), -1, dtype=torch.long)
+    report["batched"] = []
+    for step in range(2):
+        got = beng.step(bids, pos + step, one, neg).cpu()
+        if rank == 0:
+            want = bref.step(bids, pos + step, one, neg).cpu()
+            h_tp, h_1 = beng.hidden.float().cpu(), bref.hidden.float().cpu()
+            report["batched"].append({"ids_equal": int((got == want).sum()), "ids": int(got.numel()),
+                                      "hidden_max_abs": float((h_tp - h_1).abs().max()),
+                                      "hidden_scale": float(h_1.abs().max())})
+            bids = want
+        obj = [bids]
+        dist.broadcast_object_list(obj, src=0)
+        bids = obj[0]
+    report["status"] |= int(beng.status.item())
     dist.barrier()
     dist.destroy_process_group()
     if rank == 0:
