@@ -644,13 +644,13 @@ static int stream_pipe() {
 }
 
 // Pipeline shape of the small projections (at most 32 Mi weights: q|k|v and o_proj at
-// K = 4096): MT_W4_PIPE_SMALL, same values, default the shape of the large ones.
+// K = 4096): MT_W4_PIPE_SMALL, same values, default 21 (two stages of 16 blocks: the first
+// bytes arrive sooner; decode step 1.598 -> 1.583 ms against 22).
 static int stream_pipe_small() {
   static int p = -1;
   if (p < 0) {
     const char* e = getenv("MT_W4_PIPE_SMALL");
-    p = (e && (!strcmp(e, "31") || !strcmp(e, "21") || !strcmp(e, "41") || !strcmp(e, "22"))) ? atoi(e)
-                                                                                              : stream_pipe();
+    p = (e && (!strcmp(e, "31") || !strcmp(e, "21") || !strcmp(e, "41") || !strcmp(e, "22"))) ? atoi(e) : 21;
   }
   return p;
 }
