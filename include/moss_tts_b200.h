@@ -153,6 +153,20 @@ int mt_w4a16_gemm(const void* x, const void* qweight, const void* scales, const 
                   int batch, int n, int k, int mode, void* workspace, int flags, void* stream);
 
 /*
+ * Packed layout of the batched projection: mt_w4a16_gemm_pack repacks a GPTQ-layout
+ * projection once at load time (as the reference's install_packing,
+ * src/moss_tts/_runtime/dp4a_packing.py:128-160) into one contiguous 18,944-byte block per
+ * 128-row tile and 256-column chunk (mt_w4a16_gemm_pack_size bytes); mt_w4a16_gemm_packed is
+ * mt_w4a16_gemm over it (one bulk copy per chunk instead of row pieces), same results and
+ * workspace. Requires n % 128 == 0, k % 256 == 0, 16-byte aligned x / packed.
+ */
+int mt_w4a16_gemm_pack_size(int n, int k, int mode, long long* bytes);
+int mt_w4a16_gemm_pack(const void* qweight, const void* scales, const void* qzeros, int n, int k, int mode,
+                       void* packed, void* stream);
+int mt_w4a16_gemm_packed(const void* x, const void* packed, void* y, int batch, int n, int k, int mode,
+                         void* workspace, int flags, void* stream);
+
+/*
  * bf16-weight decode GEMV with the same modes as mt_w4a16_linear (w bf16 [n, k]).
  * Replaces linear_decode (src/moss_tts/_runtime/kernels.py:93-108) and the paired gate/up
  * SiLU GEMV fp8_silu_decode (src/moss_tts/_runtime/fused_mlp.py:7-30). Batch 1 with

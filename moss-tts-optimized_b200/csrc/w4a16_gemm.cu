@@ -63,6 +63,11 @@ constexpr uint32_t kCodeBytes = kTileM * kChunk / 2;  // codes of one chunk of o
 constexpr uint32_t kScaleOff = kCodeBytes;            // [128 rows][8 bf16 scales]
 constexpr uint32_t kZeroOff = kScaleOff + kTileM * 16;  // [128 rows][16 zero-point bytes (4 chunks)]
 constexpr uint32_t kXOff = kZeroOff + kTileM * 16;      // activation boxes (1024-byte aligned)
+// Packed layout (mt_w4a16_gemm_pack): one contiguous block per (tile, K chunk), tile-major, so a
+// CTA's work range is one contiguous byte range and each stage is one bulk copy.
+constexpr uint32_t kPackedZeroOff = kScaleOff + kTileM * 16;  // [128 rows][4 zero-point bytes]
+constexpr uint32_t kPackedBlock = kPackedZeroOff + kTileM * 4;  // 18,944 bytes
+constexpr uint32_t kPackedXOff = (kPackedBlock + 1023) / 1024 * 1024;
 constexpr int kTmemCols = 512;
 
 struct GemmArgs {
@@ -75,6 +80,7 @@ struct GemmArgs {
   unsigned* tickets;             // [tiles], zero on entry and exit
   int batch, n, k, n_mma, tiles, chunks, stages;
   int zt;             // zero points arrive by TMA with the codes ((k / 64) % 16 == 0), else per thread
+  const uint8_t* packed;  // packed layout: [tiles * chunks][kPackedBlock] (PACKED kernels)
   int d_cols, slots;  // accumulator columns (64 or 128) and TMEM A slots after the two accumulators
 };
 
@@ -184,7 +190,7 @@ __device__ __forceinline__ int owner_of(int w, long work, int ctas) {
   return b;
 }
 
-template <bool PAIRED>
+template <bool PAIRED, bool PACKED>
 __global__ void __launch_bounds__(kThreads, 1)
     w4a16_gemm_tc(GemmArgs a, const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap wmap,
                   const __grid_constant__ CUtensorMap smap, const __grid_constant__ CUtensorMap zmap) {
@@ -213,7 +219,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int nseg = nwork > 0 ? (w1 - 1) / chunks - t_first + 1 : 0;
   const int nslot = a.slots, a_col0 = 2 * a.d_cols;
   const uint32_t x_bytes = (uint32_t)n_mma * kChunk * 2, x_box = (uint32_t)n_mma * 128;  // 64-column boxes
-  const uint32_t stage_bytes = kXOff + x_bytes;
+  constexpr uint32_t kStageXOff = PACKED ? kPackedXOff : kXOff;
+  const uint32_t stage_bytes = kStageXOff + x_bytes;
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   float* exch = reinterpret_cast<float*>(smem + nst * stage_bytes);
 
@@ -256,7 +263,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (j < nwork) {
         const int w = w0 + j, tile = w / chunks, c = w - tile * chunks;
         const int row = PAIRED ? (m < 64 ? tile * 64 + m : n_out + tile * 64 + (m - 64)) : tile * kTileM + m;
-        if (a.qzeros && !a.zt)
+        if (!PACKED && a.qzeros && !a.zt)
           r.z = (uint32_t)__ldg(reinterpret_cast<const uint16_t*>(a.qzeros + (size_t)row * (K / 64) + c * 4 + h * 2));
       }
     };
@@ -278,7 +285,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint8_t* cs = stage + code_off;
       const uint2 sc = *reinterpret_cast<const uint2*>(stage + kScaleOff + m * 16 + h * 8);
       uint32_t zpair = 0x8888u;
-      if (a.qzeros)
+      if (PACKED)
+        zpair = *reinterpret_cast<const uint16_t*>(stage + kPackedZeroOff + m * 4 + h * 2);
+      else if (a.qzeros)
         zpair = a.zt ? (uint32_t)*reinterpret_cast<const uint16_t*>(stage + kZeroOff + m * 16 +
                                                                    (((w0 + j) % chunks) * 4 & 15) + h * 2)
                      : r.z;
@@ -332,7 +341,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // warp-uniform loop; one elected lane issues the MMAs and commits
     const uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n_mma >> 3) << 17) |
                            ((uint32_t)(kTileM >> 4) << 24);
-    const uint32_t b0 = smem_u32(smem) + kXOff;
+    const uint32_t b0 = smem_u32(smem) + kStageXOff;
     int seg = -1;
     for (int j = 0; j < nwork; ++j) {
       const int w = w0 + j, c = w % chunks;
@@ -379,7 +388,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t base = b0 + st * stage_bytes;
       __syncwarp();
       if (elect_one()) {
-        if (codes) {
+        if (codes && PACKED) {
+          mbar_expect_tx(&wfull[st], kPackedBlock);
+          bulk_copy(smem + st * stage_bytes, a.packed + (size_t)w * kPackedBlock, kPackedBlock, &wfull[st]);
+        } else if (codes) {
           const int r0 = PAIRED ? tile * 64 : tile * kTileM, r1 = PAIRED ? n_out + tile * 64 : r0 + 64;
           mbar_expect_tx(&wfull[st], kZeroOff + (a.zt ? kTileM * 16 : 0));
           tma_load_2d(base, &wmap, c * (kChunk / 2), r0, &wfull[st]);
@@ -394,7 +406,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           mbar_expect_tx(&xfull[st], x_bytes);
 #pragma unroll
           for (int bx = 0; bx < kChunk / 64; ++bx)
-            tma_load_2d(base + kXOff + bx * x_box, &xmap, c * kChunk + 64 * bx, 0, &xfull[st]);
+            tma_load_2d(base + kStageXOff + bx * x_box, &xmap, c * kChunk + 64 * bx, 0, &xfull[st]);
         }
       }
       __syncwarp();
@@ -484,12 +496,40 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// Load-time repack of a GPTQ-layout projection into the packed layout: per (tile, chunk) the
+// 128 rows' codes (16-byte pieces pre-swizzled as the 128-byte TMA swizzle would place them),
+// their 8 scales and 4 zero-point bytes (0x88 = zero point 8 without zero points). One thread
+// per (tile, chunk, row).
+template <bool PAIRED>
+__global__ void __launch_bounds__(256) w4a16_gemm_pack_kernel(const uint8_t* __restrict__ qweight,
+                                                              const __nv_bfloat16* __restrict__ scales,
+                                                              const uint8_t* __restrict__ qzeros,
+                                                              uint8_t* __restrict__ out, int n, int k, int tiles,
+                                                              int chunks) {
+  const long idx = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= (long)tiles * chunks * kTileM) return;
+  const int m = (int)(idx & (kTileM - 1));
+  const long tcw = idx >> 7;
+  const int tile = (int)(tcw / chunks), c = (int)(tcw % chunks);
+  const int n_out = PAIRED ? n / 2 : n;
+  const int row = PAIRED ? (m < 64 ? tile * 64 + m : n_out + tile * 64 + (m - 64)) : tile * kTileM + m;
+  uint8_t* blk = out + tcw * kPackedBlock;
+  const uint4* src = reinterpret_cast<const uint4*>(qweight + (size_t)row * (k / 2) + (size_t)c * (kChunk / 2));
+  uint4* dst = reinterpret_cast<uint4*>(blk + (size_t)m * (kChunk / 2));
+#pragma unroll
+  for (int p = 0; p < 8; ++p) dst[p ^ (m & 7)] = src[p];
+  *reinterpret_cast<uint4*>(blk + kScaleOff + m * 16) =
+      *reinterpret_cast<const uint4*>(scales + (size_t)row * (k / 32) + (size_t)c * 8);
+  *reinterpret_cast<uint32_t*>(blk + kPackedZeroOff + m * 4) =
+      qzeros ? *reinterpret_cast<const uint32_t*>(qzeros + (size_t)row * (k / 64) + (size_t)c * 4) : 0x88888888u;
+}
+
 struct Plan {
   int tiles, chunks, n_mma, ctas, stages, d_cols, slots;
   size_t smem, partial_bytes, ticket_bytes;
 };
 
-static bool make_plan(int batch, int n, int k, int mode, Plan* p) {
+static bool make_plan(int batch, int n, int k, int mode, Plan* p, bool packed = false) {
   const bool paired = mode & 4;
   if (batch < 1 || batch > kMaxBatch || k < kChunk || k % kChunk || n < kTileM || n % kTileM) return false;
   p->tiles = paired ? (n / 2) / 64 : n / kTileM;
@@ -499,7 +539,8 @@ static bool make_plan(int batch, int n, int k, int mode, Plan* p) {
   p->slots = (kTmemCols - 2 * p->d_cols) / kSlotCols;
   const long work = (long)p->tiles * p->chunks;
   p->ctas = (int)(work < sm_count() ? work : sm_count());
-  const size_t stage = kXOff + (size_t)p->n_mma * kChunk * 2, fixed = 1024 + 16 * 64 * sizeof(float);
+  const size_t stage = (packed ? kPackedXOff : kXOff) + (size_t)p->n_mma * kChunk * 2,
+               fixed = 1024 + 16 * 64 * sizeof(float);
   p->stages = (int)((200 * 1024 - fixed) / stage);
   if (p->stages > kMaxStages) p->stages = kMaxStages;
   if (p->stages < 2) return false;
@@ -610,6 +651,7 @@ MT_API int mt_w4a16_gemm(const void* x, const void* qweight, const void* scales,
     return kBadArgument;
   tc::GemmArgs a;
   a.x = (const __nv_bfloat16*)x;
+  a.packed = nullptr;
   a.qweight = (const uint8_t*)qweight;
   a.scales = (const __nv_bfloat16*)scales;
   a.qzeros = (const uint8_t*)qzeros;
@@ -634,6 +676,69 @@ MT_API int mt_w4a16_gemm(const void* x, const void* qweight, const void* scales,
     return (int)cudaErrorNotSupported;
   const dim3 grid(p.ctas), block(tc::kThreads);
   cudaStream_t s = (cudaStream_t)stream;
-  if (mode & 4) return (int)launch(tc::w4a16_gemm_tc<true>, grid, block, p.smem, s, flags & kFlagPdl, a, xmap, wmap, smap, zmap);
-  return (int)launch(tc::w4a16_gemm_tc<false>, grid, block, p.smem, s, flags & kFlagPdl, a, xmap, wmap, smap, zmap);
+  if (mode & 4) return (int)launch(tc::w4a16_gemm_tc<true, false>, grid, block, p.smem, s, flags & kFlagPdl, a, xmap, wmap, smap, zmap);
+  return (int)launch(tc::w4a16_gemm_tc<false, false>, grid, block, p.smem, s, flags & kFlagPdl, a, xmap, wmap, smap, zmap);
+}
+
+// Bytes of the packed layout of an [n, k] projection for mt_w4a16_gemm_packed (mode as
+// mt_w4a16_gemm): 18,944 bytes per 128-row tile and 256-column chunk.
+MT_API int mt_w4a16_gemm_pack_size(int n, int k, int mode, long long* bytes) {
+  tc::Plan p;
+  if (!bytes || (mode & ~4) || !tc::make_plan(1, n, k, mode, &p, true)) return kBadArgument;
+  *bytes = (long long)p.tiles * p.chunks * tc::kPackedBlock;
+  return 0;
+}
+
+// Load-time repack of a GPTQ-layout projection (qweight uint8 [n, k/2], scales bf16 [n, k/32],
+// qzeros uint8 [n, k/64] or NULL) into `packed` (mt_w4a16_gemm_pack_size bytes, 16-byte
+// aligned): each (tile, chunk) of the batched GEMM becomes one contiguous block, so the kernel
+// fetches it with one bulk copy instead of hundreds of row pieces. Same role as the
+// reference's load-time install_packing (src/moss_tts/_runtime/dp4a_packing.py:128-160).
+MT_API int mt_w4a16_gemm_pack(const void* qweight, const void* scales, const void* qzeros, int n, int k, int mode,
+                              void* packed, void* stream) {
+  tc::Plan p;
+  if (!qweight || !scales || !packed || (mode & ~4) || !tc::make_plan(1, n, k, mode, &p, true)) return kBadArgument;
+  if (!aligned(qweight, 16) || !aligned(scales, 16) || (qzeros && !aligned(qzeros, 4)) || !aligned(packed, 16))
+    return kBadArgument;
+  const long threads = (long)p.tiles * p.chunks * tc::kTileM;
+  const dim3 grid((unsigned)((threads + 255) / 256));
+  auto k_ = (mode & 4) ? tc::w4a16_gemm_pack_kernel<true> : tc::w4a16_gemm_pack_kernel<false>;
+  return (int)launch(k_, grid, dim3(256), 0, (cudaStream_t)stream, 0, (const uint8_t*)qweight,
+                     (const __nv_bfloat16*)scales, (const uint8_t*)qzeros, (uint8_t*)packed, n, k, p.tiles, p.chunks);
+}
+
+// mt_w4a16_gemm over the packed layout (mt_w4a16_gemm_pack): same arguments and results, the
+// weights given as `packed`; the workspace is the one of mt_w4a16_gemm_workspace.
+MT_API int mt_w4a16_gemm_packed(const void* x, const void* packed, void* y, int batch, int n, int k, int mode,
+                                void* workspace, int flags, void* stream) {
+  tc::Plan p;
+  if (!x || !packed || !y || !workspace || (mode & ~4) || !tc::make_plan(batch, n, k, mode, &p, true))
+    return kBadArgument;
+  if (!aligned(x, 16) || !aligned(packed, 16) || !aligned(workspace, 256)) return kBadArgument;
+  tc::GemmArgs a;
+  memset(&a, 0, sizeof(a));
+  a.x = (const __nv_bfloat16*)x;
+  a.packed = (const uint8_t*)packed;
+  a.y = (__nv_bfloat16*)y;
+  a.tickets = (unsigned*)workspace;
+  a.partial = (float*)((uint8_t*)workspace + p.ticket_bytes);
+  a.batch = batch;
+  a.n = n;
+  a.k = k;
+  a.n_mma = p.n_mma;
+  a.tiles = p.tiles;
+  a.chunks = p.chunks;
+  a.stages = p.stages;
+  a.d_cols = p.d_cols;
+  a.slots = p.slots;
+  alignas(64) CUtensorMap xmap, none;
+  memset(&none, 0, sizeof(none));
+  if (!tc::activation_map(&xmap, x, batch, k, p.n_mma)) return (int)cudaErrorNotSupported;
+  const dim3 grid(p.ctas), block(tc::kThreads);
+  cudaStream_t s = (cudaStream_t)stream;
+  if (mode & 4)
+    return (int)launch(tc::w4a16_gemm_tc<true, true>, grid, block, p.smem, s, flags & kFlagPdl, a, xmap, none, none,
+                       none);
+  return (int)launch(tc::w4a16_gemm_tc<false, true>, grid, block, p.smem, s, flags & kFlagPdl, a, xmap, none, none,
+                     none);
 }

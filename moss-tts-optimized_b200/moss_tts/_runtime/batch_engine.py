@@ -14,7 +14,8 @@ length and delay length (ragged static KV caches). Per step, all PDL-chained and
            F.linear heads), greedy ids + delay masks per sequence  -> next_ids [B, 33]
 
 Projections: one sequence runs the batch-1 packed GEMV; from ``gemm_min_batch`` rows the
-W4A16 projections run on the tcgen05 GEMM (``mt_w4a16_gemm``) after a separate RMSNorm;
+W4A16 projections run on the tcgen05 GEMM over its load-time packed layout
+(``mt_w4a16_gemm_pack`` / ``mt_w4a16_gemm_packed``) after a separate RMSNorm;
 below it the GPTQ-layout GEMV with its fused norm prologue (``mt_w4a16_linear``, up to 8
 rows). Inputs live in one int64 control block ``[ids B*33 | positions B | audio_length B |
 delay_length B]`` (one host-to-device copy per step); the result is ``next_ids``.
@@ -79,10 +80,17 @@ class BatchDecodeEngine:
         self.next_ids = torch.zeros(B, CONTROL_IDS, device=dev, dtype=torch.long)
         self.status = torch.zeros(1, device=dev, dtype=torch.int32)
         ws = 256
+        self.packed = {}  # id(projection) -> packed layout of the tcgen05 GEMM (repacked once)
         if self.gemm:
-            for lw in weights.layers[:1]:
+            s = torch.cuda.current_stream(dev).cuda_stream
+            for lw in weights.layers:
                 for p, paired in ((lw.qkv, False), (lw.out, False), (lw.gate_up, True), (lw.down, False)):
-                    ws = max(ws, native.w4a16_gemm_workspace(B, p.n, p.k, native.LINEAR_PAIRED if paired else 0))
+                    mode = native.LINEAR_PAIRED if paired else 0
+                    ws = max(ws, native.w4a16_gemm_workspace(B, p.n, p.k, mode))
+                    t = torch.empty(native.w4a16_gemm_pack_size(p.n, p.k, mode), device=dev, dtype=torch.uint8)
+                    native.call("mt_w4a16_gemm_pack", p.qweight.data_ptr(), p.scales.data_ptr(), native.ptr(p.qzeros),
+                                p.n, p.k, mode, t.data_ptr(), s)
+                    self.packed[id(p)] = t
         self.gemm_workspace = torch.zeros(ws, device=dev, dtype=torch.uint8)
         self.graph = None
         self.graph_advance = None
@@ -100,9 +108,8 @@ class BatchDecodeEngine:
                 native.call("mt_rmsnorm", x.data_ptr(), native.ptr(residual), norm.data_ptr(), native.ptr(summed),
                             self.normed.data_ptr(), B, x.shape[-1], eps, self.flags, s)
                 x = self.normed
-            native.call("mt_w4a16_gemm", x.data_ptr(), p.qweight.data_ptr(), p.scales.data_ptr(),
-                        native.ptr(p.qzeros), y.data_ptr(), B, p.n, p.k, native.LINEAR_PAIRED if paired else 0,
-                        self.gemm_workspace.data_ptr(), self.flags, s)
+            native.call("mt_w4a16_gemm_packed", x.data_ptr(), self.packed[id(p)].data_ptr(), y.data_ptr(), B, p.n,
+                        p.k, native.LINEAR_PAIRED if paired else 0, self.gemm_workspace.data_ptr(), self.flags, s)
             return
         mode = (native.LINEAR_NORM if norm is not None else 0) | (native.LINEAR_ADD if residual is not None else 0)
         mode |= native.LINEAR_PAIRED if paired else 0

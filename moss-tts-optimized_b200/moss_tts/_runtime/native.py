@@ -32,6 +32,9 @@ SIGNATURES = {
     "mt_w4a16_gemm_workspace": ([_I, _I, _I, _I, _LLP], _I),
     "mt_w4a16_gemm": ([_P, _P, _P, _P, _P, _I, _I, _I, _I, _P, _I, _P], _I),
     "mt_heads_select": ([_P, _P, _P, _P, _P, _P] + [_I] * 11 + [_P], _I),
+    "mt_w4a16_gemm_pack_size": ([_I, _I, _I, _LLP], _I),
+    "mt_w4a16_gemm_pack": ([_P, _P, _P, _I, _I, _I, _P, _P], _I),
+    "mt_w4a16_gemm_packed": ([_P, _P, _P, _I, _I, _I, _I, _P, _I, _P], _I),
     "mt_bf16_linear": ([_P, _P, _P, _F, _P, _P, _P, _I, _I, _I, _I, _I, _P], _I),
     "mt_rmsnorm": ([_P, _P, _P, _P, _P, _I, _I, _F, _I, _P], _I),
     "mt_silu_mul": ([_P, _P, _I, _I, _I, _P], _I),
@@ -98,6 +101,13 @@ def w4a16_gemm_workspace(batch: int, n: int, k: int, mode: int) -> int:
     """Workspace bytes of mt_w4a16_gemm for this shape on the current device."""
     b = ctypes.c_longlong(0)
     call("mt_w4a16_gemm_workspace", batch, n, k, mode, ctypes.byref(b))
+    return b.value
+
+
+def w4a16_gemm_pack_size(n: int, k: int, mode: int) -> int:
+    """Bytes of the batched GEMM's packed layout of an [n, k] projection."""
+    b = ctypes.c_longlong(0)
+    call("mt_w4a16_gemm_pack_size", n, k, mode, ctypes.byref(b))
     return b.value
 
 

@@ -210,6 +210,41 @@ def test_tcgen05_gemm_matches_oracle(cuda_device, n, k, paired, zeros, batch):
     assert np.array_equal(outs[0], outs[1]) and np.array_equal(outs[0], outs[2])
 
 
+@pytest.mark.parametrize("n,k,paired,zeros,batch", [
+    (24576, 4096, True, True, 32), (4096, 12288, False, True, 16), (768, 4096, False, False, 9),
+    (4096, 1536, False, True, 64), (256, 256, True, True, 17)])
+def test_tcgen05_gemm_packed_layout_matches_gptq_layout(cuda_device, n, k, paired, zeros, batch):
+    """The load-time packed layout gives bitwise the same results as the GPTQ layout (same
+    arithmetic, different staging), and both match the oracle."""
+    from moss_tts._runtime import native
+    rng = np.random.Generator(np.random.PCG64(3 * n + k + batch))
+    p = synthetic.quantized(rng, n, k, 32, zeros)
+    qw, sc, qz = upload_w4(p, cuda_device)
+    mode = native.LINEAR_PAIRED if paired else 0
+    packed = torch.empty(native.w4a16_gemm_pack_size(n, k, mode), dtype=torch.uint8, device=cuda_device)
+    s = torch.cuda.current_stream().cuda_stream
+    native.call("mt_w4a16_gemm_pack", qw.data_ptr(), sc.data_ptr(), native.ptr(qz), n, k, mode, packed.data_ptr(), s)
+    xb = synthetic.activation(61 + batch, (batch, k))
+    x = dev_bf16(xb, cuda_device)
+    ws = torch.zeros(native.w4a16_gemm_workspace(batch, n, k, mode), dtype=torch.uint8, device=cuda_device)
+    n_out = n // 2 if paired else n
+    y_gptq = torch.empty((batch, n_out), device=cuda_device, dtype=torch.bfloat16)
+    native.call("mt_w4a16_gemm", x.data_ptr(), qw.data_ptr(), sc.data_ptr(), native.ptr(qz), y_gptq.data_ptr(),
+                batch, n, k, mode, ws.data_ptr(), 0, s)
+    outs = []
+    for flags in (0, 1):
+        y = torch.empty_like(y_gptq)
+        native.call("mt_w4a16_gemm_packed", x.data_ptr(), packed.data_ptr(), y.data_ptr(), batch, n, k, mode,
+                    ws.data_ptr(), flags, s)
+        outs.append(host_bits(y))
+    torch.cuda.synchronize()
+    assert native.error_word(clear=True) == 0
+    assert np.array_equal(outs[0], host_bits(y_gptq)) and np.array_equal(outs[0], outs[1])
+    ref = ops.linear(from_bf16_bits(xb), quant.dequantize_w4(p["qweight"], p["scales"], p["qzeros"]))
+    close(outs[0], ops.silu_mul(ref) if paired else ref)
+    assert int(ws[:16384].view(torch.int32).abs().sum()) == 0
+
+
 def test_tcgen05_gemm_shapes_share_one_workspace(cuda_device):
     """Projections of different shapes interleaved on one workspace (as the batched decode step
     uses it): every call still matches the oracle."""
