@@ -270,6 +270,17 @@ int mt_heads_greedy(const void* x, const void* residual, const void* norm_w, flo
  * (src/moss_tts/_runtime/llm.py:276-287) for the batched decode step, whose logits come from
  * one plain bf16 GEMM per head as the reference's F.linear (llm.py:271-274).
  */
+/*
+ * Device-side advance after a decode step of `batch` sequences: control int64
+ * [ids batch*n_ids | positions batch | audio_length batch | delay_length batch] takes
+ * next_ids [batch, n_ids] as its ids; positions and audio lengths advance by one; a sequence
+ * whose next text token is delay_slot_id starts its delay count (0), and a started count
+ * advances by one. Replaces first_audio_graph._advance (src/moss_tts/_runtime/
+ * first_audio_graph.py:14-27) as one launch.
+ */
+int mt_decode_advance(void* control, const void* next_ids, int n_ids, int batch, int delay_slot_id, int flags,
+                      void* stream);
+
 int mt_heads_select(const void* text_logits, const void* audio_logits, const void* text_ids,
                     const void* audio_length, const void* delay_length, void* next_ids, int batch,
                     int n_text, int n_cb, int vocab, int cb_offset, int n_vq, int delay_slot_id,

@@ -122,6 +122,29 @@ __global__ void __launch_bounds__(256) rmsnorm_rows_v8(const __nv_bfloat16* __re
   }
 }
 
+// Device-side advance of `batch` decode steps (first_audio_graph._advance,
+// src/moss_tts/_runtime/first_audio_graph.py:14-27): control int64 [ids batch*n_ids | positions
+// batch | audio_length batch | delay_length batch] takes next_ids [batch, n_ids] as its ids,
+// positions and audio lengths advance by one, and a sequence whose text token is the delay slot
+// starts its delay count, which then advances by one per step.
+__global__ void __launch_bounds__(256) decode_advance(int64_t* __restrict__ control,
+                                                      const int64_t* __restrict__ next_ids, int n_ids, int batch,
+                                                      int delay_slot_id) {
+  pdl_wait();
+  pdl_trigger();
+  const int tid = threadIdx.x;
+  for (int i = tid; i < batch * n_ids; i += blockDim.x) control[i] = next_ids[i];
+  for (int b = tid; b < batch; b += blockDim.x) {
+    int64_t* pos = control + (size_t)batch * n_ids;
+    pos[b] += 1;                       // position
+    pos[batch + b] += 1;               // audio_length
+    int64_t d = pos[2 * batch + b];    // delay_length
+    if (d < 0 && next_ids[(size_t)b * n_ids] == delay_slot_id) d = 0;
+    if (d >= 0) d += 1;
+    pos[2 * batch + b] = d;
+  }
+}
+
 // SiLU(gate) rounded to bf16, times up (kernels.py:123-139); x is [rows, 2n].
 __global__ void silu_mul_rows(const __nv_bfloat16* __restrict__ x, __nv_bfloat16* __restrict__ y,
                               int rows, int n) {
@@ -246,4 +269,15 @@ MT_API int mt_embedding_sum(const void* ids, const void* text, const void* audio
   return launch(embedding_sum_rows, grid, dim3(64), 0, (cudaStream_t)stream, flags,
                 (const int64_t*)ids, (const __nv_bfloat16*)text, (const __nv_bfloat16*)audio,
                 (__nv_bfloat16*)out, h, vocab, audio_vocab, n_vq, (int*)status);
+}
+
+// Device-side state advance after a decode step, for `batch` sequences (one launch instead of
+// the reference's handful of tensor operations in first_audio_graph._advance,
+// src/moss_tts/_runtime/first_audio_graph.py:14-27). control int64
+// [ids batch*n_ids | positions batch | audio_length batch | delay_length batch].
+MT_API int mt_decode_advance(void* control, const void* next_ids, int n_ids, int batch, int delay_slot_id,
+                             int flags, void* stream) {
+  if (!control || !next_ids || n_ids < 1 || batch < 1 || batch > 65536) return kBadArgument;
+  return launch(decode_advance, dim3(1), dim3(256), 0, (cudaStream_t)stream, flags, (int64_t*)control,
+                (const int64_t*)next_ids, n_ids, batch, delay_slot_id);
 }

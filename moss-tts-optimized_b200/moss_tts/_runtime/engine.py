@@ -271,15 +271,10 @@ class DecodeEngine:
 
     def launch_advance(self) -> None:
         """Device-side state advance after a step (feed next_ids back, position += 1, delay
-        bookkeeping as ``first_audio_graph._advance``, ``first_audio_graph.py:14-27``)."""
-        self.ids.copy_(self.next_ids)
-        self.position.add_(1)
-        self.audio_length.add_(1)
-        text = self.next_ids[:1]
-        d = self.delay_length
-        start = (d < 0) & (text == self.cfg.audio_assistant_delay_slot_token_id)
-        d.copy_(torch.where(start, torch.zeros_like(d), d))
-        d.copy_(torch.where(d >= 0, d + 1, d))
+        bookkeeping as ``first_audio_graph._advance``, ``first_audio_graph.py:14-27``), one launch."""
+        native.call("mt_decode_advance", self.control.data_ptr(), self.next_ids.data_ptr(), CONTROL_IDS, 1,
+                    self.cfg.audio_assistant_delay_slot_token_id, self.flags,
+                    torch.cuda.current_stream(self.device).cuda_stream)
 
     # ------------------------------------------------------------------ graphs
     def capture(self, advance: bool = False) -> None:

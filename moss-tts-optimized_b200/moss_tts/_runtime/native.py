@@ -35,6 +35,7 @@ SIGNATURES = {
     "mt_w4a16_gemm_pack_size": ([_I, _I, _I, _LLP], _I),
     "mt_w4a16_gemm_pack": ([_P, _P, _P, _I, _I, _I, _P, _P], _I),
     "mt_w4a16_gemm_packed": ([_P, _P, _P, _I, _I, _I, _I, _P, _I, _P], _I),
+    "mt_decode_advance": ([_P, _P, _I, _I, _I, _I, _P], _I),
     "mt_bf16_linear": ([_P, _P, _P, _F, _P, _P, _P, _I, _I, _I, _I, _I, _P], _I),
     "mt_rmsnorm": ([_P, _P, _P, _P, _P, _I, _I, _F, _I, _P], _I),
     "mt_silu_mul": ([_P, _P, _I, _I, _I, _P], _I),

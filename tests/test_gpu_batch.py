@@ -139,3 +139,25 @@ def test_heads_select_matches_host_argmax(cuda_device):
             want = int(np.argmax(a[b, ch - 8])) if valid else 1024
             assert out[b, 1 + ch] == want, (b, ch)
     assert out[0, 1 + 8] == 3
+
+
+def test_decode_advance_matches_reference_bookkeeping(cuda_device):
+    """mt_decode_advance against first_audio_graph._advance's tensor arithmetic for a batch:
+    ids fed back, positions and audio lengths + 1, delay counts started on the delay-slot text
+    token and advanced once started."""
+    B, n, slot = 6, 33, 153
+    rng = np.random.Generator(np.random.PCG64(8))
+    nxt = torch.from_numpy(rng.integers(0, 1000, size=(B, n))).long()
+    nxt[[1, 3], 0] = slot
+    ids = torch.from_numpy(rng.integers(0, 1000, size=(B, n))).long()
+    pos = torch.tensor([5, 9, 100, 7, 0, 31])
+    alen = torch.tensor([1, 2, 33, 4, 5, 6])
+    delay = torch.tensor([-1, -1, 3, 0, 32, -1])
+    control = torch.cat([ids.reshape(-1), pos, alen, delay]).to(cuda_device)
+    native.call("mt_decode_advance", control.data_ptr(), nxt.to(cuda_device).data_ptr(), n, B, slot, 0,
+                torch.cuda.current_stream().cuda_stream)
+    got = control.cpu()
+    d = torch.where((delay < 0) & (nxt[:, 0] == slot), torch.zeros_like(delay), delay)
+    d = torch.where(d >= 0, d + 1, d)
+    want = torch.cat([nxt.reshape(-1), pos + 1, alen + 1, d])
+    assert torch.equal(got, want)
