@@ -288,7 +288,8 @@ __global__ void __launch_bounds__(128) attention_decode(AttnArgs a) {
 constexpr int kClusterCtas = 8;
 // Tokens per streamed chunk: 128 for one sequence (latency: one CTA per SM is enough), 32
 // for batches (four CTAs share an SM, so one CTA's fixed latency overlaps the others' streams;
-// at 64 sequences x 2,200 tokens: 128 -> 21.1 ms, 64 -> 16.8 ms, 32 -> 15.1 ms per step).
+// at 64 sequences x 2,200 tokens: 128 -> 21.1 ms, 64 -> 16.8 ms, 32 -> 15.1 ms per step; one
+// sequence at 512+ tokens: 128 -> 1.536 ms, 64 -> 1.600 ms, 32 -> 1.690 ms per step).
 constexpr int kAttnThreads = 256;               // 8 warps per CTA (16 measured no faster)
 constexpr int kTokenGroups = kAttnThreads / 64;  // P.V token groups of 64 dim-pair threads
 
