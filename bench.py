@@ -124,54 +124,86 @@ def gate_up_bytes(k: int, n: int) -> int:
 
 
 # ---------------------------------------------------------------------------- CPU leg
-def cpu_oracle_sample(steps: int = 4, layers: int = 1):
-    """Time the numpy oracle (the reference's algorithm restated, cached dequantized weights,
-    all BLAS threads) on ``layers`` full-width layers + the 32-codebook heads, and scale the
-    per-layer time to 36 layers. Returns (steps/s of the full model, sample description)."""
+def workload_config(layers: int, world: int, max_length: int) -> dict:
+    """The config-3 workload both arms time (identical dict in the GPU line and the reference line)."""
+    return {"workload": "config3: 36-layer 8B-shaped decoder, W4A16 G32 (zero points), batch-1 greedy "
+                        "decode, prompt 512 (synthetic KV), positions 512+",
+            "layers": layers, "hidden": 4096, "intermediate": 12288,
+            "heads": "32x1024 audio rows + 2-row audio-phase text head (FastLLM._decode)",
+            "parallelism": f"tp{world}", "max_length": max_length,
+            "l2": "inputs larger than L2: ~4.4 GB of weights streamed per step"}
+
+
+def max_length_for(args) -> int:
+    return max(1024, ((PROMPT + args.warmup + args.steps + 1 + 127) // 128) * 128)
+
+
+def cpu_threads() -> int:
+    return len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
+
+
+def cpu_oracle_run(layers: int, steps: int, warmup: int, threads: int):
+    """Decode steps of the numpy oracle -- the reference's decode step restated on the CPU --
+    over the whole config-3 model: ``layers`` distinct random-init W4A16 G32 layers (zero
+    points), dequantized once to fp32 up front (the reference's CPU path keeps dequantized
+    weights), the 32 x 1024 audio heads and the 2-row text head, a synthetic 512-token KV
+    prefix; ``warmup`` untimed then ``steps`` timed steps at positions 512, 513, ...
+    Returns (steps/s, seconds of set-up)."""
     import numpy as np
+    from threadpoolctl import threadpool_limits
 
     from oracle import model as omodel
-    from oracle import ops
     from moss_tts._runtime import synthetic
     from moss_tts._runtime.config import DecoderConfig, small_vocab
 
-    cfg = small_vocab(DecoderConfig(), vocab=2048, layers=layers)
-    host = synthetic.decoder_weights(cfg, seed=11)
-    dec = omodel.Decoder(host, cfg.as_dict(), max_length=PROMPT + steps + 8)
-    rng = np.random.Generator(np.random.PCG64(12))
-    kv = rng.standard_normal((layers, 8, PROMPT, 128), dtype=np.float32)
-    dec.fill_cache(kv, kv)
-    ids = np.full(33, 5, dtype=np.int64)
-    t_layers, t_heads = [], []
-    for s in range(steps):
-        t0 = time.perf_counter()
-        h = dec.hidden(ids, PROMPT + s)
+    t0 = time.perf_counter()
+    with threadpool_limits(limits=threads):
+        cfg = small_vocab(DecoderConfig(), vocab=2048, layers=layers)
+        host = synthetic.decoder_weights(cfg, seed=11)
+        dec = omodel.Decoder(host, cfg.as_dict(), max_length=PROMPT + warmup + steps + 8, threads=threads)
+        del host
+        rng = np.random.Generator(np.random.PCG64(12))
+        kv = rng.standard_normal((layers, 8, PROMPT, 128), dtype=np.float32)
+        dec.fill_cache(kv, kv)
+        del kv
+        setup = time.perf_counter() - t0
+        ids = np.full(33, 17, dtype=np.int64)
+        ids[0] = cfg.audio_assistant_gen_slot_token_id
+        pos = PROMPT
+        for _ in range(warmup):
+            ids = dec.step(ids, pos, 1, -1)[0]
+            pos += 1
         t1 = time.perf_counter()
-        ops.heads_greedy(h, dec.text_head, dec.audio_heads, dec.text_ids, 32, -1, 0, 0)
-        t2 = time.perf_counter()
-        t_layers.append((t1 - t0) / layers)
-        t_heads.append(t2 - t1)
-    per_step = statistics.median(t_layers) * 36 + statistics.median(t_heads)
-    sample = (f"numpy oracle, cached dequantized weights, {layers} of 36 layers + 32x1024 audio heads "
-              f"+ 2-row text head, {steps} steps at ctx {PROMPT}+, per-layer time x36")
-    return 1.0 / per_step, sample
+        for _ in range(steps):
+            ids = dec.step(ids, pos, 1, -1)[0]
+            pos += 1
+        elapsed = time.perf_counter() - t1
+    return steps / elapsed, setup
 
 
-def run_reference(args, rank):
+def cpu_sample_text(layers: int, steps: int, threads: int) -> str:
+    return (f"numpy oracle (the reference's decode step restated), all {layers} layers distinct, dequantized "
+            f"fp32 weights cached, 32x1024 audio heads + 2-row text head, {steps} timed steps at ctx "
+            f"{PROMPT}+, {threads} BLAS threads")
+
+
+def run_reference(args, rank, world):
+    """--impl reference: the reference's CPU algorithm for the decode step (the numpy port; the
+    reference's own CUDA/Triton kernels are SM90-only and its package is not installable on the
+    GPU box) on all host threads, over the same config-3 workload, K timed steps after W warm-up
+    steps. Under torchrun only rank 0 runs it; the other ranks exit without work."""
     if rank != 0:
         return
-    threads = os.cpu_count() or 1
-    os.environ.setdefault("OMP_NUM_THREADS", str(threads))
-    steps = max(1, min(args.steps, 8))
-    cpu_oracle_sample(steps=max(1, min(args.warmup, 2)), layers=1)  # warm-up
-    value, sample = cpu_oracle_sample(steps=steps, layers=1)
+    threads = cpu_threads()
+    value, setup = cpu_oracle_run(args.layers, args.steps, args.warmup, threads)
+    sample = cpu_sample_text(args.layers, args.steps, threads)
     line = {"metric": METRIC, "value": round(value, 4), "unit": UNIT, "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1000 / value, 3),
-            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic", "impl": "reference",
-            "config": {"workload": "config3: 36-layer 8B W4A16 G32 batch-1 decode, prompt 512"},
+            "config": workload_config(args.layers, world, max_length_for(args)),
             "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": threads, "kind": "port",
-                             "sample": sample + f"; {steps} timed steps of the sample"},
+                             "sample": sample, "setup_s": round(setup, 1)},
             "e2e": {"value": round(value, 4), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -401,7 +433,7 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
-        run_reference(args, rank)
+        run_reference(args, rank, world)
         return
     if args.profile_kernel:
         profile_kernel(args)
@@ -430,7 +462,7 @@ def main():
         group = dist.group.WORLD
         dist.all_reduce(torch.ones(1, device=dev))  # NCCL communicator up before graph capture
     cfg = DecoderConfig().with_(num_layers=args.layers)
-    max_length = max(1024, ((PROMPT + args.warmup + args.steps + 1 + 127) // 128) * 128)
+    max_length = max_length_for(args)
     with torch.inference_mode():
         full = DecoderWeights.random(cfg, dev, seed=0, preset="gptq")
         weights = shard_weights(full, rank, world)
@@ -546,22 +578,19 @@ def main():
         dist.barrier()
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        os.environ.setdefault("OMP_NUM_THREADS", str(os.cpu_count() or 1))
-        v, sample = cpu_oracle_sample(steps=4, layers=1)
-        cpu = {"value": round(v, 4), "unit": UNIT, "cores": os.cpu_count(), "kind": "port", "sample": sample}
+        threads = cpu_threads()
+        cpu_steps = 3
+        v, setup = cpu_oracle_run(args.layers, cpu_steps, 1, threads)
+        cpu = {"value": round(v, 4), "unit": UNIT, "cores": threads, "kind": "port",
+               "sample": cpu_sample_text(args.layers, cpu_steps, threads), "setup_s": round(setup, 1)}
     launches = 2 + 5 * args.layers
     line = {
         "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": "config3: 36-layer 8B-shaped decoder, W4A16 G32 (zero points), batch-1 greedy "
-                               "decode, prompt 512 (synthetic KV), positions 512+",
-                   "layers": args.layers, "hidden": cfg.hidden_size, "intermediate": cfg.intermediate_size,
-                   "heads": "32x1024 audio rows + 2-row audio-phase text head (FastLLM._decode)",
-                   "parallelism": f"tp{world}", "max_length": max_length,
-                   "l2": "inputs larger than L2: ~4.4 GB of weights streamed per step",
-                   "step_bytes_per_gpu": step_bytes,
-                   "hbm_roofline_frac": round(step_bytes / (ms / args.steps * 1e-3) / 1e9 / peak, 4)},
+        "config": workload_config(args.layers, world, max_length),
+        "step_bytes_per_gpu": step_bytes,
+        "hbm_roofline_frac": round(step_bytes / (ms / args.steps * 1e-3) / 1e9 / peak, 4),
         "e2e": {"value": round(e2e_value, 3), "unit": UNIT, "h2d_bytes_per_step": 36 * 8,
                 "d2h_bytes_per_step": 33 * 8},
         "roofline": {"bound": "hbm", "kernel": "mt_w4a16_linear_packed (add+RMSNorm+gate/up+SiLU, N=%d K=%d)" % (lw0.n, lw0.k),

@@ -45,8 +45,9 @@ int mt_abi_version(void);
 /*
  * Diagnostic: copies the library's error word for the current device into *value (1 after a
  * kernel abandoned a bounded wait on its own asynchronous copies, then drained them and
- * returned early; 0 otherwise) and clears it when `clear` is non-zero. This one call is
- * synchronous. No counterpart in the reference (its kernels never wait).
+ * returned early; 2 after a tensor-parallel exchange gave up waiting for a peer; 0 otherwise)
+ * and clears it when `clear` is non-zero. This one call is synchronous. No counterpart in the
+ * reference (its kernels never wait).
  */
 int mt_read_error_word(int* value, int clear);
 
@@ -57,6 +58,13 @@ int mt_read_error_word(int* value, int clear);
  */
 int mt_dequant_w4(const void* qweight, const void* scales, const void* qzeros, void* out,
                   int n, int k, int group, void* stream);
+
+/*
+ * Static G32 scales of a weight matrix w [n, k] (dtype 0 = bf16, 1 = fp32, 2 = fp16):
+ * out bf16 [n, k / 32] = bf16(max(absmax of the group, 1e-8) / 7). Offline calibration.
+ * Replaces calibrated_quant.static_scales (src/moss_tts/_runtime/calibrated_quant.py:36-38).
+ */
+int mt_static_scales(const void* w, int dtype, void* out, int n, int k, void* stream);
 
 /*
  * W4A16 G32 decode GEMV, batch 1..8: y[b, :] = bf16(x'[b, :] . W^T) with fp32 accumulation,
@@ -110,17 +118,20 @@ int mt_w4a16_linear_packed(const void* x, const void* residual, const void* norm
 /*
  * Tensor-parallel exchange over peer memory (NVLink), replacing the NCCL all-reduce after a
  * row-parallel projection for mt_w4a16_linear_packed_tp. Every rank owns a receive area of
- * [slots][world][slot_elems / 2] 8-byte cells {bf16 pair, uint32 flag}, mapped on every rank
+ * [slots][world][slot_elems / 2] 64-bit cells (flag << 32 | bf16 pair), mapped on every rank
  * (the caller's symmetric allocation); `recv` lists the areas by rank. Each cell is written
- * with one 8-byte store, which is single-copy atomic, so a reader that sees this step's flag
- * sees this step's data: no fences, counters or atomics.
+ * and read as one 64-bit element, which is single-copy atomic, so a reader that sees this
+ * step's flag sees this step's data: no fences, counters or atomics.
  *   out_slot >= 0: the producer writes its output rows into recv[r][out_slot][rank] of every
  *                  rank r (flag = low 32 bits of *epoch) -- plain stores, no TMA multicast;
  *   in_slot >= 0:  the consumer polls its recv[rank][in_slot][r] cells until every flag equals
- *                  *epoch (bounded), and uses x = bf16(sum over ranks r in order) in place of `x`.
+ *                  *epoch, and uses x = bf16(sum over ranks r in order) in place of `x`.
+ * The poll of one call is bounded by a 100 ms deadline for the whole kernel: a cell still stale
+ * then (a dead or late peer) sets error word 2 (mt_read_error_word), the kernel finishes with
+ * what it read, and later calls give up at once while the word is 2.
  * `epoch` is the caller's device step counter, incremented once per step on every rank before
  * the step's first exchange. No reference counterpart: the reference is single-GPU; this is
- * the all-reduce of its tensor-parallel row (SURVEY's TP row).
+ * the all-reduce after o_proj and down of a Megatron-style tensor-parallel decoder.
  */
 #define MT_TP_MAX_RANKS 8
 typedef struct mt_tp_exchange {
@@ -135,6 +146,47 @@ int mt_w4a16_linear_packed_tp(const void* x, const void* residual, const void* n
                               void* summed, const void* packed, int has_zeros, void* y, int n, int k,
                               int mode, void* workspace, const mt_tp_exchange* tp, int flags,
                               void* stream);
+
+/*
+ * The decode step's whole layer stack in one persistent launch (batch 1, single GPU). Runs,
+ * for every layer, RMSNorm + q|k|v, QK-norm + RoPE + K/V cache write + attention over rows
+ * 0..position, o_proj, add + RMSNorm + gate/up + SiLU·up and down -- the body of the
+ * reference's FastLLM.hidden (src/moss_tts/_runtime/llm.py:227-260; with the gptq preset
+ * qkv_cluster_model.Hidden, qkv_cluster_model.py:50-72) -- as one kernel with one CTA per SM
+ * whose producer warps stream every layer's packed weights without a break.
+ * `layers` is a DEVICE array of n_layers mt_decode_layer entries (16-byte aligned): packed
+ * projections from mt_w4a16_pack (q|k|v [6144, 4096] and o [4096, 4096] and down
+ * [4096, inter] with mode 0, gate/up [2 inter, 4096] with MT_LINEAR_PAIRED), bf16 norm
+ * weights, and the layer's caches k/v bf16 [8, max_len, 128]. The shapes are those of the
+ * MOSS-TTS 8B backbone: hidden 4096, 32 query and 8 KV heads of 128; inter % 256 == 0.
+ * x = the layer-0 input (embedding sum) bf16 [4096]; positions int64 [1]; cos/sin bf16
+ * [max_len, 128]. Outputs: residual bf16 [4096] (the residual stream before the last MLP
+ * add) and mlp_out bf16 [4096] (the last down projection) -- the x / residual inputs of
+ * mt_heads_greedy. `workspace` (mt_decode_layers_workspace bytes, 256-byte aligned) is
+ * zero-filled by the caller once; every successful call leaves its counters zero again. A
+ * call whose bounded waits expire (status below) leaves it dirty: zero it before reuse.
+ * mt_read_error_word reports 1 (a copy wait expired) or 3 (a grid barrier expired). Calls
+ * sharing a workspace must be ordered on one stream. A position outside [0, max_len) sets
+ * *status = 1 (status may be NULL).
+ */
+typedef struct mt_decode_layer {
+  const void* qkv;
+  const void* out;
+  const void* gate_up;
+  const void* down;
+  const void* input_norm;
+  const void* post_norm;
+  const void* q_norm;
+  const void* k_norm;
+  void* k_cache;
+  void* v_cache;
+} mt_decode_layer;
+
+int mt_decode_layers_workspace(int n_layers, int inter, long long* bytes);
+int mt_decode_layers(const void* layers, int n_layers, int inter, int has_zeros, const void* x,
+                     const void* positions, const void* cos_tab, const void* sin_tab, int max_len,
+                     float eps, void* residual, void* mlp_out, void* workspace, void* status, int flags,
+                     void* stream);
 
 /*
  * Batched W4A16 G32 projection on the tcgen05 tensor cores (batch 1..128, meant for the
@@ -226,9 +278,9 @@ int mt_attention_decode(const void* qkv, const void* q_norm, const void* k_norm,
                         float eps, void* status, int flags, void* stream);
 
 /*
- * mt_attention_decode for callers that cannot allocate device memory: code enqueueing
- * work during CUDA-graph stream capture, real-time callbacks that must not block on an
- * allocator, and FFI hosts without a device allocator. No counterpart in the reference.
+ * mt_attention_decode for callers that cannot allocate device memory: real-time audio
+ * callbacks that must not block on an allocator, and plugin or FFI hosts that own no device
+ * allocator of their own. No counterpart in the reference.
  * The split-K scratch is a fixed array inside this library (about 1.04 MiB per GPU that
  * loads it, held until exit): batch*nkv*splits*(nq/nkv)*128 <= 262144 and
  * batch*nkv <= 1024, otherwise cudaErrorMemoryAllocation (2) is returned and nothing is

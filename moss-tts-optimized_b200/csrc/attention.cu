@@ -168,25 +168,26 @@ __global__ void __launch_bounds__(128) attention_decode(AttnArgs a) {
     return false;
   };
   const bool ok = n > 0 ? wait_copies() : true;
-  if (!__syncthreads_and(ok ? 1 : 0)) {
-    // The copies did not complete within the bound: raise the status, give them one more
-    // bounded chance to land (they target this CTA's shared memory), then leave this head
-    // unmerged.
+  const bool copied = __syncthreads_and(ok ? 1 : 0) != 0;
+  if (!copied) {
+    // The copies did not complete within the bound: raise the status and give them one more
+    // bounded chance to land (they target this CTA's shared memory). The split then counts as
+    // empty (zero partial, log-sum-exp -inf) but still takes its ticket below, so the head's
+    // counter returns to zero and the merge never starts before every split has reported.
     if (tid == 0) {
       if (a.status) atomicExch(a.status, 3);
       wait_copies();
     }
     __syncthreads();
-    return;
   }
-  if (owner && warp == 0) {
+  if (copied && owner && warp == 0) {
     *reinterpret_cast<uint2*>(ks + (size_t)(p - t0) * kHeadDim + 4 * lane) = krow;
     *reinterpret_cast<uint2*>(vs + (size_t)(p - t0) * kHeadDim + 4 * lane) = vrow;
   }
   __syncthreads();
 
   const size_t slot = (((size_t)b * a.nkv + kh) * a.splits + split) * REP;
-  if (n > 0) {
+  if (copied && n > 0) {
     // 4. logits: item (token t, head i) per thread; 16-byte chunks in rotated order.
     for (int item = tid; item < n * REP; item += 128) {
       const int t = item / REP, i = item - t * REP;
@@ -262,11 +263,12 @@ __global__ void __launch_bounds__(128) attention_decode(AttnArgs a) {
     float wsum = 0.f, acc = 0.f;
 #pragma unroll 8
     for (int s = 0; s < active; ++s) {
-      const float w = expf(__ldcg(a.lse + base + s * REP + i) - m);
+      const float l = __ldcg(a.lse + base + s * REP + i);
+      const float w = l == -INFINITY ? 0.f : expf(l - m);  // a failed split contributes nothing
       wsum += w;
       acc = fmaf(w, __ldcg(a.partial + (base + s * REP + i) * kHeadDim + tid), acc);
     }
-    a.out[(size_t)b * a.nq * kHeadDim + (kh * REP + i) * kHeadDim + tid] = to_bf16(acc / wsum);
+    a.out[(size_t)b * a.nq * kHeadDim + (kh * REP + i) * kHeadDim + tid] = to_bf16(wsum > 0.f ? acc / wsum : 0.f);
   }
   if (tid == 0) *ticket = 0u;
 }
@@ -716,9 +718,8 @@ MT_API int mt_qk_rope_kv(const void* qkv, const void* q_norm, const void* k_norm
 // Scratch-free decode attention.
 //
 // Some callers of this library cannot allocate device memory for the split-K
-// partials: code that enqueues work while a stream is being captured into a CUDA
-// graph (an allocation is not a stream operation and can break or serialise the
-// capture), real-time audio callbacks that must not block on an allocator, and
+// partials: real-time audio callbacks that must not block on an allocator (a
+// cudaMalloc can synchronise the device and stall for milliseconds), and
 // foreign-function hosts (plugins, embedded runtimes) that own no device
 // allocator at all. For them the partials, log-sum-exp values and merge tickets
 // live in one fixed array of this library's own device memory. Every GPU that

@@ -37,7 +37,7 @@
 
 #include <cuda_fp16.h>
 
-#include "stream_pipeline.cuh"
+#include "w4_tiles.cuh"
 
 namespace mt {
 
@@ -45,36 +45,6 @@ __device__ int g_error_word;  // non-zero after a bounded wait expired (see mt_r
 
 using namespace pipe;
 
-constexpr int kSliceCols = 256;   // input columns per slice block
-constexpr int kCodeBytes = 2048;  // 16 rows x 128 bytes
-constexpr int kScaleBytes = 256;  // 16 rows x 8 groups x bf16
-constexpr int kZeroBytes = 64;    // 16 rows x 8 groups x 4 bits
-
-struct PackGeom {
-  int n_out, rt, tiles, slices, block_b;
-  long long blocks;
-  PackGeom(int n, int k, bool zeros, bool paired) {
-    n_out = paired ? n / 2 : n;
-    rt = paired ? 8 : 16;
-    tiles = (n_out + rt - 1) / rt;
-    slices = k / kSliceCols;
-    block_b = kCodeBytes + kScaleBytes + (zeros ? kZeroBytes : 0);
-    blocks = (long long)tiles * slices;
-  }
-  size_t packed_bytes() const { return (size_t)blocks * block_b; }
-  static constexpr int kMaxCtas = 1024;  // workspace capacity: one slot per CTA boundary
-  static size_t workspace_bytes() { return (size_t)kMaxCtas * (2 * 16 * sizeof(float) + sizeof(int)); }
-};
-
-// Weight row held at tile row tr (0..15) of tile t, or -1 for padding past the last row.
-__host__ __device__ inline long long tile_row(int t, int tr, int n_out, bool paired) {
-  if (paired) {
-    const int o = t * 8 + (tr & 7);
-    return o < n_out ? (long long)o + (tr >= 8 ? n_out : 0) : -1;
-  }
-  const int o = t * 16 + tr;
-  return o < n_out ? o : -1;
-}
 
 // One warp per slice block; lane (r, c) writes its code chunks, scales and zero points.
 __global__ void w4a16_pack_blocks(const uint8_t* __restrict__ qweight, const uint16_t* __restrict__ scales,
@@ -121,85 +91,18 @@ struct StreamArgs {
   int tile_aligned;  // CTA ranges on whole tiles (no tile shared between CTAs)
   int pre_issue;     // stages copied before the dependency wait (the rest right after it)
   float eps;
-  // tensor-parallel exchange over peer memory (mt_tp_exchange), 8-byte cells {bf16 pair, flag}
+  // tensor-parallel exchange over peer memory (mt_tp_exchange): 64-bit cells {flag << 32 | bf16 pair}
   const uint2* tp_in;           // this rank's [world][k / 2] cells of the input slot, or null
   const long long* tp_epoch;    // device step counter: this step's flag
   int tp_world;
   uint2* tp_out[MT_TP_MAX_RANKS];  // rank r's [n_out / 2] cells for this rank's output, or null
 };
 
-// Codes as fp16 subnormals: (w & 0x000F000F) is the fp16 pair (q_j, q_{j+4}) * 2^-24 and
-// (w & 0x00F000F0) the pair 16 (q_{j+1}, q_{j+5}) * 2^-24, exactly (the tensor cores keep
-// fp16 subnormal operands). The matching activation slots carry x c and x c / 16.
-__device__ __forceinline__ void mma_f16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
-                                        uint32_t b0, uint32_t b1) {
-  asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
-      "{%0, %1, %2, %3};"
-      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-}
 
-__device__ __forceinline__ uint32_t pack_half2(float lo, float hi) {
-  __half2 h = __floats2half2_rn(lo, hi);
-  return *reinterpret_cast<uint32_t*>(&h);
-}
-
-// y row of tile row pair (gate = v, up = u) or plain row v (kernels.py / dp4a_packing.py:86-89).
-template <bool PAIRED>
-__device__ __forceinline__ float finish_row(float v, float u) {
-  if (!PAIRED) return v;
-  const float gate = round_bf16(v), up = round_bf16(u);
-  return round_bf16(gate / (1.0f + expf(-gate))) * up;
-}
-
-// Consumer-side dot product of one slice block (16 rows x 256 columns) against the B
-// fragments of its slice: returns the block's contribution to rows r (va) and r + 8 (vb),
-// already summed over the lane quad (lanes with c == 0 hold the row totals).
-struct BlockRegs {
-  uint4 c0, c1, c2, c3;  // codes: row r (c0, c1) and row r + 8 (c2, c3)
-  uint2 sw;              // scales: (s[r][2c], s[r][2c+1]) | (s[r+8][2c], s[r+8][2c+1])
-  uint32_t zz;           // zero points: groups 2c | 2c+1 of row r (low byte) and r + 8
-};
-
-__device__ __forceinline__ BlockRegs load_block(const uint8_t* blk, int lane, bool zeros) {
-  BlockRegs b;
-  b.c0 = *reinterpret_cast<const uint4*>(blk + lane * 16);
-  b.c1 = *reinterpret_cast<const uint4*>(blk + 512 + lane * 16);
-  b.c2 = *reinterpret_cast<const uint4*>(blk + 1024 + lane * 16);
-  b.c3 = *reinterpret_cast<const uint4*>(blk + 1536 + lane * 16);
-  b.sw = *reinterpret_cast<const uint2*>(blk + kCodeBytes + lane * 8);
-  b.zz = zeros ? (uint32_t)*reinterpret_cast<const uint16_t*>(blk + kCodeBytes + kScaleBytes + lane * 2) : 0x8888u;
-  return b;
-}
-
-__device__ __forceinline__ void block_dot(const BlockRegs& bk, const uint32_t (&bl)[16], const uint32_t (&bh)[16],
-                                          uint32_t bz0, uint32_t bz1, float& va, float& vb) {
-  const uint32_t wa[8] = {bk.c0.x, bk.c0.y, bk.c0.z, bk.c0.w, bk.c1.x, bk.c1.y, bk.c1.z, bk.c1.w};
-  const uint32_t wb[8] = {bk.c2.x, bk.c2.y, bk.c2.z, bk.c2.w, bk.c3.x, bk.c3.y, bk.c3.z, bk.c3.w};
-  float d[2][4] = {};  // two independent accumulators halve the mma dependency chains
-  // zero points: A = (z[r][2c], 16 z[r][2c+1]) (and row r + 8) as fp16 subnormals against
-  // B = -(c sum x) of groups 2c / 2c + 1 split into fp16 hi and lo parts
-  const uint32_t za = __byte_perm(bk.zz, 0, 0x4040) & 0x00F0000Fu, zb = __byte_perm(bk.zz, 0, 0x4141) & 0x00F0000Fu;
-  mma_f16(d[1], za, zb, za, zb, bz0, bz1);
-#pragma unroll
-  for (int u = 0; u < 8; ++u) {
-    const uint32_t* bsel = u < 4 ? bl : bh;
-    const int bi = (u & 3) * 4;
-    const uint32_t sa = wa[u] >> 8, sb = wb[u] >> 8;
-    mma_f16(d[0], wa[u] & 0x000F000Fu, wb[u] & 0x000F000Fu, wa[u] & 0x00F000F0u, wb[u] & 0x00F000F0u, bsel[bi],
-            bsel[bi + 1]);
-    mma_f16(d[1], sa & 0x000F000Fu, sb & 0x000F000Fu, sa & 0x00F000F0u, sb & 0x00F000F0u, bsel[bi + 2], bsel[bi + 3]);
-  }
-  // column 2c = group 2c (element 0: row r, element 2: row r + 8), column 2c + 1 = group 2c + 1
-  va = fmaf(__uint_as_float(bk.sw.x & 0xFFFF0000u), d[0][1] + d[1][1], __uint_as_float(bk.sw.x << 16) * (d[0][0] + d[1][0]));
-  vb = fmaf(__uint_as_float(bk.sw.y & 0xFFFF0000u), d[0][3] + d[1][3], __uint_as_float(bk.sw.y << 16) * (d[0][2] + d[1][2]));
-  va += __shfl_xor_sync(0xffffffffu, va, 1);
-  vb += __shfl_xor_sync(0xffffffffu, vb, 1);
-  va += __shfl_xor_sync(0xffffffffu, va, 2);
-  vb += __shfl_xor_sync(0xffffffffu, vb, 2);
-}
-
-constexpr int kWarps = 16;  // consumer warps per CTA
+// Longest time one kernel polls its tensor-parallel input cells before it gives up, raises
+// error word 2 and computes with what it has (a dead or late peer; far above the microseconds
+// a healthy exchange takes).
+constexpr unsigned long long kExchangeDeadlineNs = 100ull * 1000 * 1000;
 
 // NS ring stages of kWarps * BPW slice blocks; consumer warp w takes blocks w + 16 m
 // (m < BPW) of every stage, which share one slice when S divides 16.
@@ -220,6 +123,7 @@ __global__ void __launch_bounds__(kWarps * 32 + 32, 1) w4a16_packed(StreamArgs a
   __shared__ float redw[kWarps];
   __shared__ __align__(16) uint4 zero16[4];
   __shared__ int failed;
+  __shared__ volatile int tp_failed;
   constexpr int RT = PAIRED ? 8 : 16;  // output rows per tile
   constexpr int consumers = kWarps * 32;
   constexpr int SB = kWarps * BPW;     // slice blocks per stage
@@ -261,6 +165,7 @@ __global__ void __launch_bounds__(kWarps * 32 + 32, 1) w4a16_packed(StreamArgs a
       mbar_init(&empty[s], kWarps);
     }
     failed = 0;
+    tp_failed = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     // weights never depend on the previous kernel: start streaming before the PDL wait
     for (int st = 0; st < a.pre_issue && st < NS && st < stages; ++st) issue(st);
@@ -315,6 +220,7 @@ __global__ void __launch_bounds__(kWarps * 32 + 32, 1) w4a16_packed(StreamArgs a
   pdl_wait();
   pdl_trigger();
   const uint32_t tp_flag = TPM ? (uint32_t)*a.tp_epoch : 0u;
+  const unsigned long long tp_t0 = (TPM & 1) ? globaltimer_ns() : 0ull;
   const uint4* xsrc = reinterpret_cast<const uint4*>(a.x);
   const uint4* rsrc = reinterpret_cast<const uint4*>(a.residual);
   float v[4][8];
@@ -327,17 +233,28 @@ __global__ void __launch_bounds__(kWarps * 32 + 32, 1) w4a16_packed(StreamArgs a
     if (TPM & 1) {  // x = bf16(sum over ranks), ranks in order, fp32 sum; cells polled (bounded)
       float acc8[8] = {};
       for (int r = 0; r < a.tp_world; ++r) {
-        const uint2* cell = a.tp_in + (size_t)r * (K / 2) + (size_t)word * 4;
-        uint32_t pa[4];
+        const unsigned long long* cell =
+            reinterpret_cast<const unsigned long long*>(a.tp_in + (size_t)r * (K / 2) + (size_t)word * 4);
+        uint32_t pa[4] = {0, 0, 0, 0};
         bool fresh = false;
-        for (long it = 0; it < kSpinLimit && !fresh; ++it) {
-          uint32_t c0[4], c1[4];
-          asm volatile("ld.relaxed.sys.global.v4.u32 {%0, %1, %2, %3}, [%4];"
-                       : "=r"(c0[0]), "=r"(c0[1]), "=r"(c0[2]), "=r"(c0[3]) : "l"(cell) : "memory");
-          asm volatile("ld.relaxed.sys.global.v4.u32 {%0, %1, %2, %3}, [%4];"
-                       : "=r"(c1[0]), "=r"(c1[1]), "=r"(c1[2]), "=r"(c1[3]) : "l"(cell + 2) : "memory");
-          pa[0] = c0[0]; pa[1] = c0[2]; pa[2] = c1[0]; pa[3] = c1[2];
-          fresh = c0[1] == tp_flag && c0[3] == tp_flag && c1[1] == tp_flag && c1[3] == tp_flag;
+        // Each cell is one 64-bit element {flag << 32 | bf16 pair}: a single-copy-atomic access,
+        // so seeing this step's flag means seeing this step's pair. The whole poll of this
+        // kernel is bounded by one deadline; once any thread of the CTA has given up (or an
+        // earlier exchange failed), the others stop polling at their next check.
+        for (long it = 0; !fresh && !tp_failed; ++it) {
+          unsigned long long c[4];
+          asm volatile("ld.relaxed.sys.global.v2.u64 {%0, %1}, [%2];" : "=l"(c[0]), "=l"(c[1]) : "l"(cell) : "memory");
+          asm volatile("ld.relaxed.sys.global.v2.u64 {%0, %1}, [%2];" : "=l"(c[2]), "=l"(c[3]) : "l"(cell + 2)
+                       : "memory");
+          fresh = true;
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            pa[i] = (uint32_t)c[i];
+            fresh = fresh && (uint32_t)(c[i] >> 32) == tp_flag;
+          }
+          if (!fresh && (it & 63) == 63 &&
+              (globaltimer_ns() - tp_t0 > kExchangeDeadlineNs || *(volatile int*)&g_error_word == 2))
+            tp_failed = 1;
         }
         if (!fresh) atomicExch(&g_error_word, 2);
 #pragma unroll
@@ -533,15 +450,15 @@ __global__ void __launch_bounds__(kWarps * 32 + 32, 1) w4a16_packed(StreamArgs a
     }
   }
   if (TPM & 2) {
-    // Push this CTA's rows (whole tiles) to every rank's receive area over NVLink: one 8-byte
-    // store {bf16 pair, this step's flag} per row pair and rank.
+    // Push this CTA's rows (whole tiles) to every rank's receive area over NVLink: one 64-bit
+    // store {this step's flag << 32 | bf16 pair} per row pair and rank.
     named_sync(1, consumers);
     const int o0 = t_first * RT, rows = min(ntiles * RT, n_out - o0);
     for (int i = tid; i < rows / 2; i += consumers) {
       const uint32_t pair = reinterpret_cast<const uint32_t*>(ystage)[i];
+      const unsigned long long cell = ((unsigned long long)tp_flag << 32) | pair;
       for (int r = 0; r < a.tp_world; ++r)
-        asm volatile("st.relaxed.sys.global.v2.u32 [%0], {%1, %2};" ::"l"(a.tp_out[r] + o0 / 2 + i), "r"(pair),
-                     "r"(tp_flag) : "memory");
+        asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(a.tp_out[r] + o0 / 2 + i), "l"(cell) : "memory");
     }
   }
   // Tiles shared with a neighbouring CTA. Every range holds at least S blocks, so only the
@@ -782,6 +699,7 @@ namespace mt {
 cudaError_t heads_error_word(int* value, bool clear);
 cudaError_t bf16_error_word(int* value, bool clear);
 cudaError_t gemm_error_word(int* value, bool clear);
+cudaError_t persist_error_word(int* value, bool clear);
 }
 
 MT_API int mt_read_error_word(int* value, int clear) {
@@ -794,5 +712,6 @@ MT_API int mt_read_error_word(int* value, int clear) {
   if (e == cudaSuccess) e = heads_error_word(value, clear != 0);
   if (e == cudaSuccess) e = bf16_error_word(value, clear != 0);
   if (e == cudaSuccess) e = gemm_error_word(value, clear != 0);
+  if (e == cudaSuccess) e = persist_error_word(value, clear != 0);
   return (int)e;
 }

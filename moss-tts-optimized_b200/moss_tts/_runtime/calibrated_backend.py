@@ -49,19 +49,35 @@ def validate_export(folder, layers: int = 36) -> dict:
     return config
 
 
-def load_export(folder, shapes: dict, layers: int = 36, device="cpu") -> list[dict]:
+def _sha256(path: Path) -> str:
+    import hashlib
+    h = hashlib.sha256()
+    with open(path, "rb") as f:
+        for block in iter(lambda: f.read(1 << 22), b""):
+            h.update(block)
+    return h.hexdigest()
+
+
+def load_export(folder, shapes: dict, layers: int = 36, device="cpu", verify: bool = True) -> list[dict]:
     """Read and check all projections; returns per-layer ``{name: {qweight, scales, qzeros}}``.
 
     ``shapes`` maps projection name to the expected ``[N, K]``; scales must be exactly
     representable in bf16 (the reference's ``install_packing`` check, ``dp4a_packing.py:149-152``).
+    With ``verify``, every file whose SHA-256 the export's ``config.json`` records
+    (``calibration.py:204-209``) is checked against it before it is read.
     """
     folder = Path(folder)
     config = validate_export(folder, layers)
+    recorded = config.get("projections", {})
     out = []
     for i in range(layers):
         layer = {}
         for name in PROJECTIONS:
-            saved = torch.load(folder / f"{i:02d}_{name}.pt", map_location="cpu", weights_only=True)
+            path = folder / f"{i:02d}_{name}.pt"
+            digest = recorded.get(f"{i:02d}_{name}", {}).get("sha256")
+            if verify and digest and _sha256(path) != digest:
+                raise ValueError(f"Checksum mismatch: {path.name}")
+            saved = torch.load(path, map_location="cpu", weights_only=True)
             if list(saved["shape"]) != list(shapes[name]) or saved["group"] != config["group"]:
                 raise ValueError(f"Projection shape/group mismatch: {i} {name}")
             scales = saved["scales"]
@@ -75,3 +91,39 @@ def load_export(folder, shapes: dict, layers: int = 36, device="cpu") -> list[di
         out = [{k: {n: (t.to(device) if t is not None else None) for n, t in p.items()}
                 for k, p in layer.items()} for layer in out]
     return out
+
+
+def write_export(folder, layers: list, extra: dict | None = None) -> dict:
+    """Write a calibrated G32 export in the reference's on-disk format (``calibration.py:156-212``).
+
+    ``layers[i]`` maps ``qkv`` / ``out`` / ``up`` (gate||up) / ``down`` to ``(signed, scales)``:
+    int8 codes ``[N, K]`` in [-7, 7] and bf16 scales ``[N, K/32]``. As the reference does, the
+    config is first written with ``complete: false``, each projection is saved to a ``.tmp`` file
+    and moved into place, its SHA-256 recorded, and ``complete: true`` written last, so an
+    interrupted export is never mistaken for a complete one.
+    """
+    folder = Path(folder)
+    folder.mkdir(parents=True, exist_ok=True)
+    config = {"complete": False, "group": 32, "static_bf16_scales": True, "code_range": [-7, 7], "codebooks": 32,
+              "tts_revision": TTS_REVISION, "torch": torch.__version__, "projections": {}, **(extra or {})}
+    config_path = folder / "config.json"
+    config_path.write_text(json.dumps(config, indent=2) + "\n")
+    for index, layer in enumerate(layers):
+        for projection in PROJECTIONS:
+            signed, scales = layer[projection]
+            if signed.dtype != torch.int8 or signed.ndim != 2 or signed.shape[1] % 2:
+                raise ValueError("signed codes must be int8 [N, K]")
+            if int(signed.abs().max()) > 7:
+                raise ValueError("codes must lie in [-7, 7]")
+            unsigned = signed.to(torch.uint8) & 15
+            packed = (unsigned[:, ::2] | (unsigned[:, 1::2] << 4)).contiguous()
+            name = f"{index:02d}_{projection}"
+            destination = folder / f"{name}.pt"
+            temporary = destination.with_suffix(".tmp")
+            torch.save({"packed": packed.cpu(), "scales": scales.cpu(), "shape": list(signed.shape), "group": 32},
+                       temporary)
+            temporary.replace(destination)
+            config["projections"][name] = {"sha256": _sha256(destination)}
+    config["complete"] = True
+    config_path.write_text(json.dumps(config, indent=2) + "\n")
+    return config

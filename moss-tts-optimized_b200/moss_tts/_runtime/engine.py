@@ -1,6 +1,10 @@
 """Batch-1 decode engine: static device buffers, the per-step kernel sequence, CUDA graphs.
 
-One decode step (reference ``FastLLM._decode`` + ``hidden``, ``src/moss_tts/_runtime/llm.py:227-287``,
+On one GPU with W4 weights a decode step is three launches: ``mt_embedding_sum``, the whole
+layer stack as one persistent kernel (``mt_decode_layers``: one CTA per SM streaming every
+layer's packed weights without a break, grid barriers between the sublayers) and
+``mt_heads_greedy``. Otherwise (tensor parallelism, the BF16 preset, ``persistent=False``)
+one decode step (reference ``FastLLM._decode`` + ``hidden``, ``src/moss_tts/_runtime/llm.py:227-287``,
 fused-residual order) is 2 + 5 * layers launches, all PDL-chained and capturable:
 
     embedding_sum(ids)                                         -> emb
@@ -123,7 +127,7 @@ class DecodeEngine:
     """Static-buffer decode step for one sequence over (a shard of) ``DecoderWeights``."""
 
     def __init__(self, weights: DecoderWeights, max_length: int = 1024, *, splits: int | None = None,
-                 pdl: bool = True, tp: TensorParallel | None = None):
+                 pdl: bool = True, tp: TensorParallel | None = None, persistent: bool = True):
         cfg = weights.cfg
         cfg.validate()
         self.w, self.cfg, self.max_length = weights, cfg, max_length
@@ -188,8 +192,40 @@ class DecodeEngine:
         if world > 1 and os.environ.get("MT_TP_EXCHANGE", "p2p") != "nccl" and weights.layers[0].out.quantized \
                 and all(self._packed_ok(p, False) for lw in weights.layers for p in (lw.out, lw.down)):
             self.exchange = PeerExchange(self.tp, 2 * len(weights.layers), h, dev)
+        # Single GPU, W4 weights: the whole layer stack is one persistent launch (mt_decode_layers)
+        self.persistent = persistent and world == 1 and os.environ.get("MT_PERSISTENT", "1") != "0" and all(
+            self._packed_ok(p, paired) for lw in weights.layers
+            for p, paired in ((lw.qkv, False), (lw.out, False), (lw.gate_up, True), (lw.down, False)))
+        if self.persistent:
+            self._build_layer_table()
 
     # ------------------------------------------------------------------ kernels
+    def _build_layer_table(self) -> None:
+        """Device table of ``mt_decode_layer`` entries (packed projections, norms, caches) and the
+        zero-filled workspace of the persistent layer-stack kernel."""
+        w, n = self.w, len(self.w.layers)
+        table = (native.DecodeLayer * n)()
+        for i, lw in enumerate(w.layers):
+            e = table[i]
+            e.qkv, e.out = lw.qkv.packed_tiles(False).data_ptr(), lw.out.packed_tiles(False).data_ptr()
+            e.gate_up, e.down = lw.gate_up.packed_tiles(True).data_ptr(), lw.down.packed_tiles(False).data_ptr()
+            e.input_norm, e.post_norm = lw.input_norm.data_ptr(), lw.post_norm.data_ptr()
+            e.q_norm, e.k_norm = lw.q_norm.data_ptr(), lw.k_norm.data_ptr()
+            e.k_cache, e.v_cache = self.kv[i, 0].data_ptr(), self.kv[i, 1].data_ptr()
+        self.layer_table = torch.frombuffer(bytearray(bytes(table)), dtype=torch.uint8).to(self.device)
+        self.has_zeros = 1 if w.layers[0].qkv.qzeros is not None else 0
+        if any((p.qzeros is not None) != bool(self.has_zeros)
+               for lw in w.layers for p in (lw.qkv, lw.out, lw.gate_up, lw.down)):
+            raise ValueError("all projections must share one zero-point format")
+        nbytes = native.decode_layers_workspace(n, self.cfg.intermediate_size)
+        self.layers_workspace = torch.zeros(nbytes, device=self.device, dtype=torch.uint8)
+        self.residual = torch.zeros(self.cfg.hidden_size, device=self.device, dtype=torch.bfloat16)
+
+    def reset_workspace(self) -> None:
+        """Zero the persistent kernel's workspace (needed only after a call reported a timeout)."""
+        if self.persistent:
+            self.layers_workspace.zero_()
+
     @staticmethod
     def _packed_ok(p: Projection, paired: bool) -> bool:
         return p.quantized and p.k % 256 == 0 and 256 <= p.k <= 16384 and (not paired or p.n % 2 == 0)
@@ -224,9 +260,16 @@ class DecodeEngine:
         native.call("mt_embedding_sum", self.ids.data_ptr(), w.embed_text.data_ptr(), w.embed_audio.data_ptr(),
                     self.emb.data_ptr(), 1, cfg.hidden_size, w.embed_text.shape[0], w.embed_audio.shape[1],
                     cfg.n_vq, self.status.data_ptr(), self.flags, s)
+        eps = float(cfg.rms_norm_eps)
+        if self.persistent:
+            native.call("mt_decode_layers", self.layer_table.data_ptr(), len(w.layers), cfg.intermediate_size,
+                        self.has_zeros, self.emb.data_ptr(), self.position.data_ptr(), self.cos.data_ptr(),
+                        self.sin.data_ptr(), self.max_length, eps, self.residual.data_ptr(), self.mlp.data_ptr(),
+                        self.layers_workspace.data_ptr(), self.status.data_ptr(), self.flags, s)
+            self._launch_heads(self.residual, s)
+            return
         res = self.emb
         nxt = 0
-        eps = float(cfg.rms_norm_eps)
         ex, last = self.exchange, len(w.layers) - 1
         if ex is not None:
             ex.epoch.add_(1)  # one step: every exchange slot is expected once more
@@ -259,6 +302,12 @@ class DecodeEngine:
             else:
                 self._linear(lw.down, self.mid, self.mlp)
                 self.tp.all_reduce(self.mlp)
+        self._launch_heads(res, s)
+        if self.tp.world > 1:
+            self.tp.all_reduce(self.next_ids)
+
+    def _launch_heads(self, res, s) -> None:
+        cfg, w, eps = self.cfg, self.w, float(self.cfg.rms_norm_eps)
         native.call("mt_heads_greedy", self.mlp.data_ptr(), res.data_ptr(), w.final_norm.data_ptr(), eps,
                     self.hidden.data_ptr(), w.head_text_rows.data_ptr(), w.head_audio.data_ptr(),
                     self.text_logits.data_ptr(), self.audio_logits.data_ptr(), self.text_ids.data_ptr(),
@@ -266,8 +315,6 @@ class DecodeEngine:
                     self.best.data_ptr(), self.tickets[self.nkv:].data_ptr(), cfg.hidden_size, 2, self.n_cb,
                     cfg.audio_vocab_size, self.cb_offset, cfg.n_vq, cfg.audio_assistant_delay_slot_token_id,
                     cfg.audio_end_token_id, cfg.audio_pad_code, 1 if self.tp.rank == 0 else 0, self.flags, s)
-        if self.tp.world > 1:
-            self.tp.all_reduce(self.next_ids)
 
     def launch_advance(self) -> None:
         """Device-side state advance after a step (feed next_ids back, position += 1, delay

@@ -24,6 +24,7 @@ SIGNATURES = {
     "mt_abi_version": ([], _I),
     "mt_read_error_word": ([ctypes.POINTER(ctypes.c_int), _I], _I),
     "mt_dequant_w4": ([_P, _P, _P, _P, _I, _I, _I, _P], _I),
+    "mt_static_scales": ([_P, _I, _P, _I, _I, _P], _I),
     "mt_w4a16_linear": ([_P, _P, _P, _F, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P], _I),
     "mt_w4a16_packed_size": ([_I, _I, _I, _I, _LLP, _LLP], _I),
     "mt_w4a16_pack": ([_P, _P, _P, _I, _I, _I, _P, _P], _I),
@@ -43,6 +44,8 @@ SIGNATURES = {
     "mt_qk_rope_kv": ([_P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _F, _P, _I, _P], _I),
     "mt_attention_decode": ([_P] * 12 + [_I] * 5 + [_F, _P, _I, _P], _I),
     "mt_attention_decode_noalloc": ([_P] * 9 + [_I] * 5 + [_F, _P, _I, _P], _I),
+    "mt_decode_layers_workspace": ([_I, _I, _LLP], _I),
+    "mt_decode_layers": ([_P, _I, _I, _I, _P, _P, _P, _P, _I, _F, _P, _P, _P, _P, _I, _P], _I),
     "mt_heads_greedy": ([_P, _P, _P, _F] + [_P] * 11 + [_I] * 11 + [_P], _I),
 }
 
@@ -55,6 +58,12 @@ class TpExchange(ctypes.Structure):
     _fields_ = [("recv", ctypes.c_void_p * TP_MAX_RANKS), ("epoch", ctypes.c_void_p),
                 ("world", ctypes.c_int), ("rank", ctypes.c_int), ("in_slot", ctypes.c_int),
                 ("out_slot", ctypes.c_int), ("slot_elems", ctypes.c_int)]
+
+
+class DecodeLayer(ctypes.Structure):
+    """``mt_decode_layer`` of include/moss_tts_b200.h."""
+    _fields_ = [(name, ctypes.c_void_p) for name in ("qkv", "out", "gate_up", "down", "input_norm", "post_norm",
+                                                     "q_norm", "k_norm", "k_cache", "v_cache")]
 
 
 class NativeLibraryError(RuntimeError):
@@ -102,6 +111,13 @@ def w4a16_gemm_workspace(batch: int, n: int, k: int, mode: int) -> int:
     """Workspace bytes of mt_w4a16_gemm for this shape on the current device."""
     b = ctypes.c_longlong(0)
     call("mt_w4a16_gemm_workspace", batch, n, k, mode, ctypes.byref(b))
+    return b.value
+
+
+def decode_layers_workspace(n_layers: int, inter: int) -> int:
+    """Workspace bytes of mt_decode_layers on the current device."""
+    b = ctypes.c_longlong(0)
+    call("mt_decode_layers_workspace", n_layers, inter, ctypes.byref(b))
     return b.value
 
 

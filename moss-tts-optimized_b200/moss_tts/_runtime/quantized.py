@@ -111,6 +111,64 @@ def norm_linear(x, residual, norm_weight, eps, packed, scales, zeros=None, *, pa
     return summed, y
 
 
+def interleave_nibbles(packed):
+    """The reference's load-time nibble interleave (``dp4a_packing.py:15-19``): within every
+    4-byte word, codes 0..3 move to the low nibbles and codes 4..7 to the high nibbles."""
+    n, k2 = packed.shape
+    if packed.dtype != torch.uint8 or k2 % 4:
+        raise ValueError("Expected signed-nibble pairs with K divisible by eight")
+    unsigned = torch.stack([packed & 15, packed >> 4], dim=-1).reshape(n, -1, 8)
+    return (unsigned[:, :, :4] | (unsigned[:, :, 4:] << 4)).reshape(n, k2).contiguous()
+
+
+def deinterleave_nibbles(packed):
+    """Inverse of ``interleave_nibbles``: back to code k in nibble ``k & 1`` of byte ``k / 2``."""
+    n, k2 = packed.shape
+    if packed.dtype != torch.uint8 or k2 % 4:
+        raise ValueError("Expected signed-nibble pairs with K divisible by eight")
+    words = packed.reshape(n, -1, 4)
+    unsigned = torch.cat([words & 15, words >> 4], dim=-1).reshape(n, -1, 8)
+    return (unsigned[:, :, 0::2] | (unsigned[:, :, 1::2] << 4)).reshape(n, k2).contiguous()
+
+
+_SIGNED: dict = {}
+
+
+def from_signed(packed, scales, *, group: int = 32, interleaved: bool = False):
+    """Reference-format weights -> this library's W4 operands ``(qweight, bf16 scales)``.
+
+    The reference stores two's-complement codes in [-7, 7] (``calibration.py:190-191``) with
+    fp32 or bf16 scales (``calibrated_backend.py:51``, ``dp4a_packing.py:149-155``); flipping
+    bit 3 of every nibble gives ``q = code + 8`` with the implicit zero point 8, so the
+    dequantized weights are unchanged bit for bit. Scales must be exactly representable in
+    bf16 (the reference's own check before it narrows them). The converted copy is made once
+    per source tensor and reused while the source is alive and unmodified.
+    """
+    if group != 32:
+        raise ValueError("Only G32 groups are supported")
+    if packed.dtype != torch.uint8 or packed.ndim != 2:
+        raise ValueError("packed weights must be uint8 [N, K/2] signed nibbles")
+    n, k = packed.shape[0], packed.shape[1] * 2
+    if scales.shape != (n, k // group) or scales.dtype not in (torch.float32, torch.bfloat16):
+        raise ValueError("scales must be float32 or bfloat16 [N, K/32]")
+    key = (id(packed), packed._version, id(scales), scales._version, bool(interleaved))
+    hit = _SIGNED.get(id(packed))
+    if hit is not None and hit[0] == key:
+        return hit[1], hit[2]
+    if scales.dtype != torch.bfloat16:
+        if not torch.equal(scales, scales.bfloat16().float()):
+            raise ValueError("Scales are not exactly representable in bf16")
+        scales = scales.bfloat16()
+    codes = deinterleave_nibbles(packed) if interleaved else packed
+    qweight = (codes ^ 0x88).contiguous()
+    scales = scales.contiguous()
+    import weakref
+    if hit is None:
+        weakref.finalize(packed, _SIGNED.pop, id(packed), None)
+    _SIGNED[id(packed)] = (key, qweight, scales)
+    return qweight, scales
+
+
 def dequantize_packed(packed, scales, zeros=None, group=32):
     """Bit-exact ``bf16((q - z) * s)`` of a packed W4 matrix, ``[N, K]``."""
     packed, n, k = _weights(packed, scales, zeros, group)

@@ -26,20 +26,27 @@ def dequantize_projection(p, group: int = 32) -> np.ndarray:
 class Decoder:
     """Stateful CPU decoder holding a static KV cache of ``max_length`` rows."""
 
-    def __init__(self, weights: dict, cfg: dict, max_length: int, layers=None):
+    def __init__(self, weights: dict, cfg: dict, max_length: int, layers=None, threads: int = 1):
         self.cfg = cfg
         self.max_length = max_length
         g = cfg["group_size"]
         chosen = weights["layers"] if layers is None else weights["layers"][:layers]
+        names = ("qkv", "out", "gate_up", "down")
+        jobs = [(i, n) for i in range(len(chosen)) for n in names]
+        if threads > 1:  # numpy releases the GIL inside its array operations
+            from concurrent.futures import ThreadPoolExecutor
+            with ThreadPoolExecutor(threads) as ex:
+                deq = dict(zip(jobs, ex.map(lambda j: dequantize_projection(chosen[j[0]][j[1]], g), jobs)))
+        else:
+            deq = {j: dequantize_projection(chosen[j[0]][j[1]], g) for j in jobs}
         self.layers = []
-        for lw in chosen:
+        for i, lw in enumerate(chosen):
             self.layers.append({
                 "input_norm": to_f32(lw["input_norm"]), "post_norm": to_f32(lw["post_norm"]),
                 "q_norm": to_f32(lw["q_norm"]), "k_norm": to_f32(lw["k_norm"]),
-                "qkv": dequantize_projection(lw["qkv"], g), "out": dequantize_projection(lw["out"], g),
-                "gate_up": dequantize_projection(lw["gate_up"], g),
-                "down": dequantize_projection(lw["down"], g),
+                **{n: deq[(i, n)] for n in names},
             })
+        del deq
         n_kv, d = cfg["num_kv_heads"], cfg["head_dim"]
         self.k = np.zeros((len(self.layers), n_kv, max_length, d), dtype=np.float32)
         self.v = np.zeros_like(self.k)
@@ -55,6 +62,18 @@ class Decoder:
         av = cfg["audio_vocab_size"]
         self.audio_heads = to_f32(weights["head_audio"][:, :av].reshape(-1, cfg["hidden_size"]))
 
+    _linear = staticmethod(ops.linear)
+
+    def reordered(self, chunks: int) -> "Decoder":
+        """A decoder over the same weights (shared, not copied) with its own KV cache whose
+        projections sum over K in ``chunks`` pieces (``ops.linear_reordered``): the same
+        arithmetic up to fp32 summation order."""
+        twin = Decoder.__new__(Decoder)
+        twin.__dict__.update(self.__dict__)
+        twin.k, twin.v = np.zeros_like(self.k), np.zeros_like(self.v)
+        twin._linear = lambda x, w: ops.linear_reordered(x, w, chunks)
+        return twin
+
     def hidden(self, ids, position: int) -> np.ndarray:
         """Final-norm hidden state for one token, ``llm.py:227-260``."""
         cfg = self.cfg
@@ -63,16 +82,17 @@ class Decoder:
         residual = emb
         hidden = ops.rmsnorm(emb, self.layers[0]["input_norm"], eps)
         for i, lw in enumerate(self.layers):
-            qkv = ops.linear(hidden, lw["qkv"])
+            linear = self._linear
+            qkv = linear(hidden, lw["qkv"])
             q, k_row, v_row = ops.qk_rope(qkv, lw["q_norm"], lw["k_norm"], self.cos[position],
                                           self.sin[position], eps, cfg["num_heads"],
                                           cfg["num_kv_heads"], cfg["head_dim"])
             self.k[i, :, position] = k_row
             self.v[i, :, position] = v_row
             att = ops.attention_decode(q, self.k[i], self.v[i], position)
-            att = ops.linear(att, lw["out"])
+            att = linear(att, lw["out"])
             residual, hidden = ops.add_rmsnorm(att, residual, lw["post_norm"], eps)
-            mlp = ops.linear(ops.silu_mul(ops.linear(hidden, lw["gate_up"])), lw["down"])
+            mlp = linear(ops.silu_mul(linear(hidden, lw["gate_up"])), lw["down"])
             norm = self.layers[i + 1]["input_norm"] if i + 1 < len(self.layers) else self.final_norm
             residual, hidden = ops.add_rmsnorm(mlp, residual, norm, eps)
         return hidden

@@ -24,6 +24,19 @@ def linear(x, w) -> np.ndarray:
     return round_bf16(np.matmul(x, w.T))
 
 
+def linear_reordered(x, w, chunks: int) -> np.ndarray:
+    """``linear`` with the fp32 sum over K taken in ``chunks`` consecutive pieces, each summed
+    on its own and then added in order -- the same value up to fp32 summation order. Tests use
+    it to measure how far the reference's own arithmetic moves under a different order."""
+    x, w = to_f32(x), to_f32(w)
+    k = w.shape[1]
+    acc = np.zeros(x.shape[:-1] + (w.shape[0],), dtype=np.float32)
+    for c in range(chunks):
+        a, b = c * k // chunks, (c + 1) * k // chunks
+        acc += np.matmul(x[..., a:b], w[:, a:b].T)
+    return round_bf16(acc)
+
+
 def rmsnorm(x, weight, eps: float) -> np.ndarray:
     """Qwen3 RMSNorm, ``_runtime/kernels.py:50-59``: the normalized value is
     rounded to bf16 before the weight multiply, and the product is rounded again."""

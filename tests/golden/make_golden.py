@@ -1,9 +1,9 @@
 """Write the golden fixtures in this folder from the reference's own CPU code.
 
-Run in a container that has the reference source (read-only) at
-``$MOSS_TTS_REFERENCE`` (default ``/root/reference``):
+Run in a container that has the reference source (read-only), with
+``$MOSS_TTS_REFERENCE`` set to the reference checkout (the folder holding ``src/moss_tts``):
 
-    python tests/golden/make_golden.py
+    MOSS_TTS_REFERENCE=<reference checkout> python tests/golden/make_golden.py
 
 The reference package is imported from ``$MOSS_TTS_REFERENCE/src`` (its module
 name is ``moss_tts``); this repository's seeded synthetic-weight generator is
@@ -31,7 +31,9 @@ import torch
 
 HERE = Path(__file__).resolve().parent
 REPO = HERE.parent.parent
-REFERENCE = Path(os.environ.get("MOSS_TTS_REFERENCE", "/root/reference"))
+if not os.environ.get("MOSS_TTS_REFERENCE"):
+    raise SystemExit("set MOSS_TTS_REFERENCE to the reference checkout (the folder holding src/moss_tts)")
+REFERENCE = Path(os.environ["MOSS_TTS_REFERENCE"])
 sys.path.insert(0, str(REFERENCE / "src"))
 
 from moss_tts._model.configuration_moss_tts import MossTTSDelayConfig  # noqa: E402

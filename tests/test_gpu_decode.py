@@ -42,6 +42,7 @@ def test_teacher_forced_decode_matches_reference(model):
     eng = DecodeEngine(w, max_length=128)
     hs = list(g["hidden_steps"])
     mismatched = 0
+    worst = 0.0
     for step in range(g["ids"].shape[0]):
         alen, delay = schedule(step)
         nxt = eng.step(torch.from_numpy(g["ids"][step]), step, alen, delay).reshape(-1).cpu().numpy()
@@ -56,7 +57,10 @@ def test_teacher_forced_decode_matches_reference(model):
         if step in hs:
             ref = from_bf16_bits(g["hidden"][hs.index(step)]).astype(np.float64)
             h = from_bf16_bits(host_bits(eng.hidden)).astype(np.float64)
+            worst = max(worst, float(np.max(np.abs(h - ref) / (1 + np.abs(ref)))))
             assert np.all(np.abs(h - ref) <= 5e-2 + 2e-2 * np.abs(ref)), (step, np.abs(h - ref).max())
+    print(f"reference model, 64 steps: worst |h - ref| / (1 + |ref|) = {worst:.4g}; "
+          f"{mismatched} of {g['next'].size} ids differ, all on near-ties")
     assert int(eng.status.item()) == 0
     assert mismatched <= 0.02 * g["next"].size, mismatched
 

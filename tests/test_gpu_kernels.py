@@ -35,6 +35,7 @@ def close(y_bits, ref, atol=ATOL, rtol=RTOL):
     ref = np.asarray(ref, dtype=np.float64)
     err = np.abs(y - ref)
     bad = err > atol + rtol * np.abs(ref)
+    print(f"max abs err {err.max():.4g} (bar {atol:g} + {rtol:g} |ref|)")
     assert not bad.any(), f"max err {err.max():.4g} at {np.argmax(err)}; {bad.sum()} outside tolerance"
     return err.max()
 
@@ -135,7 +136,7 @@ def test_mlp_config1(cuda_device):
         x = dev_bf16(synthetic.activation(80 + b, (b, 4096)), cuda_device)
         _, mid = quantized.norm_linear(x, None, dev_bf16(nw, cuda_device), 1e-6, *gu_d, paired=True)
         y = quantized.linear(mid, *dn_d)
-        close(host_bits(y), from_bf16_bits(g[f"b{b}_y"]), 5e-2, 2e-2)
+        close(host_bits(y), from_bf16_bits(g[f"b{b}_y"]))
 
 
 # ------------------------------------------------------------------ small operators
@@ -362,7 +363,7 @@ def test_rope_tables_match_transformers():
         assert ulps.max() <= 1, ulps.max()
 
 
-@pytest.mark.parametrize("ctx", [0, 1, 31, 96, 777, 2048])
+@pytest.mark.parametrize("ctx", [0, 1, 31, 96, 777, 2048, 4095])
 def test_attention_decode_against_oracle(cuda_device, ctx):
     L = max(ctx + 1, 128)
     g = golden("ops")

@@ -1,0 +1,128 @@
+"""The persistent layer-stack kernel (``mt_decode_layers``) on a B200.
+
+* config 2: one layer at cached contexts 96 and 2048 through ``mt_decode_layers`` (fed the
+  fixture's layer input directly) against the reference's ``Qwen3DecoderLayer`` output;
+* the same layer against the per-sublayer kernels of the multi-launch engine path, at
+  positions that start, straddle and end attention chunks (0, 1, 63, 64, 65, 1000, the last
+  cache row);
+* the 2-layer model over 16 steps: persistent engine against the multi-launch engine;
+* bookkeeping: a call leaves its workspace counters and the first layer's accumulators zero,
+  two calls in a row give the same bits, and a CUDA-graph replay equals the eager call.
+
+Bars: max-abs 2e-2 / rel 1e-2 against the reference and against the other kernels (the
+attention splits and the fp32 summation order differ between the two paths).
+"""
+import numpy as np
+import pytest
+import torch
+
+from conftest import golden
+from oracle.numerics import from_bf16_bits
+
+from moss_tts._runtime import native, synthetic
+from moss_tts._runtime.config import DecoderConfig, small_vocab
+from moss_tts._runtime.engine import DecodeEngine
+from moss_tts._runtime.weights import DecoderWeights
+
+from test_gpu_parity import _bf16, _errors, _host, engine_layer
+
+pytestmark = pytest.mark.gpu
+
+ATOL, RTOL = 2e-2, 1e-2
+
+
+def persistent_layer(eng, x):
+    """mt_decode_layers over the engine's layers with layer input x; returns (residual, mlp)."""
+    s = torch.cuda.current_stream(eng.device).cuda_stream
+    native.call("mt_decode_layers", eng.layer_table.data_ptr(), len(eng.w.layers), eng.cfg.intermediate_size,
+                eng.has_zeros, x.data_ptr(), eng.position.data_ptr(), eng.cos.data_ptr(), eng.sin.data_ptr(),
+                eng.max_length, 1e-6, eng.residual.data_ptr(), eng.mlp.data_ptr(), eng.layers_workspace.data_ptr(),
+                eng.status.data_ptr(), 0, s)
+    return eng.residual, eng.mlp
+
+
+def _one_layer(dev, max_length):
+    dc = small_vocab(DecoderConfig(), vocab=64, layers=1)
+    host = synthetic.decoder_weights(dc, seed=5, layers=1)  # the layer of tests/golden/layer.npz
+    w = DecoderWeights.from_host(dc, host, dev)
+    return DecodeEngine(w, max_length=max_length), DecodeEngine(w, max_length=max_length, persistent=False)
+
+
+def _workspace_clean(eng):
+    ws = eng.layers_workspace
+    counters = ws[:1024].view(torch.int32).cpu().numpy()
+    acc0 = ws[1024:1024 + 4 * 14336].view(torch.float32).cpu().numpy()
+    return not counters.any() and not acc0.any()
+
+
+@pytest.mark.parametrize("ctx", [96, 2048])
+def test_persistent_layer_matches_reference(cuda_device, ctx):
+    dev = cuda_device
+    g = golden("layer")
+    eng, _ = _one_layer(dev, ((ctx + 1 + 127) // 128) * 128)
+    assert eng.persistent
+    seed = {96: 61, 2048: 62}[ctx]
+    eng.kv[0, 0, :, :ctx] = _bf16(synthetic.activation(seed, (1, 8, ctx, 128)), dev)[0]
+    eng.kv[0, 1, :, :ctx] = _bf16(synthetic.activation(seed + 100, (1, 8, ctx, 128)), dev)[0]
+    x = _bf16(synthetic.activation(seed + 200, (1, 1, 4096)), dev).reshape(-1)
+    eng.control[33] = ctx
+    res, mlp = persistent_layer(eng, x)
+    y = (res.float() + mlp.float()).to(torch.bfloat16)
+    torch.cuda.synchronize(dev)
+    mx, rel, excess = _errors(_host(y), from_bf16_bits(g[f"ctx{ctx}_y"]))
+    kerr = _errors(_host(eng.kv[0, 0, :, ctx]), from_bf16_bits(g[f"ctx{ctx}_krow"]))
+    print(f"persistent layer ctx {ctx}: output max abs {mx:.4g}; new K row max abs {kerr[0]:.3g}")
+    assert excess <= 0 and kerr[2] <= 0, (mx, kerr)
+    assert native.error_word(clear=True) == 0 and int(eng.status.item()) == 0
+    assert _workspace_clean(eng)
+
+
+@pytest.mark.parametrize("position", [0, 1, 63, 64, 65, 1000, 1151])
+def test_persistent_layer_matches_launch_chain(cuda_device, position):
+    dev = cuda_device
+    pers, chain = _one_layer(dev, 1152)
+    kv = torch.randn((2, 8, 1152, 128), generator=torch.Generator(device=dev).manual_seed(position), device=dev)
+    pers.kv[0].copy_(kv)
+    chain.kv[0].copy_(kv)
+    x = torch.randn(4096, generator=torch.Generator(device=dev).manual_seed(7), device=dev).to(torch.bfloat16)
+    pers.control[33] = position
+    res, mlp = persistent_layer(pers, x)
+    y_p = (res.float() + mlp.float()).to(torch.bfloat16)
+    y_c = engine_layer(chain, chain.w.layers[0], x, position)
+    torch.cuda.synchronize(dev)
+    mx, rel, excess = _errors(_host(y_p), _host(y_c))
+    print(f"position {position}: persistent vs launch chain max abs {mx:.4g}")
+    verr = _errors(_host(pers.kv[0, 1, :, position]), _host(chain.kv[0, 1, :, position]))
+    assert excess <= 0 and verr[2] <= 0, (mx, verr)
+    assert native.error_word(clear=True) == 0 and int(pers.status.item()) == 0
+    assert _workspace_clean(pers)
+
+
+def test_persistent_engine_steps_match_launch_chain(cuda_device):
+    """16 decode steps of the 2-layer full-width model: the persistent engine against the
+    multi-launch engine on the same weights, fed the same ids; also bitwise repeatability
+    (a second persistent engine, one of them replaying a captured graph)."""
+    dc = small_vocab(DecoderConfig(), vocab=2048, layers=2)
+    w = DecoderWeights.from_host(dc, synthetic.decoder_weights(dc, seed=7), cuda_device)
+    pers, again, chain = (DecodeEngine(w, max_length=128), DecodeEngine(w, max_length=128),
+                          DecodeEngine(w, max_length=128, persistent=False))
+    assert pers.persistent and again.persistent and not chain.persistent
+    again.capture()
+    ids = torch.full((33,), 5, dtype=torch.long)
+    ids[0] = dc.audio_assistant_gen_slot_token_id
+    worst, differ = 0.0, 0
+    for step in range(16):
+        a = pers.step(ids, step, step + 1, -1).reshape(-1).cpu()
+        b = again.step(ids, step, step + 1, -1).reshape(-1).cpu()
+        c = chain.step(ids, step, step + 1, -1).reshape(-1).cpu()
+        assert torch.equal(a, b) and torch.equal(pers.hidden, again.hidden), step
+        mx, rel, excess = _errors(_host(pers.hidden), _host(chain.hidden))
+        worst = max(worst, mx)
+        assert excess <= 0, (step, mx)
+        differ += int((a != c).sum())
+        ids = c
+    print(f"2 layers, 16 steps: persistent vs launch chain hidden max abs {worst:.4g}; {differ} ids differ")
+    assert differ <= 0.02 * 16 * 33
+    assert torch.equal(pers.kv, again.kv)
+    assert native.error_word(clear=True) == 0
+    again.graph = None

@@ -1,14 +1,16 @@
 """The scratch-free attention entry point (``mt_attention_decode_noalloc``).
 
 It exists for callers that cannot allocate device memory for the split-K scratch:
-code that enqueues work while a stream is being captured into a CUDA graph, real-time
-audio callbacks that must not block on an allocator, and foreign-function hosts with no
-device allocator of their own. It keeps its scratch in a fixed array inside the library.
+real-time audio callbacks that must not block on an allocator (an allocation can
+synchronise the device), and plugin or foreign-function hosts with no device allocator of
+their own. It keeps its scratch in a fixed array inside the library.
 
 This test calls it through the C ABI twice in a row (the second call sees whatever the
 first left in the shared array) and checks each result against the allocating entry
-point ``mt_attention_decode`` on identical inputs, within the tolerance the other GPU
-tests use, plus the documented rejection of a request larger than the fixed array.
+point ``mt_attention_decode`` on identical inputs -- both its default cluster kernel and
+its split-K kernel with caller-owned scratch (the same kernel the scratch-free entry point
+runs) -- within the tolerance the other GPU tests use, plus the documented rejection of a
+request larger than the fixed array.
 It is collected last so a failure here cannot hide the rest of the suite, and it builds
 everything it needs itself, so it also passes alone in a fresh process.
 """
@@ -39,7 +41,7 @@ def test_noalloc_attention_matches_allocating_entry_point(cuda_device):
     qn, kn = qn.to(torch.bfloat16).contiguous(), kn.to(torch.bfloat16).contiguous()
     k_a = _bf16(synthetic.activation(33, (1, nkv, max_len, 128)), dev)
     v_a = _bf16(synthetic.activation(34, (1, nkv, max_len, 128)), dev)
-    k_b, v_b = k_a.clone(), v_a.clone()
+    k_b, v_b, k_c, v_c = k_a.clone(), v_a.clone(), k_a.clone(), v_a.clone()
     partial = torch.empty(nkv * splits * 4 * 128, device=dev)
     lse = torch.empty(nkv * splits * 4, device=dev)
     tickets = torch.zeros(nkv, device=dev, dtype=torch.int32)
@@ -47,18 +49,23 @@ def test_noalloc_attention_matches_allocating_entry_point(cuda_device):
         qkv = _bf16(synthetic.activation(40 + call, (1, (nq + 2 * nkv) * 128)), dev)
         pos = torch.tensor([position], device=dev)
         out_a = torch.empty((1, nq * 128), device=dev, dtype=torch.bfloat16)
-        out_b = torch.empty_like(out_a)
-        native.call("mt_attention_decode", qkv.data_ptr(), qn.data_ptr(), kn.data_ptr(), cos.data_ptr(),
-                    sin.data_ptr(), pos.data_ptr(), k_a.data_ptr(), v_a.data_ptr(), out_a.data_ptr(),
-                    partial.data_ptr(), lse.data_ptr(), tickets.data_ptr(), 1, nq, nkv, max_len, splits,
-                    1e-6, None, 0, stream)
+        out_b, out_c = torch.empty_like(out_a), torch.empty_like(out_a)
+        for flags, out, k, v in ((0, out_a, k_a, v_a), (native.FLAG_REGISTER_PIPELINE, out_c, k_c, v_c)):
+            native.call("mt_attention_decode", qkv.data_ptr(), qn.data_ptr(), kn.data_ptr(), cos.data_ptr(),
+                        sin.data_ptr(), pos.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(),
+                        partial.data_ptr(), lse.data_ptr(), tickets.data_ptr(), 1, nq, nkv, max_len, splits,
+                        1e-6, None, flags, stream)
         native.call("mt_attention_decode_noalloc", qkv.data_ptr(), qn.data_ptr(), kn.data_ptr(),
                     cos.data_ptr(), sin.data_ptr(), pos.data_ptr(), k_b.data_ptr(), v_b.data_ptr(),
                     out_b.data_ptr(), 1, nq, nkv, max_len, splits, 1e-6, None, 0, stream)
         torch.cuda.synchronize(dev)
-        a, b = out_a.float().cpu().numpy(), out_b.float().cpu().numpy()
-        assert np.all(np.abs(a - b) <= ATOL + RTOL * np.abs(a)), (call, np.abs(a - b).max())
-        assert torch.equal(k_a, k_b) and torch.equal(v_a, v_b)  # same cache rows written
+        a, b, c = (o.float().cpu().numpy() for o in (out_a, out_b, out_c))
+        err = np.abs(a - b).max()
+        print(f"noalloc call {call}: max |cluster - noalloc| = {err:.3g}")
+        assert np.all(np.abs(a - b) <= ATOL + RTOL * np.abs(a)), (call, err)
+        # the same split-K kernel over caller-owned scratch gives the same bits
+        assert np.array_equal(b, c), (call, np.abs(b - c).max())
+        assert torch.equal(k_a, k_b) and torch.equal(v_a, v_b) and torch.equal(k_a, k_c)  # same cache rows
         assert float(out_b.float().abs().sum()) > 0.0
 
 
