@@ -52,6 +52,10 @@ def parse():
     ap.add_argument("--profile-gemm", type=int, default=0, metavar="B",
                     help="only launch the tcgen05 W4A16 GEMM on the fused gate/up shape with B rows "
                          "(4 launches on random weights, for an ncu capture); prints its mean launch time")
+    ap.add_argument("--config0", action="store_true",
+                    help="config 0 alone: the 12288 x 4096 W4A16 G32 GEMV (zero points), 8 rotating weight sets "
+                         "(233 MB > L2, every launch L2-cold), CUDA events; prints one JSON line with its roofline")
+    ap.add_argument("--config0-sets", type=int, default=8, help=argparse.SUPPRESS)
     ap.add_argument("--profile-kernel", action="store_true",
                     help="only launch the dominant kernel (packed add+norm+gate/up+SiLU GEMV), once per "
                          "layer per step, for an ncu capture; prints its mean launch time")
@@ -302,6 +306,77 @@ def bf16_step_rate(args, cfg, dev, rank, world, group, max_length):
     return args.steps / (ms / 1000.0), ms / args.steps, step_bytes, status
 
 
+def config0(args):
+    """Config 0 on its own: y[1, 12288] = x[1, 4096] . W^T, W4A16 G32 with per-group zero points
+    (codes U[0, 15], zeros U[6, 9], scales |N(0, 0.02)| / 7 + 1e-4), the packed tensor-core GEMV
+    (mt_w4a16_linear_packed) and, beside it, the GPTQ-layout register GEMV (mt_w4a16_linear).
+    ``--config0-sets`` independent weight sets (default 8: 233 MB, more than the 126 MB L2) are
+    used in rotation, so every launch reads its weights from HBM. Algorithmic bytes per launch:
+    codes + scales + zero points + x + y = 29,130,752 (the survey's config-0 figure)."""
+    import torch
+
+    from moss_tts._runtime import native
+    from moss_tts._runtime.weights import Projection
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    n, k, sets = 12288, 4096, max(1, args.config0_sets)
+    g = torch.Generator(device=dev).manual_seed(0)
+    projs = []
+    for _ in range(sets):
+        qw = torch.randint(0, 256, (n, k // 2), generator=g, device=dev, dtype=torch.uint8)
+        sc = (torch.randn((n, k // 32), generator=g, device=dev).abs() * 0.02 / 7 + 1e-4).to(torch.bfloat16)
+        z = torch.randint(6, 10, (n, k // 32), generator=g, device=dev, dtype=torch.uint8)
+        p = Projection(n, k, qw, sc, (z[:, 0::2] | (z[:, 1::2] << 4)).contiguous())
+        p.packed_tiles(False)
+        projs.append(p)
+    x = torch.randn(k, generator=g, device=dev).to(torch.bfloat16)
+    y = torch.empty(n, device=dev, dtype=torch.bfloat16)
+    ws = torch.zeros(native.w4a16_packed_size(n, k, True, 0)[1], device=dev, dtype=torch.uint8)
+    stream = torch.cuda.current_stream(dev)
+    algo = n * k // 2 + n * (k // 32) * 2 + n * (k // 64) + k * 2 + n * 2
+    peak, peak_kind = measured_peaks()
+
+    def packed(p):
+        native.call("mt_w4a16_linear_packed", x.data_ptr(), None, None, 0.0, None, p.packed_tiles(False).data_ptr(), 1,
+                    y.data_ptr(), n, k, 0, ws.data_ptr(), native.FLAG_PDL, stream.cuda_stream)
+
+    def gptq(p):
+        native.call("mt_w4a16_linear", x.data_ptr(), None, None, 0.0, None, p.qweight.data_ptr(), p.scales.data_ptr(),
+                    p.qzeros.data_ptr(), y.data_ptr(), 1, n, k, 32, 0, native.FLAG_PDL, stream.cuda_stream)
+
+    results = {}
+    for name, fn in (("packed", packed), ("gptq_layout", gptq)):
+        for _ in range(max(3, args.warmup)):
+            for p in projs:
+                fn(p)
+        torch.cuda.synchronize(dev)
+        reps = max(1, args.steps)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with ClockSampler(0) as clocks:
+            e0.record(stream)
+            for _ in range(reps):
+                for p in projs:
+                    fn(p)
+            e1.record(stream)
+            torch.cuda.synchronize(dev)
+        us = e0.elapsed_time(e1) * 1000 / (reps * sets)
+        results[name] = {"launch_us": round(us, 3), "achieved_gbs": round(algo / (us * 1e-6) / 1e9, 1),
+                         "frac": round(algo / (us * 1e-6) / 1e9 / peak, 4), "clocks": clocks.summary()}
+    best = results["packed"]
+    print(json.dumps({
+        "metric": "config0 W4A16 G32 GEMV HBM GB/s (12288 x 4096, batch 1)", "value": best["achieved_gbs"],
+        "unit": "GB/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+        "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "config0: one W4A16 G32 linear 12288 x 4096 with zero points, batch 1",
+                   "weight_sets": sets, "l2": f"{sets} rotating weight sets ({sets * algo / 1e6:.0f} MB > L2)"},
+        "roofline": {"bound": "hbm", "kernel": "mt_w4a16_linear_packed (mode 0, N=12288 K=4096)",
+                     "achieved": best["achieved_gbs"], "peak": peak, "peak_kind": peak_kind, "unit": "GB/s",
+                     "frac": best["frac"], "bytes_per_launch": algo, "launch_us": best["launch_us"],
+                     "traffic": None},
+        "kernels": results}), flush=True)
+
+
 def profile_gemm(rows: int):
     """The batched projection alone: mt_w4a16_gemm on gate/up (N = 24576, K = 4096, fused pair)
     with `rows` activation rows, random codes / scales / zero points, 4 launches."""
@@ -443,6 +518,9 @@ def main():
         return
     if args.profile_gemm:
         profile_gemm(args.profile_gemm)
+        return
+    if args.config0:
+        config0(args)
         return
     import torch
     import torch.distributed as dist

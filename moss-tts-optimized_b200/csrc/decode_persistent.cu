@@ -10,7 +10,7 @@
 // and an activation prologue during which HBM sits idle. Here the weight stream never
 // stops: the weights do not depend on the activations, so each CTA's producer warp streams
 // its whole schedule -- every layer's projection blocks and its slice of the KV cache -- into
-// a 4-stage shared-memory ring (150 KB per SM, ~22 MB in flight over the GPU), while the 16
+// a 4-stage shared-memory ring (142 KB per SM, ~21 MB in flight over the GPU), while the 15
 // consumer warps step through the phases and meet the other CTAs at grid barriers. A barrier
 // or an attention chain then costs consumer time only; the ring keeps filling meanwhile.
 //
@@ -49,9 +49,13 @@ namespace persist {
 
 using namespace pipe;
 
+// 15 consumer warps + 1 producer warp: 16 warps may hold 128 registers each (warps get
+// registers in groups of four, so a 17th warp would cap every warp at 96 and spill)
+constexpr int kCW = 15;                     // consumer warps
 constexpr int kNS = 4;                      // ring stages
-constexpr int kSB = 16;                     // slice blocks per stage: one per consumer warp
-constexpr int kConsumers = kWarps * 32;     // 512 consumer threads
+constexpr int kSB = kCW;                    // slice blocks per stage: one per consumer warp
+constexpr int kConsumers = kCW * 32;        // 480 consumer threads
+constexpr int kTG = kConsumers / 64;        // P.V token groups of 64 dim-pair threads (7)
 constexpr int kHeadDim = 128, kRep = 4, kNq = 32, kNkv = 8, kHidden = 4096, kQkvRows = 6144;
 constexpr int kChunk = 64;                  // attention tokens per stage (K and V rows: 32 KB)
 constexpr int kAccPerLayer = kQkvRows + 2 * kHidden;  // q|k|v, o, down fp32 accumulators
@@ -293,7 +297,7 @@ __device__ __forceinline__ void attention_phase(const Args* a, const mt_decode_l
             }
           }
           if (tid < kRep) { m_run[tid] = -INFINITY; l_run[tid] = 0.f; }
-          const int dp = tid & 63, tg = tid >> 6;  // P.V: dim pair, token group (8 groups)
+          const int dp = tid & 63, tg = tid >> 6;  // P.V: dim pair, token group (tg < kTG take part)
           float accv[kRep][2];
 #pragma unroll
           for (int hh = 0; hh < kRep; ++hh) accv[hh][0] = accv[hh][1] = 0.f;
@@ -373,7 +377,7 @@ __device__ __forceinline__ void attention_phase(const Args* a, const mt_decode_l
               for (int hh = 0; hh < kRep; ++hh) { accv[hh][0] *= sc[hh]; accv[hh][1] *= sc[hh]; }
               const uint32_t* v2 = reinterpret_cast<const uint32_t*>(vs) + dp;
 #pragma unroll 4
-              for (int t = tg; t < rows; t += kConsumers / 64) {
+              for (int t = tg; tg < kTG && t < rows; t += kTG) {
                 const uint32_t vv = v2[(size_t)t * (kHeadDim / 2)];
                 const float va = bf16_lo(vv), vb = bf16_hi(vv);
 #pragma unroll
@@ -390,21 +394,25 @@ __device__ __forceinline__ void attention_phase(const Args* a, const mt_decode_l
           }
           if (!fail_flag) {
             // token groups -> one unnormalised partial per (query head, dim) of this split
-            float* redv = reinterpret_cast<float*>(xp);  // [8 token groups][kRep][128]
+            float* redv = reinterpret_cast<float*>(xp);  // [kTG token groups][kRep][128]
+            if (tg < kTG) {
 #pragma unroll
-            for (int hh = 0; hh < kRep; ++hh)
-              *reinterpret_cast<float2*>(&redv[(tg * kRep + hh) * kHeadDim + 2 * dp]) =
-                  make_float2(accv[hh][0], accv[hh][1]);
+              for (int hh = 0; hh < kRep; ++hh)
+                *reinterpret_cast<float2*>(&redv[(tg * kRep + hh) * kHeadDim + 2 * dp]) =
+                    make_float2(accv[hh][0], accv[hh][1]);
+            }
             named_sync(1, kConsumers);
-            const int hh = tid >> 7, d = tid & (kHeadDim - 1);  // 512 threads = kRep heads x 128 dims
-            float o = 0.f;
+            for (int item = tid; item < kRep * kHeadDim; item += kConsumers) {
+              const int hh = item >> 7, d = item & (kHeadDim - 1);
+              float o = 0.f;
 #pragma unroll
-            for (int q = 0; q < kConsumers / 64; ++q) o += redv[(q * kRep + hh) * kHeadDim + d];
-            const size_t cell = ((size_t)h * a->spl + it.s) * kRep + hh;
-            a->att_o[cell * kHeadDim + d] = o;
-            if (d == 0) {
-              a->att_m[cell] = m_run[hh];
-              a->att_l[cell] = l_run[hh];
+              for (int q = 0; q < kTG; ++q) o += redv[(q * kRep + hh) * kHeadDim + d];
+              const size_t cell = ((size_t)h * a->spl + it.s) * kRep + hh;
+              a->att_o[cell * kHeadDim + d] = o;
+              if (d == 0) {
+                a->att_m[cell] = m_run[hh];
+                a->att_l[cell] = l_run[hh];
+              }
             }
             named_sync(1, kConsumers);
             // the last split of this KV head to report merges all of them (kernels.py:198-208)
@@ -415,17 +423,43 @@ __device__ __forceinline__ void attention_phase(const Args* a, const mt_decode_l
             named_sync(1, kConsumers);
             if (bcast) {
               __threadfence();
+              // the splits' statistics into shared memory (one parallel load), then per (head,
+              // dim) the weighted sum of the partials, their loads issued in batches of 16
               const size_t base = (size_t)h * a->spl;
-              float M = -INFINITY;
-              for (int s = 0; s < a->spl; ++s) M = fmaxf(M, __ldcg(a->att_m + (base + s) * kRep + hh));
-              float lsum = 0.f, osum = 0.f;
-              for (int s = 0; s < a->spl; ++s) {
-                const float m = __ldcg(a->att_m + (base + s) * kRep + hh);
-                const float w = m == -INFINITY ? 0.f : expf(m - M);  // a split without tokens adds nothing
-                lsum = fmaf(w, __ldcg(a->att_l + (base + s) * kRep + hh), lsum);
-                osum = fmaf(w, __ldcg(a->att_o + ((base + s) * kRep + hh) * kHeadDim + d), osum);
+              float* st_m = redv + kTG * kRep * kHeadDim;  // [spl][kRep]
+              float* st_w = st_m + a->spl * kRep;          // [spl][kRep]: exp(m_s - M), then / L
+              for (int i = tid; i < a->spl * kRep; i += kConsumers) {
+                st_m[i] = __ldcg(a->att_m + base * kRep + i);
+                st_w[i] = __ldcg(a->att_l + base * kRep + i);
               }
-              a->attn[(h * kRep + hh) * kHeadDim + d] = to_bf16(lsum > 0.f ? osum / lsum : 0.f);
+              named_sync(1, kConsumers);
+              if (tid < kRep) {
+                float M = -INFINITY, lsum = 0.f;
+                for (int s = 0; s < a->spl; ++s) M = fmaxf(M, st_m[s * kRep + tid]);
+                for (int s = 0; s < a->spl; ++s) {
+                  const float m = st_m[s * kRep + tid];
+                  const float w = m == -INFINITY ? 0.f : expf(m - M);  // a split without tokens adds nothing
+                  lsum = fmaf(w, st_w[s * kRep + tid], lsum);
+                  st_m[s * kRep + tid] = w;
+                }
+                const float inv_l = lsum > 0.f ? 1.f / lsum : 0.f;
+                for (int s = 0; s < a->spl; ++s) st_w[s * kRep + tid] = st_m[s * kRep + tid] * inv_l;
+              }
+              named_sync(1, kConsumers);
+              for (int item = tid; item < kRep * kHeadDim; item += kConsumers) {
+                const int hh = item >> 7, d = item & (kHeadDim - 1);
+                float osum = 0.f;
+                for (int s0 = 0; s0 < a->spl; s0 += 16) {
+                  float ov[16];
+#pragma unroll
+                  for (int u = 0; u < 16; ++u)
+                    ov[u] = s0 + u < a->spl ? __ldcg(a->att_o + ((base + s0 + u) * kRep + hh) * kHeadDim + d) : 0.f;
+#pragma unroll
+                  for (int u = 0; u < 16; ++u)
+                    if (s0 + u < a->spl) osum = fmaf(st_w[(s0 + u) * kRep + hh], ov[u], osum);
+                }
+                a->attn[(h * kRep + hh) * kHeadDim + d] = to_bf16(osum);
+              }
               if (tid == 0) a->tickets[h] = 0u;
             }
           }
@@ -433,13 +467,11 @@ __device__ __forceinline__ void attention_phase(const Args* a, const mt_decode_l
   *g_io = g;
 }
 
-// 17 warps x 120 registers = 65,280 of the SM's 65,536: one CTA per SM with no spills (the
-// compiler's default cap for 544 threads is 96, which spills in the attention phase).
-__global__ void __maxnreg__(120) decode_persistent(Args a) {
+__global__ void __launch_bounds__(kConsumers + 32, 1) decode_persistent(Args a) {
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ __align__(8) uint64_t full[kNS];
   __shared__ __align__(8) uint64_t empty[kNS];
-  __shared__ float red[kWarps], redmax[kWarps], redw[kWarps];
+  __shared__ float red[kCW], redmax[kCW], redw[kCW];
   __shared__ __align__(16) uint4 zero16[4];
   __shared__ volatile int cta_abort;
   __shared__ volatile int fail_flag;  // set by any consumer thread whose bounded wait expired
@@ -453,16 +485,16 @@ __global__ void __maxnreg__(120) decode_persistent(Args a) {
   const int G = gridDim.x, c = blockIdx.x;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int kmax = a.inter > kHidden ? a.inter : kHidden;
-  const int xp_bytes = max(kmax / 8 * 16, kRep * (kConsumers / 64) * kHeadDim * 4);
+  const int xp_bytes = max(kmax / 8 * 16, (kRep * kTG * kHeadDim + 2 * kRep * a.spl) * 4);
   uint8_t* ring = smem;
   uint4* xp = reinterpret_cast<uint4*>(smem + (size_t)kNS * a.stage_b);  // [K / 8] fp16 pairs
   float* xsum = reinterpret_cast<float*>(smem + (size_t)kNS * a.stage_b + xp_bytes);  // [K / 32]
-  float* partial = xsum + kmax / 32;  // [kWarps][max_tiles][16]
+  float* partial = xsum + kmax / 32;  // [kCW][max_tiles][16]
 
   if (tid == kConsumers) {
     for (int s = 0; s < kNS; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], kWarps);
+      mbar_init(&empty[s], kCW);
     }
     cta_abort = 0;
     fail_flag = 0;
@@ -474,7 +506,7 @@ __global__ void __maxnreg__(120) decode_persistent(Args a) {
     attn_sm = AttnSmem{ring, full, empty, xp, qs, pr, m_run, l_run, scl, &fail_flag, &bcast};
   }
   __syncthreads();
-  if (warp == kWarps) {
+  if (warp == kCW) {
     if (lane == 0) producer(a, ring, full, empty, &cta_abort);
     return;
   }
@@ -535,7 +567,7 @@ __global__ void __maxnreg__(120) decode_persistent(Args a) {
     for (int p = 0; p < kPhases && ok; ++p) {
       // ---- work that needs no other CTA: clear the row sums, zero the next layer's accumulators
       if (p != P_ATTN)
-        for (int i = tid; i < kWarps * a.max_tiles * 16; i += kConsumers) partial[i] = 0.f;
+        for (int i = tid; i < kCW * a.max_tiles * 16; i += kConsumers) partial[i] = 0.f;
       if (p == P_OUT && L + 1 < a.n_layers) {
         float* nxt = a.acc + (size_t)(L + 1) * kAccPerLayer;
         const int z0 = (int)((long long)c * kAccPerLayer / G), z1 = (int)((long long)(c + 1) * kAccPerLayer / G);
@@ -622,7 +654,7 @@ __global__ void __maxnreg__(120) decode_persistent(Args a) {
       named_sync(1, kConsumers);
       float tot = 0.f, mx = 0.f, mxw = 0.f;
 #pragma unroll
-      for (int w = 0; w < kWarps; ++w) {
+      for (int w = 0; w < kCW; ++w) {
         tot += red[w];
         mx = fmaxf(mx, redmax[w]);
         mxw = fmaxf(mxw, redw[w]);
@@ -722,7 +754,7 @@ __global__ void __maxnreg__(120) decode_persistent(Args a) {
           const int lt = i >> 3, tr = i & 7, o = (t_first + lt) * 8 + tr;
           float gsum = 0.f, usum = 0.f;
 #pragma unroll 4
-          for (int w = 0; w < kWarps; ++w) {
+          for (int w = 0; w < kCW; ++w) {
             gsum += partial[((size_t)w * a.max_tiles + lt) * 16 + tr];
             usum += partial[((size_t)w * a.max_tiles + lt) * 16 + tr + 8];
           }
@@ -734,7 +766,7 @@ __global__ void __maxnreg__(120) decode_persistent(Args a) {
           const int lt = i >> 4, tr = i & 15, o = (t_first + lt) * 16 + tr;
           float sum = 0.f;
 #pragma unroll 4
-          for (int w = 0; w < kWarps; ++w) sum += partial[((size_t)w * a.max_tiles + lt) * 16 + tr];
+          for (int w = 0; w < kCW; ++w) sum += partial[((size_t)w * a.max_tiles + lt) * 16 + tr];
           if (o < rg.n_out) red_add_f32(dst + o, sum * inv_c);
         }
       }
@@ -800,11 +832,11 @@ static int max_tiles_for(int inter, int G) {
   return m;
 }
 
-static size_t smem_bytes(int inter, int zeros, int max_tiles) {
+static size_t smem_bytes(int inter, int zeros, int max_tiles, int spl) {
   const int block_b = kCodeBytes + kScaleBytes + (zeros ? kZeroBytes : 0);
   const int kmax = inter > kHidden ? inter : kHidden;
-  const int xp_bytes = max(kmax / 8 * 16, kRep * (kConsumers / 64) * kHeadDim * 4);
-  return (size_t)kNS * kSB * block_b + xp_bytes + (size_t)kmax / 32 * 4 + (size_t)kWarps * max_tiles * 16 * 4;
+  const int xp_bytes = max(kmax / 8 * 16, (kRep * kTG * kHeadDim + 2 * kRep * spl) * 4);
+  return (size_t)kNS * kSB * block_b + xp_bytes + (size_t)kmax / 32 * 4 + (size_t)kCW * max_tiles * 16 * 4;
 }
 
 static bool shape_ok(int n_layers, int inter) {
@@ -883,7 +915,7 @@ MT_API int mt_decode_layers(const void* layers, int n_layers, int inter, int has
   a.res_a = (__nv_bfloat16*)(base + ws.res_a);
   // a 64-token K + V chunk must fit one ring stage
   if (2 * kChunk * kHeadDim * 2 > a.stage_b) return kBadArgument;
-  const size_t smem = smem_bytes(inter, a.zeros, a.max_tiles);
+  const size_t smem = smem_bytes(inter, a.zeros, a.max_tiles, a.spl);
   if (smem > 227 * 1024) return kBadArgument;
   cudaError_t e = cudaFuncSetAttribute(decode_persistent, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return (int)e;

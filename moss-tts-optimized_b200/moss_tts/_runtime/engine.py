@@ -127,7 +127,7 @@ class DecodeEngine:
     """Static-buffer decode step for one sequence over (a shard of) ``DecoderWeights``."""
 
     def __init__(self, weights: DecoderWeights, max_length: int = 1024, *, splits: int | None = None,
-                 pdl: bool = True, tp: TensorParallel | None = None, persistent: bool = True):
+                 pdl: bool = True, tp: TensorParallel | None = None, persistent: bool | None = None):
         cfg = weights.cfg
         cfg.validate()
         self.w, self.cfg, self.max_length = weights, cfg, max_length
@@ -192,8 +192,11 @@ class DecodeEngine:
         if world > 1 and os.environ.get("MT_TP_EXCHANGE", "p2p") != "nccl" and weights.layers[0].out.quantized \
                 and all(self._packed_ok(p, False) for lw in weights.layers for p in (lw.out, lw.down)):
             self.exchange = PeerExchange(self.tp, 2 * len(weights.layers), h, dev)
-        # Single GPU, W4 weights: the whole layer stack is one persistent launch (mt_decode_layers)
-        self.persistent = persistent and world == 1 and os.environ.get("MT_PERSISTENT", "1") != "0" and all(
+        # Single GPU, W4 weights: the whole layer stack can run as one persistent launch
+        # (mt_decode_layers); None follows MT_PERSISTENT (default: the per-sublayer launch chain)
+        if persistent is None:
+            persistent = os.environ.get("MT_PERSISTENT", "0") == "1"
+        self.persistent = persistent and world == 1 and all(
             self._packed_ok(p, paired) for lw in weights.layers
             for p, paired in ((lw.qkv, False), (lw.out, False), (lw.gate_up, True), (lw.down, False)))
         if self.persistent:

@@ -45,7 +45,8 @@ def _one_layer(dev, max_length):
     dc = small_vocab(DecoderConfig(), vocab=64, layers=1)
     host = synthetic.decoder_weights(dc, seed=5, layers=1)  # the layer of tests/golden/layer.npz
     w = DecoderWeights.from_host(dc, host, dev)
-    return DecodeEngine(w, max_length=max_length), DecodeEngine(w, max_length=max_length, persistent=False)
+    return (DecodeEngine(w, max_length=max_length, persistent=True),
+            DecodeEngine(w, max_length=max_length, persistent=False))
 
 
 def _workspace_clean(eng):
@@ -104,7 +105,8 @@ def test_persistent_engine_steps_match_launch_chain(cuda_device):
     (a second persistent engine, one of them replaying a captured graph)."""
     dc = small_vocab(DecoderConfig(), vocab=2048, layers=2)
     w = DecoderWeights.from_host(dc, synthetic.decoder_weights(dc, seed=7), cuda_device)
-    pers, again, chain = (DecodeEngine(w, max_length=128), DecodeEngine(w, max_length=128),
+    pers, again, chain = (DecodeEngine(w, max_length=128, persistent=True),
+                          DecodeEngine(w, max_length=128, persistent=True),
                           DecodeEngine(w, max_length=128, persistent=False))
     assert pers.persistent and again.persistent and not chain.persistent
     again.capture()
@@ -116,9 +118,12 @@ def test_persistent_engine_steps_match_launch_chain(cuda_device):
         b = again.step(ids, step, step + 1, -1).reshape(-1).cpu()
         c = chain.step(ids, step, step + 1, -1).reshape(-1).cpu()
         assert torch.equal(a, b) and torch.equal(pers.hidden, again.hidden), step
-        mx, rel, excess = _errors(_host(pers.hidden), _host(chain.hidden))
+        # each engine evolves its own KV cache over the steps, so the two evaluation orders drift
+        # apart as in the reference-model test: bar 5e-2 + 2e-2 |ref| there and here
+        ref = _host(chain.hidden)
+        mx = float(np.abs(_host(pers.hidden) - ref).max())
         worst = max(worst, mx)
-        assert excess <= 0, (step, mx)
+        assert np.all(np.abs(_host(pers.hidden) - ref) <= 5e-2 + 2e-2 * np.abs(ref)), (step, mx)
         differ += int((a != c).sum())
         ids = c
     print(f"2 layers, 16 steps: persistent vs launch chain hidden max abs {worst:.4g}; {differ} ids differ")
