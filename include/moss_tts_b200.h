@@ -295,6 +295,22 @@ int mt_attention_decode_noalloc(const void* qkv, const void* q_norm, const void*
                                 void* stream);
 
 /*
+ * Prompt prefill, the non-projection parts of the reference's batched prompt pass
+ * (FastLLM.prefill / _prefill_forward, src/moss_tts/_runtime/llm.py:204-226, 303-318; the
+ * fused prefill_qkv.project, prefill_qkv.py:7-69). Prompt row t of n sits at position
+ * start + t; the cache is one sequence's bf16 [nkv, max_len, 128] (start + n <= max_len).
+ * mt_prefill_qk_rope_kv: qkv bf16 [n, (nq + 2 nkv) * 128] -> head RMSNorm + rotate-half RoPE,
+ * q_out bf16 [n, nq, 128], K/V rows written into the cache.
+ * mt_prefill_attention: causal GQA attention of q bf16 [n, nq, 128] over cache rows
+ * 0..start + t for row t, out bf16 [n, nq * 128] (fp32 softmax, scale 1/sqrt(128)).
+ */
+int mt_prefill_qk_rope_kv(const void* qkv, const void* q_norm, const void* k_norm, const void* cos_tab,
+                          const void* sin_tab, int start, void* q_out, void* k_cache, void* v_cache, int n,
+                          int nq, int nkv, int max_len, float eps, int flags, void* stream);
+int mt_prefill_attention(const void* q, const void* k_cache, const void* v_cache, void* out, int start, int n,
+                         int nq, int nkv, int max_len, int flags, void* stream);
+
+/*
  * Output heads of one decode step with greedy selection: final add_rmsnorm of
  * (x + residual), logits of the n_text text-head rows and n_cb audio codebooks of `vocab`
  * rows each, argmax with the first-index tie rule, delay-pattern masks, next token ids

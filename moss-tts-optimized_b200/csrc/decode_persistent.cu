@@ -167,9 +167,10 @@ __device__ void producer(const Args& a, uint8_t* ring, uint64_t* full, uint64_t*
     if (gg < kNS) return true;
     uint64_t* bar = &empty[gg % kNS];
     const unsigned parity = (unsigned)(((gg / kNS) - 1) & 1);
+    unsigned long long t0 = globaltimer_ns();
     for (long i = 0; i < kSpinLimit; ++i) {
-      if (mbar_try_wait(bar, parity)) return true;
-      if (*cta_abort) return false;
+      if (mbar_try_wait_sleep(bar, parity, 2000)) return true;  // sleeps instead of spinning
+      if (*cta_abort || globaltimer_ns() - t0 > kWaitDeadlineNs) return false;
     }
     return false;
   };
@@ -714,10 +715,9 @@ __global__ void __launch_bounds__(kConsumers + 32, 1) decode_persistent(Args a) 
       for (int st = 0; st < stages; ++st) {
         if (st > 0) {
           jj += kSB;
-          if (jj >= S) {
-            const int q = jj / S;
-            tt += q;
-            jj -= q * S;
+          while (jj >= S) {  // S >= kSB for every shape but the smallest: one subtraction
+            jj -= S;
+            ++tt;
           }
         }
         if (!wait_full(g)) {

@@ -28,9 +28,32 @@ static __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, unsigned par
       : "memory");
   return ok != 0;
 }
+// try_wait with a suspend-time hint: a thread whose phase is not complete sleeps (up to
+// `hint_ns`) instead of spinning, so waiting warps do not take issue slots from working ones.
+static __device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, unsigned parity, unsigned hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
+// Longest wait for one pipeline phase before a kernel gives up (its copies or its partner
+// warps are stuck): far above any healthy wait, short enough to return control.
+static constexpr unsigned long long kWaitDeadlineNs = 200ull * 1000 * 1000;
+
 static __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, unsigned parity) {
-  for (long i = 0; i < kSpinLimit; ++i)
-    if (mbar_try_wait(bar, parity)) return true;
+  if (mbar_try_wait(bar, parity)) return true;
+  unsigned long long t0;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+  for (long i = 0; i < kSpinLimit; ++i) {
+    if (mbar_try_wait_sleep(bar, parity, 2000)) return true;
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    if (t - t0 > kWaitDeadlineNs) return false;
+  }
   return false;
 }
 static __device__ __forceinline__ void bulk_copy(void* dst, const void* src, unsigned bytes, uint64_t* bar) {

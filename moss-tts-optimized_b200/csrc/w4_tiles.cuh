@@ -84,27 +84,38 @@ __device__ __forceinline__ BlockRegs load_block(const uint8_t* blk, int lane, bo
   return b;
 }
 
+// NACC independent accumulators: the 17 mma of a block form NACC dependency chains (mma.sync
+// has a long latency; the chains let one warp keep several in flight).
+template <int NACC = 2>
 __device__ __forceinline__ void block_dot(const BlockRegs& bk, const uint32_t (&bl)[16], const uint32_t (&bh)[16],
                                           uint32_t bz0, uint32_t bz1, float& va, float& vb) {
   const uint32_t wa[8] = {bk.c0.x, bk.c0.y, bk.c0.z, bk.c0.w, bk.c1.x, bk.c1.y, bk.c1.z, bk.c1.w};
   const uint32_t wb[8] = {bk.c2.x, bk.c2.y, bk.c2.z, bk.c2.w, bk.c3.x, bk.c3.y, bk.c3.z, bk.c3.w};
-  float d[2][4] = {};  // two independent accumulators halve the mma dependency chains
+  float d[NACC][4] = {};
   // zero points: A = (z[r][2c], 16 z[r][2c+1]) (and row r + 8) as fp16 subnormals against
   // B = -(c sum x) of groups 2c / 2c + 1 split into fp16 hi and lo parts
   const uint32_t za = __byte_perm(bk.zz, 0, 0x4040) & 0x00F0000Fu, zb = __byte_perm(bk.zz, 0, 0x4141) & 0x00F0000Fu;
-  mma_f16(d[1], za, zb, za, zb, bz0, bz1);
+  mma_f16(d[NACC - 1], za, zb, za, zb, bz0, bz1);
 #pragma unroll
   for (int u = 0; u < 8; ++u) {
     const uint32_t* bsel = u < 4 ? bl : bh;
     const int bi = (u & 3) * 4;
     const uint32_t sa = wa[u] >> 8, sb = wb[u] >> 8;
-    mma_f16(d[0], wa[u] & 0x000F000Fu, wb[u] & 0x000F000Fu, wa[u] & 0x00F000F0u, wb[u] & 0x00F000F0u, bsel[bi],
-            bsel[bi + 1]);
-    mma_f16(d[1], sa & 0x000F000Fu, sb & 0x000F000Fu, sa & 0x00F000F0u, sb & 0x00F000F0u, bsel[bi + 2], bsel[bi + 3]);
+    mma_f16(d[(2 * u) % NACC], wa[u] & 0x000F000Fu, wb[u] & 0x000F000Fu, wa[u] & 0x00F000F0u, wb[u] & 0x00F000F0u,
+            bsel[bi], bsel[bi + 1]);
+    mma_f16(d[(2 * u + 1) % NACC], sa & 0x000F000Fu, sb & 0x000F000Fu, sa & 0x00F000F0u, sb & 0x00F000F0u,
+            bsel[bi + 2], bsel[bi + 3]);
+  }
+#pragma unroll
+  for (int i = 1; i < NACC; ++i) {
+    d[0][0] += d[i][0];
+    d[0][1] += d[i][1];
+    d[0][2] += d[i][2];
+    d[0][3] += d[i][3];
   }
   // column 2c = group 2c (element 0: row r, element 2: row r + 8), column 2c + 1 = group 2c + 1
-  va = fmaf(__uint_as_float(bk.sw.x & 0xFFFF0000u), d[0][1] + d[1][1], __uint_as_float(bk.sw.x << 16) * (d[0][0] + d[1][0]));
-  vb = fmaf(__uint_as_float(bk.sw.y & 0xFFFF0000u), d[0][3] + d[1][3], __uint_as_float(bk.sw.y << 16) * (d[0][2] + d[1][2]));
+  va = fmaf(__uint_as_float(bk.sw.x & 0xFFFF0000u), d[0][1], __uint_as_float(bk.sw.x << 16) * d[0][0]);
+  vb = fmaf(__uint_as_float(bk.sw.y & 0xFFFF0000u), d[0][3], __uint_as_float(bk.sw.y << 16) * d[0][2]);
   va += __shfl_xor_sync(0xffffffffu, va, 1);
   vb += __shfl_xor_sync(0xffffffffu, vb, 1);
   va += __shfl_xor_sync(0xffffffffu, va, 2);

@@ -39,6 +39,10 @@
 
 #include "w4_tiles.cuh"
 
+#ifndef MT_NACC
+#define MT_NACC 2
+#endif
+
 namespace mt {
 
 __device__ int g_error_word;  // non-zero after a bounded wait expired (see mt_read_error_word)
@@ -387,10 +391,9 @@ __global__ void __launch_bounds__(kWarps * 32 + 32, 1) w4a16_packed(StreamArgs a
 #pragma unroll
       for (int m = 0; m < BPW; ++m) {
         jj[m] += SB;
-        if (jj[m] >= S) {
-          const int q = jj[m] / S;
-          tt[m] += q;
-          jj[m] -= q * S;
+        while (jj[m] >= S) {  // S >= SB for K >= 4096: one subtraction
+          jj[m] -= S;
+          ++tt[m];
         }
       }
     }
@@ -412,7 +415,7 @@ __global__ void __launch_bounds__(kWarps * 32 + 32, 1) w4a16_packed(StreamArgs a
       if (live) {
         if (jj[m] != cur_j) load_b(jj[m]);
         float va, vb;
-        block_dot(bk, bl, bh, bz0, bz1, va, vb);
+        block_dot<MT_NACC>(bk, bl, bh, bz0, bz1, va, vb);
         if (c == 0) {
           float* pp = partial + ((size_t)warp * max_tiles + (tt[m] - t_first)) * 16;
           pp[r] += va;

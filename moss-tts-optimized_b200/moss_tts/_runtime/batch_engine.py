@@ -13,11 +13,11 @@ length and delay length (ragged static KV caches). Per step, all PDL-chained and
     heads: add + final RMSNorm, text/audio logits (plain bf16 GEMMs, as the reference's
            F.linear heads), greedy ids + delay masks per sequence  -> next_ids [B, 33]
 
-Projections: one sequence runs the batch-1 packed GEMV; from ``gemm_min_batch`` rows the
-W4A16 projections run on the tcgen05 GEMM over its load-time packed layout
-(``mt_w4a16_gemm_pack`` / ``mt_w4a16_gemm_packed``) after a separate RMSNorm;
-below it the GPTQ-layout GEMV with its fused norm prologue (``mt_w4a16_linear``, up to 8
-rows). Inputs live in one int64 control block ``[ids B*33 | positions B | audio_length B |
+Projections: up to 8 sequences run the GPTQ-layout GEMV with its fused norm prologue
+(``mt_w4a16_linear``, which reads each weight once for all rows); from ``gemm_min_batch``
+(default 9) rows the W4A16 projections run on the tcgen05 GEMM over its load-time packed
+layout (``mt_w4a16_gemm_pack`` / ``mt_w4a16_gemm_packed``) after a separate RMSNorm, whose
+per-chunk pipeline costs more than it saves below that. Inputs live in one int64 control block ``[ids B*33 | positions B | audio_length B |
 delay_length B]`` (one host-to-device copy per step); the result is ``next_ids``.
 """
 import torch
@@ -31,7 +31,7 @@ class BatchDecodeEngine:
     """Static-buffer decode step for ``batch`` sequences over (a shard of) W4A16 ``DecoderWeights``."""
 
     def __init__(self, weights: DecoderWeights, batch: int, max_length: int = 4096, *, pdl: bool = True,
-                 tp: TensorParallel | None = None, gemm_min_batch: int = 2):
+                 tp: TensorParallel | None = None, gemm_min_batch: int = 9):
         cfg = weights.cfg
         cfg.validate()
         if batch < 1 or batch > 128:

@@ -144,11 +144,24 @@ class FastLLM:
 
     @torch.inference_mode()
     def prefill(self, ids):
-        """Process a ``[1, n, 33]`` prompt token by token through the decode step and return the
-        last token's ``(text logits [1, V], audio logits [32, 1024])`` (``llm.py:303-318``)."""
-        if ids.shape[0] != 1 or ids.shape[1] >= self.max_length:
+        """Run a ``[1, n, 33]`` prompt as one batched causal pass at positions 0..n-1 (filling
+        the KV cache) and return the last row's ``(text logits [1, V], audio logits [32, 1024])``
+        (``llm.py:303-318``). W4A16 weights on one GPU run the batched prefill kernels
+        (``prefill.Prefill``); otherwise the prompt goes through the decode step row by row."""
+        ids = torch.as_tensor(ids)
+        if ids.dim() != 3 or ids.shape[0] != 1 or ids.shape[1] >= self.max_length:
             raise ValueError("Batch must be one and prompt must fit the KV capacity")
+        e = self.engine
+        batched = e.tp.world == 1 and self.model.head_text is not None and all(
+            p.quantized for lw in self.model.layers for p in (lw.qkv, lw.out, lw.gate_up, lw.down))
+        if batched:
+            from .prefill import Prefill
+            n = ids.shape[1]
+            runner = self.prefill_graphs.get("runner")
+            if runner is None or runner.max_tokens < n:
+                runner = self.prefill_graphs["runner"] = Prefill(e, max_tokens=max(512, n))
+            return runner.run(ids.to(e.device))
         for t in range(ids.shape[1]):
-            self.engine.set_inputs(ids[0, t], t, 1, -1)
-            self.engine.launch_step()
-        return self._full_text_logits(), self.engine.audio_logits.view(-1, self.cfg.audio_vocab_size)
+            e.set_inputs(ids[0, t], t, 1, -1)
+            e.launch_step()
+        return self._full_text_logits(), e.audio_logits.view(-1, self.cfg.audio_vocab_size)

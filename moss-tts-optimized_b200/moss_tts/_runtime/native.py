@@ -46,6 +46,8 @@ SIGNATURES = {
     "mt_attention_decode_noalloc": ([_P] * 9 + [_I] * 5 + [_F, _P, _I, _P], _I),
     "mt_decode_layers_workspace": ([_I, _I, _LLP], _I),
     "mt_decode_layers": ([_P, _I, _I, _I, _P, _P, _P, _P, _I, _F, _P, _P, _P, _P, _I, _P], _I),
+    "mt_prefill_qk_rope_kv": ([_P, _P, _P, _P, _P, _I, _P, _P, _P, _I, _I, _I, _I, _F, _I, _P], _I),
+    "mt_prefill_attention": ([_P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P], _I),
     "mt_heads_greedy": ([_P, _P, _P, _F] + [_P] * 11 + [_I] * 11 + [_P], _I),
 }
 

@@ -59,6 +59,7 @@ class Decoder:
         # FastLLM keeps the two audio-phase rows of the text head and the first
         # 1024 rows of each audio head (llm.py:188-191).
         self.text_head = to_f32(weights["head_text"][self.text_ids])
+        self.full_text_head = weights["head_text"]  # bf16 bits [V, H], for prefill / full_step
         av = cfg["audio_vocab_size"]
         self.audio_heads = to_f32(weights["head_audio"][:, :av].reshape(-1, cfg["hidden_size"]))
 
@@ -111,6 +112,19 @@ class Decoder:
             cfg["audio_assistant_delay_slot_token_id"], cfg["audio_end_token_id"], cfg["n_vq"],
             cfg["audio_vocab_size"], cfg["audio_pad_code"])
         return nxt, text, audio, h
+
+    def prefill(self, ids):
+        """``FastLLM.prefill`` (``llm.py:303-318``): the prompt ``ids [n, 1 + n_vq]`` at positions
+        0..n-1, causal attention (row t attends rows 0..t), cache filled; the last row's
+        final-norm hidden state gives the full text-head logits ``[V]`` and the audio logits
+        ``[n_vq, 1024]`` (``llm.py:207``). Row by row, which is the causal pass's arithmetic."""
+        ids = np.asarray(ids).reshape(-1, 1 + self.cfg["n_vq"])
+        h = None
+        for t in range(ids.shape[0]):
+            h = self.hidden(ids[t], t)
+        text = ops.linear(h, to_f32(self.full_text_head))
+        audio = ops.linear(h, self.audio_heads).reshape(self.cfg["n_vq"], -1)
+        return text, audio, h
 
     def fill_cache(self, k, v):
         """Install caller-provided cache rows (``[layers, n_kv, P, d]`` each)."""

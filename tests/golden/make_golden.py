@@ -270,12 +270,9 @@ def audio_schedule(step: int):
     return audio_length, delay
 
 
-def decode_fixture(steps=64):
-    """Teacher-forced greedy decode of a 2-layer, full-width, small-vocab model through
-    the reference's MossTTSDelayModel, with FastLLM's head/mask semantics."""
-    dc = config_mod.small_vocab(config_mod.DecoderConfig(), vocab=2048, layers=2)
-    weights = synthetic.decoder_weights(dc, seed=7)
-    qcfg = qwen3_config(layers=2, vocab=dc.vocab_size)
+def reference_model(dc, weights):
+    """The reference's MossTTSDelayModel (bf16, CPU, SDPA attention) holding the synthetic weights."""
+    qcfg = qwen3_config(layers=dc.num_layers, vocab=dc.vocab_size)
     mcfg = MossTTSDelayConfig(language_config=qcfg.to_dict(), n_vq=32, audio_vocab_size=1024,
                               pad_token_id=dc.pad_token_id, im_start_token_id=dc.im_start_token_id,
                               im_end_token_id=dc.im_end_token_id,
@@ -295,6 +292,36 @@ def decode_fixture(steps=64):
     model.lm_heads[0].weight.data = from_bits(weights["head_text"])
     for i in range(32):
         model.lm_heads[i + 1].weight.data = from_bits(weights["head_audio"][i])
+    return model, mcfg
+
+
+def prefill_fixture(n=40):
+    """FastLLM.prefill of an n-token prompt (llm.py:303-318 without a captured bucket): the
+    2-layer model of the decode fixture runs the whole prompt as one causal pass at positions
+    0..n-1; the last row gives the full text-head logits and the 32 x 1024 audio logits."""
+    dc = config_mod.small_vocab(config_mod.DecoderConfig(), vocab=2048, layers=2)
+    weights = synthetic.decoder_weights(dc, seed=7)
+    model, _ = reference_model(dc, weights)
+    rng = np.random.Generator(np.random.PCG64(79))
+    ids = torch.full((1, n, 33), 1024, dtype=torch.long)
+    ids[0, :, 0] = torch.from_numpy(rng.integers(0, dc.vocab_size - 16, size=n))
+    ids[0, :, 1:] = torch.from_numpy(rng.integers(0, 1025, size=(n, 32)))
+    audio_heads = torch.cat([h.weight[:1024] for h in model.lm_heads[1:]], 0)
+    with torch.no_grad():
+        emb = model._compute_input_embeddings(ids)
+        pos = torch.arange(n)
+        h = model.language_model(inputs_embeds=emb, position_ids=pos[None], use_cache=False).last_hidden_state[0, -1]
+        text = torch.nn.functional.linear(h, model.lm_heads[0].weight)
+        audio = torch.nn.functional.linear(h, audio_heads).view(32, 1024)
+    return {"ids": ids.numpy(), "hidden": bits(h), "text": bits(text), "audio": bits(audio)}
+
+
+def decode_fixture(steps=64):
+    """Teacher-forced greedy decode of a 2-layer, full-width, small-vocab model through
+    the reference's MossTTSDelayModel, with FastLLM's head/mask semantics."""
+    dc = config_mod.small_vocab(config_mod.DecoderConfig(), vocab=2048, layers=2)
+    weights = synthetic.decoder_weights(dc, seed=7)
+    model, mcfg = reference_model(dc, weights)
     # FastLLM's decode heads (llm.py:188-191).
     text_ids = torch.tensor([dc.audio_assistant_gen_slot_token_id,
                              dc.audio_assistant_delay_slot_token_id])
@@ -342,6 +369,9 @@ def decode_fixture(steps=64):
 
 
 def main():
+    if sys.argv[1:] == ["prefill"]:  # only the prefill fixture
+        np.savez_compressed(HERE / "prefill.npz", **prefill_fixture())
+        return
     q, big, wbig = quant_fixture()
     np.savez_compressed(HERE / "quant.npz", **q)
     np.savez_compressed(HERE / "linear.npz", **linear_fixture(big, wbig))
@@ -350,6 +380,7 @@ def main():
     np.savez_compressed(HERE / "layer.npz", **layer_fixture())
     np.savez_compressed(HERE / "mlp.npz", **mlp_fixture())
     np.savez_compressed(HERE / "decode.npz", **decode_fixture())
+    np.savez_compressed(HERE / "prefill.npz", **prefill_fixture())
     for f in sorted(HERE.glob("*.npz")):
         print(f.name, f.stat().st_size)
 

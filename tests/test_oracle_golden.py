@@ -221,3 +221,23 @@ def test_decode_steps_against_reference_model():
     # 64 steps x 33 channels; the oracle and the reference differ only in fp32
     # summation order and softmax evaluation, so a few near-ties flip
     assert mismatched <= 0.02 * g["next"].size, mismatched
+
+
+@pytest.mark.slow
+def test_prefill_against_reference_model():
+    """The reference's batched prompt pass (FastLLM.prefill semantics, a 40-token prompt through
+    the 2-layer MossTTSDelayModel): the oracle's row-by-row causal pass gives the same last
+    hidden state and logits. The reference evaluates its prompt pass with bf16 matmul and
+    attention outputs on the CPU, rounding where the decode kernels keep fp32, so the bar is
+    that of the reference-model decode test (5e-2 + 2e-2 |ref|) for the hidden state, and for
+    the logits (dot products of 4096 such values) 0.1 + 2e-2 |ref| with a relative RMS <= 2%."""
+    g = golden("prefill")
+    dc = small_vocab(DecoderConfig(), vocab=2048, layers=2)
+    w = synthetic.decoder_weights(dc, seed=7)
+    dec = omodel.Decoder(w, dc.as_dict(), max_length=64)
+    text, audio, h = dec.prefill(g["ids"][0])
+    for got, want, atol in ((h, g["hidden"], 5e-2), (text, g["text"], 0.1), (audio, g["audio"], 0.1)):
+        want = f(want).reshape(np.asarray(got).shape)
+        err = np.abs(np.asarray(got, np.float64) - want)
+        assert np.all(err <= atol + 2e-2 * np.abs(want)), err.max()
+        assert np.sqrt(np.mean(err ** 2) / np.mean(want.astype(np.float64) ** 2)) <= 0.02
