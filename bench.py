@@ -46,6 +46,7 @@ def parse():
     ap.add_argument("--layers", type=int, default=36, help=argparse.SUPPRESS)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-bf16", action="store_true", help="skip the BF16-preset step timing")
+    ap.add_argument("--no-prefill", action="store_true", help="skip the 512-token prefill timing")
     ap.add_argument("--batch-sweep", default=None, metavar="B,B,...",
                     help="config 4: batched decode of B sequences with ragged contexts (uniform in "
                          "[256, 4096], seeded) for each listed B; prints one JSON line per B")
@@ -411,7 +412,8 @@ def batch_sweep(args, rank, world, local):
     length drawn uniformly from [256, 4096] (seeded), for every B of --batch-sweep. One step
     advances every sequence by one token; the metric is tokens/s = B x steps/s (device-resident
     inputs, CUDA graph with device-side advance, CUDA events, max over ranks). B = 1 runs the
-    batch-1 engine; larger B the batched engine (tcgen05 GEMM projections)."""
+    batch-1 engine; larger B the batched engine (two-row packed GEMV below 5 sequences, tcgen05
+    GEMM projections from 5)."""
     import torch
     import torch.distributed as dist
 
@@ -489,7 +491,8 @@ def batch_sweep(args, rank, world, local):
                     "config": {"workload": "config4: 36-layer 8B-shaped decoder, W4A16 G32, batched greedy decode, "
                                            "per-sequence context uniform in [256, 4096] (seeded)",
                                "parallelism": f"tp{world}", "projections": "packed GEMV" if B == 1 else
-                               ("tcgen05 GEMM" if getattr(eng, "gemm", False) else "GPTQ-layout GEMV"),
+                               ("tcgen05 GEMM" if getattr(eng, "gemm", False) else
+                                "packed two-row GEMV" if getattr(eng, "rows_packed", False) else "GPTQ-layout GEMV"),
                                "mean_context": round(mean_ctx, 1)},
                     "step_bytes_per_gpu": step_bytes,
                     "hbm_roofline_frac": round(step_bytes / (ms * 1e-3) / 1e9 / peak, 4), "peak_gbs": peak,
@@ -633,6 +636,37 @@ def main():
         torch.cuda.synchronize(dev)
         kernel_us = k0.elapsed_time(k1) * 1000 / (reps * len(weights.layers))
         del kgraph
+
+        # ---------------- prefill of the 512-token prompt (FastLLM.prefill, one GPU)
+        prefill = None
+        if world == 1 and not args.no_prefill:
+            g2 = torch.Generator().manual_seed(3)
+            pids = torch.full((1, PROMPT, 33), 1024, dtype=torch.long)
+            pids[0, :, 0] = torch.randint(0, cfg.vocab_size, (PROMPT,), generator=g2)
+            pids[0, :, 1:] = torch.randint(0, 1025, (PROMPT, 32), generator=g2)
+            pids = pids.to(dev)
+            preps, pms = 5, {}
+            for mode in ("bf16", "dequant", "w4"):
+                llm.prefill_mode = mode
+                for _ in range(2):
+                    llm.prefill(pids)
+                torch.cuda.synchronize(dev)
+                p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                p0.record(stream)
+                for _ in range(preps):
+                    llm.prefill(pids)
+                p1.record(stream)
+                torch.cuda.synchronize(dev)
+                pms[mode] = p0.elapsed_time(p1) / preps
+                llm.prefill_graphs.clear()
+            llm.prefill_mode = "auto"
+            prefill = {"prompt_tokens": PROMPT, "ms": round(pms["bf16"], 3),
+                       "tokens_per_s": round(PROMPT / pms["bf16"] * 1000, 1), "reps": preps,
+                       "path": "resident bf16 weights (bit-exact W4 dequantization, once) + bf16 GEMM (cuBLAS), "
+                               "prefill QK-norm/RoPE/KV and causal attention kernels",
+                       "dequant_per_call_ms": round(pms["dequant"], 3), "w4_gemm_ms": round(pms["w4"], 3),
+                       "reference_published_ms": 6.83,
+                       "reference_note": "H200 NVL, BF16 prefill of the G32 preset (docs/benchmark.json:85)"}
     # the BF16 preset (config 3 is timed in both formats), after releasing the W4A16 engine's graphs
     bf16 = None
     if not args.no_bf16:
@@ -661,7 +695,7 @@ def main():
         v, setup = cpu_oracle_run(args.layers, cpu_steps, 1, threads)
         cpu = {"value": round(v, 4), "unit": UNIT, "cores": threads, "kind": "port",
                "sample": cpu_sample_text(args.layers, cpu_steps, threads), "setup_s": round(setup, 1)}
-    launches = 2 + 5 * args.layers
+    launches = 3 + 5 * args.layers  # embedding, 5 per layer, heads, the device advance
     line = {
         "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True,
@@ -677,6 +711,7 @@ def main():
                      "launch_us": round(kernel_us, 3)},
         "cpu_baseline": cpu,
         "bf16": bf16,
+        "prefill": prefill,
         "clocks": clocks.summary(),
         "gpu_launches": launches * args.steps,
         "status": status,

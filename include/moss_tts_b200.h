@@ -67,6 +67,21 @@ int mt_dequant_w4(const void* qweight, const void* scales, const void* qzeros, v
 int mt_static_scales(const void* w, int dtype, void* out, int n, int k, void* stream);
 
 /*
+ * One block of the GPTQ column loop: columns [start, start + cols) (cols <= 128) of the
+ * permuted weights for n rows. w fp32 [n, cols] (the block, updated in place), errors fp32
+ * [n, cols] (out: (w - bf16(code * s)) / hinv[c][c] per column), codes int8 [n, k] (written at
+ * the original column perm[start + c]), scales bf16 [n, k / group], hinv fp32 [k, k] (upper
+ * Cholesky factor of the damped, permuted inverse Hessian), perm int64 [k]. Per column:
+ * code = clamp(rint(w / s), -7, 7), then w[:, j] -= err * hinv[c][j] for j >= c, each
+ * operation rounded on its own. The caller applies errors @ hinv[block, after] to the
+ * columns after the block.
+ * Replaces the per-column Triton _column launches of calibrated_quant.gptq
+ * (src/moss_tts/_runtime/calibrated_quant.py:15-33, 65-84).
+ */
+int mt_gptq_block(void* w, void* errors, void* codes, const void* scales, const void* hinv, const void* perm,
+                  int start, int cols, int n, int k, int group, void* stream);
+
+/*
  * W4A16 G32 decode GEMV, batch 1..8: y[b, :] = bf16(x'[b, :] . W^T) with fp32 accumulation,
  * where x' = x, or RMSNorm(x) (mode NORM), or RMSNorm(bf16(x + residual)) (mode NORM|ADD,
  * also storing bf16(x + residual) into `summed` when non-NULL). With mode PAIRED, y has
@@ -105,8 +120,8 @@ int mt_w4a16_pack(const void* qweight, const void* scales, const void* qzeros, i
 
 /*
  * Batch-1 W4A16 GEMV over packed weights, same math and modes as mt_w4a16_linear (replaces
- * the same reference projections): bulk-copy streaming of the packed tiles, dequantization
- * into bf16 pairs feeding mma.sync m16n8k16, split-K over the SMs. `workspace` holds
+ * the same reference projections): bulk-copy streaming of the packed tiles, codes as exact
+ * fp16 operands of mma.sync m16n8k16, split-K over the SMs. `workspace` holds
  * mt_w4a16_packed_size's workspace bytes, zero-filled by the caller once before first
  * use; every call leaves it zeroed again. Calls that share a workspace must be ordered on
  * one stream. All pointers 16-byte aligned.
@@ -114,6 +129,17 @@ int mt_w4a16_pack(const void* qweight, const void* scales, const void* qzeros, i
 int mt_w4a16_linear_packed(const void* x, const void* residual, const void* norm_w, float eps,
                            void* summed, const void* packed, int has_zeros, void* y, int n, int k,
                            int mode, void* workspace, int flags, void* stream);
+
+/*
+ * The same projection for `rows` (1..64) activation rows: x, residual and summed [rows, k],
+ * y [rows, n (n / 2 when PAIRED)], row-major; the RMSNorm is per row. Two rows share one
+ * pass over the weights (the activation rows ride in separate columns of the same mma), so
+ * a pair costs about one batch-1 call; an odd last row runs the batch-1 kernel. Used for
+ * the batched decode step of 2-4 sequences; replaces the same reference projections.
+ */
+int mt_w4a16_linear_packed_rows(const void* x, const void* residual, const void* norm_w, float eps,
+                                void* summed, const void* packed, int has_zeros, void* y, int rows,
+                                int n, int k, int mode, void* workspace, int flags, void* stream);
 
 /*
  * Tensor-parallel exchange over peer memory (NVLink), replacing the NCCL all-reduce after a
@@ -353,6 +379,27 @@ int mt_heads_select(const void* text_logits, const void* audio_logits, const voi
                     const void* audio_length, const void* delay_length, void* next_ids, int batch,
                     int n_text, int n_cb, int vocab, int cb_offset, int n_vq, int delay_slot_id,
                     int audio_end_id, int pad_code, int text_owner, int flags, void* stream);
+
+/*
+ * Sampled next ids for `batch` sequences from their head logits: the non-greedy half of
+ * FastLLM._decode (src/moss_tts/_runtime/llm.py:280-287) with the reference sampler
+ * sample_topk (llm.py:10-19) per channel -- x = float(logit) / temperature, the top_k largest
+ * (ties in ascending index order), softmax over them, entries whose cumulative probability
+ * before them exceeds top_p dropped, one draw in proportion to the rest -- then the delay
+ * masks. Text: (text_temperature, text_top_k, text_top_p) over n_text logits, the index mapped
+ * through text_ids; audio: (audio_*) over each codebook's `vocab` logits (vocab <= 1024). A
+ * temperature <= 0 selects the argmax (first index on ties). The uniform of each draw is
+ * Philox4x32-10 keyed by seed[b] (uint64) with counter (channel, position[b]): reproducible
+ * per (seed, position, channel). position, audio_length, delay_length int64 [batch];
+ * next_ids int64 [batch, 1 + n_vq] as mt_heads_select writes it. top_k in 1..64.
+ */
+int mt_heads_sample(const void* text_logits, const void* audio_logits, const void* text_ids,
+                    const void* position, const void* audio_length, const void* delay_length,
+                    const void* seed, void* next_ids, int batch, int n_text, int n_cb, int vocab,
+                    int cb_offset, int n_vq, int delay_slot_id, int audio_end_id, int pad_code,
+                    int text_owner, float text_temperature, int text_top_k, float text_top_p,
+                    float audio_temperature, int audio_top_k, float audio_top_p, int flags,
+                    void* stream);
 
 #ifdef __cplusplus
 }

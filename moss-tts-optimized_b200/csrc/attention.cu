@@ -552,9 +552,12 @@ static cudaError_t launch_cluster_rep(cudaLaunchConfig_t& cfg, const AttnArgs& a
   return cudaLaunchKernelEx(&cfg, attention_cluster<REP, CH>, a);
 }
 
-// Chunk size of the cluster kernel: MT_ATTN_CHUNK (32, 64 or 128) overrides the default of
-// 128 tokens for one sequence and 32 for batches.
-static int attention_chunk(int batch) {
+// Chunk size of the cluster kernel: MT_ATTN_CHUNK (32, 64 or 128) overrides the default:
+// 128 tokens for one sequence (8 CTAs per KV head, one per SM), 64 while the batch's CTAs fit
+// three per SM in one wave, 32 (four and more per SM) beyond. Measured at contexts
+// U[256, 4096] (tokens/s, chunk 128 / 64 / 32): B = 2 886 / 938 / 815, B = 3 804 / 816 / 735,
+// B = 4 1013 / 993 / 885, B = 6 1217 / 1279 / 1190; B = 64: 32 is 1.5x faster than 128.
+static int attention_chunk(int batch, int nkv) {
   static int forced = -1;
   if (forced < 0) {
     const char* env = getenv("MT_ATTN_CHUNK");
@@ -562,7 +565,8 @@ static int attention_chunk(int batch) {
     forced = (v == 32 || v == 64 || v == 128) ? v : 0;
   }
   if (forced) return forced;
-  return batch > 1 ? 32 : 128;
+  if (batch == 1) return 128;
+  return (long long)batch * nkv * kClusterCtas <= 3LL * sm_count() ? 64 : 32;
 }
 
 static cudaError_t launch_cluster_attention(const AttnArgs& a, int batch, int rep, cudaStream_t s, int flags) {
@@ -579,7 +583,7 @@ static cudaError_t launch_cluster_attention(const AttnArgs& a, int batch, int re
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = (flags & kFlagPdl) ? 2 : 1;
-  const int ch = attention_chunk(batch);
+  const int ch = attention_chunk(batch, a.nkv);
   switch (rep) {
     case 4: return ch == 128 ? launch_cluster_rep<4, 128>(cfg, a) : ch == 64 ? launch_cluster_rep<4, 64>(cfg, a)
                                                                            : launch_cluster_rep<4, 32>(cfg, a);

@@ -27,7 +27,8 @@ struct PackGeom {
   }
   size_t packed_bytes() const { return (size_t)blocks * block_b; }
   static constexpr int kMaxCtas = 1024;  // workspace capacity: one slot per CTA boundary
-  static size_t workspace_bytes() { return (size_t)kMaxCtas * (2 * 16 * sizeof(float) + sizeof(int)); }
+  static constexpr int kSlotFloats = 32;  // per slot side: 16 tile rows x up to 2 activation rows
+  static size_t workspace_bytes() { return (size_t)kMaxCtas * (2 * kSlotFloats * sizeof(float) + sizeof(int)); }
 };
 
 // Weight row held at tile row tr (0..15) of tile t, or -1 for padding past the last row.
@@ -120,6 +121,46 @@ __device__ __forceinline__ void block_dot(const BlockRegs& bk, const uint32_t (&
   vb += __shfl_xor_sync(0xffffffffu, vb, 1);
   va += __shfl_xor_sync(0xffffffffu, va, 2);
   vb += __shfl_xor_sync(0xffffffffu, vb, 2);
+}
+
+// Two activation rows per mma: the one-row B operand uses only column 2c + h of k-slot c (group
+// 2c + h); with one accumulator per group instead (group 2c: mmas 0-7, group 2c + 1: mmas 8-15)
+// column 2c + b of k-slot c can carry activation row b. The zero-point mma runs once per
+// accumulator, its B holding -(c_b sum x_b) of that group only. Returns, summed over the lane
+// quad, rows r (va[b]) and r + 8 (vb[b]) of activation rows b = 0, 1.
+__device__ __forceinline__ void block_dot_rows2(const BlockRegs& bk, const uint32_t (&bl)[16], const uint32_t (&bh)[16],
+                                                uint32_t bzl0, uint32_t bzl1, uint32_t bzh0, uint32_t bzh1,
+                                                float (&va)[2], float (&vb)[2]) {
+  const uint32_t wa[8] = {bk.c0.x, bk.c0.y, bk.c0.z, bk.c0.w, bk.c1.x, bk.c1.y, bk.c1.z, bk.c1.w};
+  const uint32_t wb[8] = {bk.c2.x, bk.c2.y, bk.c2.z, bk.c2.w, bk.c3.x, bk.c3.y, bk.c3.z, bk.c3.w};
+  float dl[4] = {}, dh[4] = {};
+  const uint32_t za = __byte_perm(bk.zz, 0, 0x4040) & 0x00F0000Fu, zb = __byte_perm(bk.zz, 0, 0x4141) & 0x00F0000Fu;
+  mma_f16(dl, za, zb, za, zb, bzl0, bzl1);
+  mma_f16(dh, za, zb, za, zb, bzh0, bzh1);
+#pragma unroll
+  for (int u = 0; u < 8; ++u) {
+    float (&d)[4] = u < 4 ? dl : dh;
+    const uint32_t* bsel = u < 4 ? bl : bh;
+    const int bi = (u & 3) * 4;
+    const uint32_t sa = wa[u] >> 8, sb = wb[u] >> 8;
+    mma_f16(d, wa[u] & 0x000F000Fu, wb[u] & 0x000F000Fu, wa[u] & 0x00F000F0u, wb[u] & 0x00F000F0u, bsel[bi],
+            bsel[bi + 1]);
+    mma_f16(d, sa & 0x000F000Fu, sb & 0x000F000Fu, sa & 0x00F000F0u, sb & 0x00F000F0u, bsel[bi + 2], bsel[bi + 3]);
+  }
+  // element 0 / 1: row r, activation row 0 / 1; element 2 / 3: row r + 8
+  const float sl_a = __uint_as_float(bk.sw.x << 16), sh_a = __uint_as_float(bk.sw.x & 0xFFFF0000u);
+  const float sl_b = __uint_as_float(bk.sw.y << 16), sh_b = __uint_as_float(bk.sw.y & 0xFFFF0000u);
+  va[0] = fmaf(sh_a, dh[0], sl_a * dl[0]);
+  va[1] = fmaf(sh_a, dh[1], sl_a * dl[1]);
+  vb[0] = fmaf(sh_b, dh[2], sl_b * dl[2]);
+  vb[1] = fmaf(sh_b, dh[3], sl_b * dl[3]);
+#pragma unroll
+  for (int o = 1; o <= 2; o <<= 1) {
+    va[0] += __shfl_xor_sync(0xffffffffu, va[0], o);
+    va[1] += __shfl_xor_sync(0xffffffffu, va[1], o);
+    vb[0] += __shfl_xor_sync(0xffffffffu, vb[0], o);
+    vb[1] += __shfl_xor_sync(0xffffffffu, vb[1], o);
+  }
 }
 
 constexpr int kWarps = 16;  // consumer warps per CTA

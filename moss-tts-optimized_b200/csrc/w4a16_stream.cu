@@ -20,12 +20,19 @@
 //     a producer warp into an NS-stage ring; the first NS copies go out before
 //     griddepcontrol.wait, because weights never depend on the previous kernel;
 //   * consumer warp w takes block w of every stage. Lane (r, c) turns its 64 codes of rows
-//     r and r + 8 into bf16 pairs (128 + q_j, 128 + q_{j+4}) with one LOP3 each and feeds
-//     them as the A operand of 16 mma.sync.m16n8k16 (bf16 -> fp32). The B operand carries
-//     the activation only in column n = 2c + h for the codes of group 2c + h and zeros
-//     elsewhere, so accumulator column n holds every row's dot product with group n alone
-//     and the group's scale and zero point apply afterwards:
-//         y_r += s_rg * (D_rg - (128 + z_rg) * sum(x_g));
+//     r and r + 8 into fp16 subnormal pairs with one AND each ((q_j, q_{j+4}) 2^-24, or the
+//     same times 16 for the odd nibbles: exact operands) and feeds them as the A operand of
+//     16 mma.sync.m16n8k16 (fp16 -> fp32). The B operand is the activation times a power of
+//     two c (chosen from max |x| so that it is an exact fp16; c / 16 against the odd
+//     nibbles), present only in column n = 2c + h for the codes of group 2c + h and zero
+//     elsewhere, so accumulator column n holds every row's dot product with group n alone;
+//     a 17th mma with the zero points as A and -(c sum x_g) as B subtracts z sum(x_g), and
+//     the group's scale applies afterwards:
+//         y_r += s_rg * (sum_j q_rj x_j - z_rg * sum(x_g))   (all over c at the end);
+//   * the two-row variant (NBR = 2, a batch of two activation rows) uses the B columns
+//     the one-row kernel leaves zero: one accumulator per group of the k-slot, column
+//     2c + b for activation row b (block_dot_rows2): the same weight stream and 18 mma
+//     per block instead of 17;
 //   * row sums are kept per warp and tile in shared memory and reduced at the end; a tile
 //     split between two CTAs is finished by whichever arrives second, through a small
 //     workspace and a per-tile ticket (own + other: the same fp32 sum in either order),
@@ -117,13 +124,14 @@ __device__ __forceinline__ bool prefetch_act() { return MT_PREFETCH_ACT; }
 
 // TPM: tensor-parallel exchange compiled in (bit 0: input from peer cells, bit 1: output
 // pushed to peer cells); the single-GPU instantiations carry no exchange code.
-template <int NS, int BPW, bool NORM, bool ADD, bool PAIRED, int TPM>
+template <int NS, int BPW, bool NORM, bool ADD, bool PAIRED, int TPM, int NBR = 1>
 __global__ void __launch_bounds__(kWarps * 32 + 32, 1) w4a16_packed(StreamArgs a, int max_tiles) {
+  static_assert(NBR == 1 || (NBR == 2 && TPM == 0), "two activation rows only without the exchange");
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ __align__(8) uint64_t full[NS];
   __shared__ __align__(8) uint64_t empty[NS];
-  __shared__ float red[kWarps];
-  __shared__ float redmax[kWarps];
+  __shared__ float red[2 * kWarps];     // per activation row
+  __shared__ float redmax[2 * kWarps];
   __shared__ float redw[kWarps];
   __shared__ __align__(16) uint4 zero16[4];
   __shared__ int failed;
@@ -150,9 +158,9 @@ __global__ void __launch_bounds__(kWarps * 32 + 32, 1) w4a16_packed(StreamArgs a
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   uint8_t* ring = smem;
-  uint4* xp = reinterpret_cast<uint4*>(smem + (size_t)NS * stage_b);  // [K / 8] bf16 pairs
-  float* xsum = reinterpret_cast<float*>(xp + K / 8);                 // [K / 32]
-  float* partial = xsum + K / 32;                                     // [kWarps][max_tiles][16]
+  uint4* xp = reinterpret_cast<uint4*>(smem + (size_t)NS * stage_b);  // [NBR][K / 8] fp16 pairs
+  float* xsum = reinterpret_cast<float*>(xp + NBR * (K / 8));         // [NBR][K / 32]
+  float* partial = xsum + NBR * (K / 32);                             // [kWarps][max_tiles][NBR][16]
 
   auto issue = [&](int st) {  // one lane: stage st = blocks [b0 + SB st, ...)
     const int slot = st % NS;
@@ -175,7 +183,7 @@ __global__ void __launch_bounds__(kWarps * 32 + 32, 1) w4a16_packed(StreamArgs a
     for (int st = 0; st < a.pre_issue && st < NS && st < stages; ++st) issue(st);
   }
   if (tid < 4) zero16[tid] = make_uint4(0, 0, 0, 0);
-  for (int i = tid; i < kWarps * max_tiles * 16; i += blockDim.x) partial[i] = 0.f;
+  for (int i = tid; i < kWarps * max_tiles * 16 * NBR; i += blockDim.x) partial[i] = 0.f;
   __syncthreads();
 
   if (warp == kWarps) {  // producer warp
@@ -216,8 +224,12 @@ __global__ void __launch_bounds__(kWarps * 32 + 32, 1) w4a16_packed(StreamArgs a
     for (int j = 0; j < 4; ++j) {
       const int word = tid + j * consumers;
       if (j < wpt && word < K / 8) {
-        asm volatile("prefetch.global.L2 [%0];" ::"l"(reinterpret_cast<const uint4*>(a.x) + word));
-        if (ADD) asm volatile("prefetch.global.L2 [%0];" ::"l"(reinterpret_cast<const uint4*>(a.residual) + word));
+#pragma unroll
+        for (int br = 0; br < NBR; ++br) {
+          asm volatile("prefetch.global.L2 [%0];" ::"l"(reinterpret_cast<const uint4*>(a.x + (size_t)br * K) + word));
+          if (ADD)
+            asm volatile("prefetch.global.L2 [%0];" ::"l"(reinterpret_cast<const uint4*>(a.residual + (size_t)br * K) + word));
+        }
       }
     }
   }
@@ -225,8 +237,124 @@ __global__ void __launch_bounds__(kWarps * 32 + 32, 1) w4a16_packed(StreamArgs a
   pdl_trigger();
   const uint32_t tp_flag = TPM ? (uint32_t)*a.tp_epoch : 0u;
   const unsigned long long tp_t0 = (TPM & 1) ? globaltimer_ns() : 0ull;
-  const uint4* xsrc = reinterpret_cast<const uint4*>(a.x);
-  const uint4* rsrc = reinterpret_cast<const uint4*>(a.residual);
+  float inv_c0 = 0.f, inv_c1 = 0.f;  // 2^24 / c of activation rows 0 and 1
+  if constexpr (NBR == 2) {
+    // Two rows, two passes through shared memory: pass 1 loads both rows (the loads of
+    // both in flight together), adds the residual and keeps the bf16 words in the rows' xp
+    // slots; one block reduction gives both rows' statistics; pass 2 normalises from the
+    // slots and overwrites them with the fp16 operand pairs (same words, same thread).
+    float ss2[2] = {0.f, 0.f}, mv2[2] = {0.f, 0.f}, mw = 0.f;
+    if (NORM) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        if (j >= wpt || tid + j * consumers >= K / 8) continue;
+        const uint32_t na[4] = {nwv[j].x, nwv[j].y, nwv[j].z, nwv[j].w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) mw = fmaxf(mw, fmaxf(fabsf(bf16_lo(na[i])), fabsf(bf16_hi(na[i]))));
+      }
+    }
+#pragma unroll
+    for (int br = 0; br < 2; ++br) {
+      const uint4* xsrc = reinterpret_cast<const uint4*>(a.x + (size_t)br * K);
+      const uint4* rsrc = reinterpret_cast<const uint4*>(a.residual + (size_t)br * K);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int word = tid + j * consumers;
+        if (j >= wpt || word >= K / 8) continue;
+        const uint4 xw = xsrc[word];
+        uint32_t o[4] = {xw.x, xw.y, xw.z, xw.w};
+        if (ADD) {
+          const uint4 rw = rsrc[word];
+          const uint32_t ra[4] = {rw.x, rw.y, rw.z, rw.w};
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            __nv_bfloat162 pr = __floats2bfloat162_rn(round_bf16(bf16_lo(o[i]) + bf16_lo(ra[i])),
+                                                      round_bf16(bf16_hi(o[i]) + bf16_hi(ra[i])));
+            o[i] = *reinterpret_cast<uint32_t*>(&pr);
+          }
+          if (a.summed && blockIdx.x == 0)
+            reinterpret_cast<uint4*>(a.summed + (size_t)br * K)[word] = make_uint4(o[0], o[1], o[2], o[3]);
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const float lo = bf16_lo(o[i]), hi = bf16_hi(o[i]);
+          mv2[br] = fmaxf(mv2[br], fmaxf(fabsf(lo), fabsf(hi)));
+          if (NORM) {
+            ss2[br] += lo * lo;
+            ss2[br] += hi * hi;
+          }
+        }
+        xp[br * (K / 8) + word] = make_uint4(o[0], o[1], o[2], o[3]);
+      }
+    }
+    if (NORM) {
+      ss2[0] = warp_sum(ss2[0]);
+      ss2[1] = warp_sum(ss2[1]);
+      mw = warp_max(mw);
+    }
+    mv2[0] = warp_max(mv2[0]);
+    mv2[1] = warp_max(mv2[1]);
+    if (lane == 0) {
+      red[warp] = ss2[0];
+      red[kWarps + warp] = ss2[1];
+      redmax[warp] = mv2[0];
+      redmax[kWarps + warp] = mv2[1];
+      redw[warp] = mw;
+    }
+    named_sync(1, consumers);
+    float tot2[2] = {0.f, 0.f}, mx2[2] = {0.f, 0.f}, mxw = 0.f;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) {
+      tot2[0] += red[w];
+      tot2[1] += red[kWarps + w];
+      mx2[0] = fmaxf(mx2[0], redmax[w]);
+      mx2[1] = fmaxf(mx2[1], redmax[kWarps + w]);
+      mxw = fmaxf(mxw, redw[w]);
+    }
+#pragma unroll
+    for (int br = 0; br < 2; ++br) {
+      float inv = 1.f, mx = mx2[br];
+      if (NORM) {
+        inv = 1.0f / sqrtf(tot2[br] / (float)K + a.eps);
+        mx = mx * inv * mxw * 1.0079f;
+      }
+      const int ex = mx > 0.f ? min(max((int)((__float_as_uint(mx) >> 23) & 0xFF) - 127, -100), 100) : 0;
+      const float cs = __uint_as_float((uint32_t)(127 + 9 - ex) << 23);
+      const float ic = __uint_as_float((uint32_t)(127 + 24 - 9 + ex) << 23);
+      if (br == 0) inv_c0 = ic; else inv_c1 = ic;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int word = tid + j * consumers;
+        if (j >= wpt || word >= K / 8) continue;  // K / 8 is a multiple of 32: whole warps skip
+        const uint4 sw = xp[br * (K / 8) + word];
+        const uint32_t sa[4] = {sw.x, sw.y, sw.z, sw.w};
+        float v8[8];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) { v8[2 * i] = bf16_lo(sa[i]); v8[2 * i + 1] = bf16_hi(sa[i]); }
+        if (NORM) {
+          const uint32_t na[4] = {nwv[j].x, nwv[j].y, nwv[j].z, nwv[j].w};
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            v8[2 * i] = round_bf16(round_bf16(v8[2 * i] * inv) * bf16_lo(na[i]));
+            v8[2 * i + 1] = round_bf16(round_bf16(v8[2 * i + 1] * inv) * bf16_hi(na[i]));
+          }
+        }
+        float wsum = 0.f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) wsum += v8[i];
+        xp[br * (K / 8) + word] =
+            make_uint4(pack_half2(v8[0] * cs, v8[4] * cs), pack_half2(v8[1] * cs * 0.0625f, v8[5] * cs * 0.0625f),
+                       pack_half2(v8[2] * cs, v8[6] * cs), pack_half2(v8[3] * cs * 0.0625f, v8[7] * cs * 0.0625f));
+        wsum += __shfl_xor_sync(0xffffffffu, wsum, 1);
+        wsum += __shfl_xor_sync(0xffffffffu, wsum, 2);
+        if ((lane & 3) == 0) xsum[br * (K / 32) + (word >> 2)] = wsum * cs;
+      }
+    }
+    named_sync(1, consumers);
+  } else {
+  constexpr int br = 0;
+  const uint4* xsrc = reinterpret_cast<const uint4*>(a.x + (size_t)br * K);
+  const uint4* rsrc = reinterpret_cast<const uint4*>(a.residual + (size_t)br * K);
   float v[4][8];
   float ss = 0.f, mv = 0.f, mw = 0.f;
 #pragma unroll
@@ -288,7 +416,8 @@ __global__ void __launch_bounds__(kWarps * 32 + 32, 1) w4a16_packed(StreamArgs a
         __nv_bfloat162 pr = __floats2bfloat162_rn(v[j][2 * i], v[j][2 * i + 1]);
         o[i] = *reinterpret_cast<uint32_t*>(&pr);
       }
-      if (a.summed && blockIdx.x == 0) reinterpret_cast<uint4*>(a.summed)[word] = make_uint4(o[0], o[1], o[2], o[3]);
+      if (a.summed && blockIdx.x == 0)
+        reinterpret_cast<uint4*>(a.summed + (size_t)br * K)[word] = make_uint4(o[0], o[1], o[2], o[3]);
     }
 #pragma unroll
     for (int i = 0; i < 8; ++i) mv = fmaxf(mv, fabsf(v[j][i]));
@@ -333,8 +462,9 @@ __global__ void __launch_bounds__(kWarps * 32 + 32, 1) w4a16_packed(StreamArgs a
   // fp16 normal for every |x| >= 2^-23 max |x| (2^-19 max |x|); smaller values keep their
   // fp16 subnormal bits.
   const int ex = mx > 0.f ? min(max((int)((__float_as_uint(mx) >> 23) & 0xFF) - 127, -100), 100) : 0;
-  const float cs = __uint_as_float((uint32_t)(127 + 9 - ex) << 23);           // c
-  const float inv_c = __uint_as_float((uint32_t)(127 + 24 - 9 + ex) << 23);   // 2^24 / c
+  const float cs = __uint_as_float((uint32_t)(127 + 9 - ex) << 23);  // c
+  const float ic = __uint_as_float((uint32_t)(127 + 24 - 9 + ex) << 23);  // 2^24 / c
+  if (br == 0) inv_c0 = ic; else inv_c1 = ic;
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
     const int word = tid + j * consumers;
@@ -344,21 +474,44 @@ __global__ void __launch_bounds__(kWarps * 32 + 32, 1) w4a16_packed(StreamArgs a
     for (int i = 0; i < 8; ++i) wsum += v[j][i];
     // pairs (x0, x4) c, (x1, x5) c / 16, (x2, x6) c, (x3, x7) c / 16: the code slots'
     // (q_j, q_{j+4}) and 16 (q_{j+1}, q_{j+5}) factors
-    xp[word] = make_uint4(pack_half2(v[j][0] * cs, v[j][4] * cs), pack_half2(v[j][1] * cs * 0.0625f, v[j][5] * cs * 0.0625f),
-                          pack_half2(v[j][2] * cs, v[j][6] * cs), pack_half2(v[j][3] * cs * 0.0625f, v[j][7] * cs * 0.0625f));
+    xp[br * (K / 8) + word] =
+        make_uint4(pack_half2(v[j][0] * cs, v[j][4] * cs), pack_half2(v[j][1] * cs * 0.0625f, v[j][5] * cs * 0.0625f),
+                   pack_half2(v[j][2] * cs, v[j][6] * cs), pack_half2(v[j][3] * cs * 0.0625f, v[j][7] * cs * 0.0625f));
     wsum += __shfl_xor_sync(0xffffffffu, wsum, 1);
     wsum += __shfl_xor_sync(0xffffffffu, wsum, 2);
-    if ((lane & 3) == 0) xsum[word >> 2] = wsum * cs;
+    if ((lane & 3) == 0) xsum[br * (K / 32) + (word >> 2)] = wsum * cs;
   }
   named_sync(1, consumers);
+  }
 
   // ---- main loop ----
   const int r = lane >> 2, c = lane & 3;
   const int hsel = r - 2 * c;  // this lane's B column carries group 2c + hsel (if 0 or 1)
   uint32_t bl[16], bh[16];     // B operands of mmas 0-7 (group 2c) and 8-15 (group 2c + 1)
   uint32_t bz0 = 0, bz1 = 0;   // B operands of the zero-point mma (hi and lo fp16 parts)
+  uint32_t bz2 = 0, bz3 = 0;   // two rows: the zero-point mma of group 2c + 1
   int cur_j = -1;
   auto load_b = [&](int j) {   // B fragments of slice j: real data for the designated lanes only
+    if (NBR == 2) {            // column 2c + hsel carries activation row hsel, both groups
+      const bool live = hsel == 0 || hsel == 1;
+      const uint4* pl = live ? xp + hsel * (K / 8) + j * 32 + 8 * c : zero16;
+      const uint4* ph = live ? pl + 4 : zero16;
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const uint4 ql = pl[u], qh = ph[u];
+        bl[4 * u] = ql.x; bl[4 * u + 1] = ql.y; bl[4 * u + 2] = ql.z; bl[4 * u + 3] = ql.w;
+        bh[4 * u] = qh.x; bh[4 * u + 1] = qh.y; bh[4 * u + 2] = qh.z; bh[4 * u + 3] = qh.w;
+      }
+      const float* xs = xsum + (live ? hsel : 0) * (K / 32) + j * 8 + 2 * c;
+      const float z0 = live ? -xs[0] : 0.f, z1 = live ? -xs[1] * 0.0625f : 0.f;
+      const float h0 = __half2float(__float2half_rn(z0)), h1 = __half2float(__float2half_rn(z1));
+      bz0 = pack_half2(h0, 0.f);
+      bz1 = pack_half2(z0 - h0, 0.f);
+      bz2 = pack_half2(0.f, h1);
+      bz3 = pack_half2(0.f, z1 - h1);
+      cur_j = j;
+      return;
+    }
     const uint4* pl = hsel == 0 ? xp + j * 32 + 8 * c : zero16;
     const uint4* ph = hsel == 1 ? xp + j * 32 + 8 * c + 4 : zero16;
 #pragma unroll
@@ -414,12 +567,23 @@ __global__ void __launch_bounds__(kWarps * 32 + 32, 1) w4a16_packed(StreamArgs a
       }
       if (live) {
         if (jj[m] != cur_j) load_b(jj[m]);
-        float va, vb;
-        block_dot<MT_NACC>(bk, bl, bh, bz0, bz1, va, vb);
-        if (c == 0) {
-          float* pp = partial + ((size_t)warp * max_tiles + (tt[m] - t_first)) * 16;
-          pp[r] += va;
-          pp[r + 8] += vb;
+        float* pp = partial + ((size_t)warp * max_tiles + (tt[m] - t_first)) * 16 * NBR;
+        if (NBR == 2) {
+          float va2[2], vb2[2];
+          block_dot_rows2(bk, bl, bh, bz0, bz1, bz2, bz3, va2, vb2);
+          if (c == 0) {
+            pp[r] += va2[0];
+            pp[r + 8] += vb2[0];
+            pp[16 + r] += va2[1];
+            pp[16 + r + 8] += vb2[1];
+          }
+        } else {
+          float va, vb;
+          block_dot<MT_NACC>(bk, bl, bh, bz0, bz1, va, vb);
+          if (c == 0) {
+            pp[r] += va;
+            pp[r + 8] += vb;
+          }
         }
       }
     }
@@ -432,23 +596,25 @@ __global__ void __launch_bounds__(kWarps * 32 + 32, 1) w4a16_packed(StreamArgs a
     return;
   }
   // sum the warps' rows of every local tile into partial[0][lt][*]
-  for (int i = tid; i < ntiles * 16; i += consumers) {
-    const int lt = i >> 4, tr = i & 15;
+  for (int i = tid; i < ntiles * 16 * NBR; i += consumers) {
+    const int lt = i / (16 * NBR), tr = i - lt * 16 * NBR;
     float sum = 0.f;
 #pragma unroll 4
-    for (int w = 0; w < kWarps; ++w) sum += partial[((size_t)w * max_tiles + lt) * 16 + tr];
-    partial[(size_t)lt * 16 + tr] = sum * inv_c;
+    for (int w = 0; w < kWarps; ++w) sum += partial[((size_t)w * max_tiles + lt) * 16 * NBR + tr];
+    partial[(size_t)lt * 16 * NBR + tr] = sum * ((NBR == 2 && tr >= 16) ? inv_c1 : inv_c0);
   }
   named_sync(1, consumers);
   // tiles wholly inside this CTA's range
   __nv_bfloat16* ystage = reinterpret_cast<__nv_bfloat16*>(partial + (size_t)kWarps * max_tiles * 16);
-  for (int i = tid; i < ntiles * RT; i += consumers) {
-    const int lt = i / RT, tr = i - lt * RT, tq = t_first + lt;
+  for (int i = tid; i < ntiles * RT * NBR; i += consumers) {
+    const int br = NBR == 2 ? i / (ntiles * RT) : 0, ii = i - br * ntiles * RT;
+    const int lt = ii / RT, tr = ii - lt * RT, tq = t_first + lt;
     if (tq * S < b0 || (tq + 1) * S > b1) continue;
     const int o = tq * RT + tr;
     if (o < n_out) {
-      const __nv_bfloat16 yv = to_bf16(finish_row<PAIRED>(partial[lt * 16 + tr], partial[lt * 16 + 8 + tr]));
-      a.y[o] = yv;
+      const float* pt = partial + (size_t)lt * 16 * NBR + br * 16;
+      const __nv_bfloat16 yv = to_bf16(finish_row<PAIRED>(pt[tr], pt[8 + tr]));
+      a.y[(size_t)br * n_out + o] = yv;
       if (TPM & 2) ystage[i] = yv;
     }
   }
@@ -477,19 +643,21 @@ __global__ void __launch_bounds__(kWarps * 32 + 32, 1) w4a16_packed(StreamArgs a
       const int lt = ts - t_first;
       const int side = warp == 0 ? 1 : 0;  // 1: this CTA holds the tile's tail
       const int slot = warp == 0 ? blockIdx.x - 1 : blockIdx.x;
-      float own[16];
+      constexpr int F = 16 * NBR;
+      float own[F];
 #pragma unroll
-      for (int i = 0; i < 16; ++i) own[i] = partial[lt * 16 + i];
-      float4* mine = reinterpret_cast<float4*>(a.ws + ((size_t)slot * 2 + side) * 16);
+      for (int i = 0; i < F; ++i) own[i] = partial[lt * F + i];
+      float4* mine = reinterpret_cast<float4*>(a.ws + ((size_t)slot * 2 + side) * PackGeom::kSlotFloats);
 #pragma unroll
-      for (int i = 0; i < 4; ++i) mine[i] = make_float4(own[4 * i], own[4 * i + 1], own[4 * i + 2], own[4 * i + 3]);
+      for (int i = 0; i < F / 4; ++i) mine[i] = make_float4(own[4 * i], own[4 * i + 1], own[4 * i + 2], own[4 * i + 3]);
       int prev;
       asm volatile("atom.add.acq_rel.gpu.s32 %0, [%1], 1;" : "=r"(prev) : "l"(a.tickets + slot) : "memory");
       if (prev == 1) {  // second to arrive: finish the tile
-        const float4* other = reinterpret_cast<const float4*>(a.ws + ((size_t)slot * 2 + (1 - side)) * 16);
-        float tot[16];
+        const float4* other =
+            reinterpret_cast<const float4*>(a.ws + ((size_t)slot * 2 + (1 - side)) * PackGeom::kSlotFloats);
+        float tot[F];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
+        for (int i = 0; i < F / 4; ++i) {
           const float4 o = __ldcg(other + i);
           tot[4 * i] = own[4 * i] + o.x;
           tot[4 * i + 1] = own[4 * i + 1] + o.y;
@@ -497,20 +665,22 @@ __global__ void __launch_bounds__(kWarps * 32 + 32, 1) w4a16_packed(StreamArgs a
           tot[4 * i + 3] = own[4 * i + 3] + o.w;
         }
 #pragma unroll
-        for (int tr = 0; tr < RT; ++tr) {
-          const int o = ts * RT + tr;
-          if (o < n_out) a.y[o] = to_bf16(finish_row<PAIRED>(tot[tr], tot[(tr + 8) & 15]));
-        }
+        for (int br = 0; br < NBR; ++br)
+#pragma unroll
+          for (int tr = 0; tr < RT; ++tr) {
+            const int o = ts * RT + tr;
+            if (o < n_out) a.y[(size_t)br * n_out + o] = to_bf16(finish_row<PAIRED>(tot[br * 16 + tr], tot[br * 16 + ((tr + 8) & 15)]));
+          }
         a.tickets[slot] = 0;
       }
     }
   }
 }
 
-static size_t packed_smem(int ns, int bpw, int k, bool zeros, int max_tiles) {
+static size_t packed_smem(int ns, int bpw, int k, bool zeros, int max_tiles, int nbr) {
   const int block_b = kCodeBytes + kScaleBytes + (zeros ? kZeroBytes : 0);
-  return (size_t)ns * kWarps * bpw * block_b + (size_t)k / 8 * 16 + (size_t)k / 32 * 4 +
-         (size_t)kWarps * max_tiles * 16 * 4 + (size_t)max_tiles * 16 * 2;  // + staged output rows
+  return (size_t)ns * kWarps * bpw * block_b + (size_t)nbr * ((size_t)k / 8 * 16 + (size_t)k / 32 * 4) +
+         (size_t)kWarps * max_tiles * 16 * nbr * 4 + (size_t)max_tiles * 16 * 2;  // + staged output rows
 }
 
 // MT_W4_SPLIT = 1 forces split-K ranges, 2 whole-tile ranges (default: whole tiles when
@@ -535,7 +705,7 @@ static int pre_issue_stages() {
   return m;
 }
 
-template <int NS, int BPW, bool NORM, bool ADD, bool PAIRED, int TPM>
+template <int NS, int BPW, bool NORM, bool ADD, bool PAIRED, int TPM, int NBR = 1>
 static cudaError_t go(StreamArgs a, cudaStream_t s, int flags) {
   const PackGeom pg(a.n, a.k, a.zeros != 0, PAIRED);
   int grid = sm_count();
@@ -546,10 +716,10 @@ static cudaError_t go(StreamArgs a, cudaStream_t s, int flags) {
                                               : (pg.blocks + grid - 1) / grid;
   const int max_tiles = (int)((max_blocks + pg.slices - 1) / pg.slices) + 1;
   a.pre_issue = pre_issue_stages();
-  const size_t smem = packed_smem(NS, BPW, a.k, a.zeros != 0, max_tiles);
+  const size_t smem = packed_smem(NS, BPW, a.k, a.zeros != 0, max_tiles, NBR);
   if (smem > 227 * 1024) return cudaErrorInvalidValue;
-  return launch(w4a16_packed<NS, BPW, NORM, ADD, PAIRED, TPM>, dim3(grid), dim3(kWarps * 32 + 32), smem, s, flags, a,
-                max_tiles);
+  return launch(w4a16_packed<NS, BPW, NORM, ADD, PAIRED, TPM, NBR>, dim3(grid), dim3(kWarps * 32 + 32), smem, s, flags,
+                a, max_tiles);
 }
 
 // Pipeline shape: MT_W4_PIPE = "<stages><blocks per warp>": 21 (default: two stages of 16
@@ -586,6 +756,12 @@ static cudaError_t go_ns(const StreamArgs& a, cudaStream_t s, int flags) {
   }
 }
 
+// Two activation rows per launch (the default pipeline shape).
+template <bool NORM, bool ADD, bool PAIRED>
+static cudaError_t go_rows2(const StreamArgs& a, cudaStream_t s, int flags) {
+  return go<2, 1, NORM, ADD, PAIRED, 0, 2>(a, s, flags);
+}
+
 static bool packed_shape_ok(int n, int k, int mode) {
   if (k < kSliceCols || k % kSliceCols || k > 16384 || (mode & ~7)) return false;
   const int n_out = (mode & 4) ? n / 2 : n;
@@ -620,7 +796,7 @@ MT_API int mt_w4a16_pack(const void* qweight, const void* scales, const void* qz
 
 static int linear_packed(const void* x, const void* residual, const void* norm_w, float eps, void* summed,
                          const void* packed, int has_zeros, void* y, int n, int k, int mode, void* workspace,
-                         const mt_tp_exchange* tp, int flags, void* stream) {
+                         const mt_tp_exchange* tp, int flags, void* stream, int nbr = 1) {
   if (!packed || !y || !workspace || !packed_shape_ok(n, k, mode)) return kBadArgument;
   if ((mode & 2) && (!(mode & 1) || !residual)) return kBadArgument;
   if ((mode & 1) && !norm_w) return kBadArgument;
@@ -637,7 +813,7 @@ static int linear_packed(const void* x, const void* residual, const void* norm_w
   a.packed = (const uint8_t*)packed;
   a.y = (__nv_bfloat16*)y;
   a.ws = (float*)workspace;
-  a.tickets = (int*)((uint8_t*)workspace + (size_t)PackGeom::kMaxCtas * 2 * 16 * sizeof(float));
+  a.tickets = (int*)((uint8_t*)workspace + (size_t)PackGeom::kMaxCtas * 2 * PackGeom::kSlotFloats * sizeof(float));
   a.n = n;
   a.k = k;
   a.zeros = has_zeros ? 1 : 0;
@@ -664,6 +840,12 @@ static int linear_packed(const void* x, const void* residual, const void* norm_w
   cudaStream_t s = (cudaStream_t)stream;
   flags &= kFlagPdl;
   const bool paired = mode & 4;
+  if (nbr == 2) {
+    if (tp) return kBadArgument;
+    if (mode & 2) return (int)(paired ? go_rows2<true, true, true>(a, s, flags) : go_rows2<true, true, false>(a, s, flags));
+    if (mode & 1) return (int)(paired ? go_rows2<true, false, true>(a, s, flags) : go_rows2<true, false, false>(a, s, flags));
+    return (int)(paired ? go_rows2<false, false, true>(a, s, flags) : go_rows2<false, false, false>(a, s, flags));
+  }
   // The exchange variants the tensor-parallel decode step uses: input into the add + norm
   // projections (q|k|v, gate/up; RMSNorm-only for a first layer), output from plain ones.
   if (tp_in && tp_out) return kBadArgument;
@@ -685,6 +867,28 @@ MT_API int mt_w4a16_linear_packed(const void* x, const void* residual, const voi
   if (!x) return kBadArgument;
   return linear_packed(x, residual, norm_w, eps, summed, packed, has_zeros, y, n, k, mode, workspace, nullptr,
                        flags, stream);
+}
+
+// rows activation rows (x, residual, summed [rows, k], y [rows, n_out], row-major) through the
+// packed layout: pairs of rows share one weight stream (the two-row kernel), an odd last row
+// runs the one-row kernel.
+MT_API int mt_w4a16_linear_packed_rows(const void* x, const void* residual, const void* norm_w, float eps,
+                                       void* summed, const void* packed, int has_zeros, void* y, int rows, int n,
+                                       int k, int mode, void* workspace, int flags, void* stream) {
+  if (!x || rows < 1 || rows > 64 || !packed_shape_ok(n, k, mode)) return kBadArgument;
+  const size_t n_out = (mode & 4) ? n / 2 : n;
+  const __nv_bfloat16* xb = (const __nv_bfloat16*)x;
+  const __nv_bfloat16* rb = (const __nv_bfloat16*)residual;
+  __nv_bfloat16* sb = (__nv_bfloat16*)summed;
+  __nv_bfloat16* yb = (__nv_bfloat16*)y;
+  for (int r0 = 0; r0 < rows; r0 += 2) {
+    const size_t xo = (size_t)r0 * k, yo = (size_t)r0 * n_out;
+    const int rc = linear_packed(xb + xo, rb ? rb + xo : nullptr, norm_w, eps, sb ? sb + xo : nullptr, packed,
+                                 has_zeros, yb ? yb + yo : nullptr, n, k, mode, workspace, nullptr, flags, stream,
+                                 rows - r0 >= 2 ? 2 : 1);
+    if (rc) return rc;
+  }
+  return 0;
 }
 
 MT_API int mt_w4a16_linear_packed_tp(const void* x, const void* residual, const void* norm_w, float eps,

@@ -13,12 +13,15 @@ length and delay length (ragged static KV caches). Per step, all PDL-chained and
     heads: add + final RMSNorm, text/audio logits (plain bf16 GEMMs, as the reference's
            F.linear heads), greedy ids + delay masks per sequence  -> next_ids [B, 33]
 
-Projections: up to 8 sequences run the GPTQ-layout GEMV with its fused norm prologue
-(``mt_w4a16_linear``, which reads each weight once for all rows); from ``gemm_min_batch``
-(default 9) rows the W4A16 projections run on the tcgen05 GEMM over its load-time packed
-layout (``mt_w4a16_gemm_pack`` / ``mt_w4a16_gemm_packed``) after a separate RMSNorm, whose
-per-chunk pipeline costs more than it saves below that. Inputs live in one int64 control block ``[ids B*33 | positions B | audio_length B |
-delay_length B]`` (one host-to-device copy per step); the result is ``next_ids``.
+Projections: below ``gemm_min_batch`` (default 5) sequences run the packed tensor-core GEMV
+with its fused norm prologue (``mt_w4a16_linear_packed_rows``: two activation rows share one
+pass over the weights, so B = 2 costs about one batch-1 step); from ``gemm_min_batch`` rows
+the W4A16 projections run on the tcgen05 GEMM over its load-time packed layout
+(``mt_w4a16_gemm_pack`` / ``mt_w4a16_gemm_packed``) after a separate RMSNorm. Shapes the
+packed layout does not take (K not a multiple of 256), or ``packed_gemv=False``, use the
+GPTQ-layout GEMV (``mt_w4a16_linear``, up to 8 rows). Inputs live in one int64 control block ``[ids B*33 |
+positions B | audio_length B | delay_length B]`` (one host-to-device copy per step); the
+result is ``next_ids``.
 """
 import torch
 
@@ -31,7 +34,7 @@ class BatchDecodeEngine:
     """Static-buffer decode step for ``batch`` sequences over (a shard of) W4A16 ``DecoderWeights``."""
 
     def __init__(self, weights: DecoderWeights, batch: int, max_length: int = 4096, *, pdl: bool = True,
-                 tp: TensorParallel | None = None, gemm_min_batch: int = 9):
+                 tp: TensorParallel | None = None, gemm_min_batch: int = 5, packed_gemv: bool = True):
         cfg = weights.cfg
         cfg.validate()
         if batch < 1 or batch > 128:
@@ -46,6 +49,10 @@ class BatchDecodeEngine:
         self.gemm = batch >= gemm_min_batch
         if not self.gemm and batch > 8:
             raise ValueError("more than 8 rows need the tcgen05 GEMM (gemm_min_batch <= batch)")
+        layers = weights.layers
+        self.rows_packed = packed_gemv and not self.gemm and all(
+            p.k % 256 == 0 and 256 <= p.k <= 16384 and (not paired or p.n % 2 == 0)
+            for lw in layers for p, paired in ((lw.qkv, False), (lw.out, False), (lw.gate_up, True), (lw.down, False)))
         h, d, B = cfg.hidden_size, cfg.head_dim, batch
         self.nq, self.nkv = cfg.num_heads // world, cfg.num_kv_heads // world
         self.n_cb = cfg.n_vq // world
@@ -91,6 +98,12 @@ class BatchDecodeEngine:
                     native.call("mt_w4a16_gemm_pack", p.qweight.data_ptr(), p.scales.data_ptr(), native.ptr(p.qzeros),
                                 p.n, p.k, mode, t.data_ptr(), s)
                     self.packed[id(p)] = t
+        if self.rows_packed:  # the packed GEMV's tiles (shared with a batch-1 engine on the same weights)
+            for lw in layers:
+                for p, paired in ((lw.qkv, False), (lw.out, False), (lw.gate_up, True), (lw.down, False)):
+                    p.packed_tiles(paired)
+                    ws = max(ws, native.w4a16_packed_size(p.n, p.k, p.qzeros is not None,
+                                                          native.LINEAR_PAIRED if paired else 0)[1])
         self.gemm_workspace = torch.zeros(ws, device=dev, dtype=torch.uint8)
         self.graph = None
         self.graph_advance = None
@@ -113,6 +126,11 @@ class BatchDecodeEngine:
             return
         mode = (native.LINEAR_NORM if norm is not None else 0) | (native.LINEAR_ADD if residual is not None else 0)
         mode |= native.LINEAR_PAIRED if paired else 0
+        if self.rows_packed:
+            native.call("mt_w4a16_linear_packed_rows", x.data_ptr(), native.ptr(residual), native.ptr(norm), eps,
+                        native.ptr(summed), p.packed_tiles(paired).data_ptr(), 1 if p.qzeros is not None else 0,
+                        y.data_ptr(), B, p.n, p.k, mode, self.gemm_workspace.data_ptr(), self.flags, s)
+            return
         native.call("mt_w4a16_linear", x.data_ptr(), native.ptr(residual), native.ptr(norm), eps, native.ptr(summed),
                     p.qweight.data_ptr(), p.scales.data_ptr(), native.ptr(p.qzeros), y.data_ptr(), B, p.n, p.k, 32,
                     mode, self.flags, s)

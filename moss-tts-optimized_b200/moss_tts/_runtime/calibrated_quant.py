@@ -10,8 +10,13 @@ Same names and signatures as ``src/moss_tts/_runtime/calibrated_quant.py``:
   + 8`` and zero point 8 on the way; the product is exact in fp32, so one rounding defines
   every output bit).
 
-The GPTQ solver of the same reference module (``gptq``, ``calibrated_quant.py:45-85``) is
-offline calibration and lives in ``gptq_solver``.
+* ``gptq(weight, inputs, group=32, damping=.01, actorder=True, block=128, backend='triton',
+  scales_override=None)`` (``calibrated_quant.py:45-85``): the Hessian set-up and the trailing
+  block updates are the reference's torch calls (Cholesky, matmul) on the device; the column
+  loop of each 128-column block is one launch of ``mt_gptq_block`` instead of one Triton
+  ``_column`` launch per column. ``backend`` accepts the reference's ``'triton'`` (the fused
+  column kernel) and ``'cuda'``; the codes are bit-identical to the reference's column loop on
+  the same block inputs.
 """
 import torch
 
@@ -55,3 +60,47 @@ def dequantize(signed, scales, group):
     native.call("mt_dequant_w4", qweight.data_ptr(), scales.contiguous().data_ptr(), None, out.data_ptr(), n, k,
                 group, native.stream_of(signed))
     return out
+
+
+@torch.inference_mode()
+def gptq(weight, inputs, group=32, damping=.01, actorder=True, block=128, backend="triton", scales_override=None):
+    """Signed G32 codes ``int8 [N, K]`` in [-7, 7] and their static bf16 scales, by GPTQ error
+    feedback over calibration inputs ``[m, K]`` (``calibrated_quant.py:45-85``)."""
+    n, k = weight.shape
+    if k % block or k % group:
+        raise ValueError("Dimensions must be divisible by group/block sizes")
+    if inputs.ndim != 2 or inputs.shape[1] != k:
+        raise ValueError("Calibration input shape mismatch")
+    if backend not in ("triton", "cuda"):
+        raise ValueError("Unknown GPTQ backend")
+    if block > 128:
+        raise ValueError("GPTQ blocks of at most 128 columns are supported")
+    _cuda(weight, inputs)
+    scales = static_scales(weight, group) if scales_override is None else scales_override
+    if (scales.shape != (n, k // group) or scales.dtype != torch.bfloat16 or scales.device != weight.device
+            or not scales.is_contiguous() or not torch.isfinite(scales).all() or not (scales > 0).all()):
+        raise ValueError("Invalid static group scales")
+    x = inputs.float()
+    h = (x.T @ x) * (2 / x.shape[0])
+    dead = h.diagonal() == 0
+    h[dead, dead] = 1
+    w = weight.float().clone()
+    w[:, dead] = 0
+    perm = torch.argsort(h.diagonal(), descending=True) if actorder else torch.arange(k, device=w.device)
+    w = w[:, perm].contiguous()
+    h = h[perm][:, perm].contiguous()
+    h.diagonal().add_(damping * h.diagonal().mean())
+    hinv = torch.linalg.cholesky(torch.cholesky_inverse(torch.linalg.cholesky(h)), upper=True).contiguous()
+    del h, x
+    perm = perm.to(torch.int64).contiguous()
+    signed = torch.empty((n, k), device=w.device, dtype=torch.int8)
+    s = native.stream_of(w)
+    for start in range(0, k, block):
+        end = start + block
+        chunk = w[:, start:end].contiguous()
+        errors = torch.empty_like(chunk)
+        native.call("mt_gptq_block", chunk.data_ptr(), errors.data_ptr(), signed.data_ptr(), scales.data_ptr(),
+                    hinv.data_ptr(), perm.data_ptr(), start, block, n, k, group, s)
+        if end < k:
+            w[:, end:] -= errors @ hinv[start:end, end:]
+    return signed, scales

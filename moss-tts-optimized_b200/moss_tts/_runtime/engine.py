@@ -171,6 +171,12 @@ class DecodeEngine:
         self.audio_logits = torch.zeros(self.n_cb * cfg.audio_vocab_size, **bf)
         self.next_ids = torch.zeros(CONTROL_IDS, device=dev, dtype=torch.long)
         self.status = torch.zeros(1, device=dev, dtype=torch.int32)
+        # Non-greedy decoding: (text T, top-k, top-p, audio T, top-k, top-p) of the device sampler
+        # (mt_heads_sample) run after the heads, or None for the heads kernel's greedy ids. The
+        # seed (drawn from torch's default generator, so torch.manual_seed fixes it) keys the
+        # sampler's counter-based generator together with the position.
+        self.sampling = None
+        self.seed = torch.randint(0, 2 ** 62, (1,), dtype=torch.int64).to(dev)
         self.graph = None
         self.graph_advance = None
         self._host_control = torch.zeros(CONTROL_IDS + 3, dtype=torch.long, pin_memory=True)
@@ -318,6 +324,19 @@ class DecodeEngine:
                     self.best.data_ptr(), self.tickets[self.nkv:].data_ptr(), cfg.hidden_size, 2, self.n_cb,
                     cfg.audio_vocab_size, self.cb_offset, cfg.n_vq, cfg.audio_assistant_delay_slot_token_id,
                     cfg.audio_end_token_id, cfg.audio_pad_code, 1 if self.tp.rank == 0 else 0, self.flags, s)
+        if self.sampling is not None:
+            tt, tk, tp_, at, ak, ap = self.sampling
+            native.call("mt_heads_sample", self.text_logits.data_ptr(), self.audio_logits.data_ptr(),
+                        self.text_ids.data_ptr(), self.position.data_ptr(), self.audio_length.data_ptr(),
+                        self.delay_length.data_ptr(), self.seed.data_ptr(), self.next_ids.data_ptr(), 1, 2,
+                        self.n_cb, cfg.audio_vocab_size, self.cb_offset, cfg.n_vq,
+                        cfg.audio_assistant_delay_slot_token_id, cfg.audio_end_token_id, cfg.audio_pad_code,
+                        1 if self.tp.rank == 0 else 0, float(tt), int(tk), float(tp_), float(at), int(ak), float(ap),
+                        self.flags, s)
+
+    def set_seed(self, seed: int) -> None:
+        """Seed of the device sampler (any integer; reduced to 64 bits)."""
+        self.seed.fill_(int(seed) & (2 ** 63 - 1))
 
     def launch_advance(self) -> None:
         """Device-side state advance after a step (feed next_ids back, position += 1, delay

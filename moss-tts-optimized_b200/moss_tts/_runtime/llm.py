@@ -9,8 +9,12 @@ are validated as the reference validates them and otherwise ignored.
 
 ``model`` is a ``DecoderWeights`` (device-resident, optionally a tensor-parallel
 shard). Sampling: ``greedy=True`` selects argmax on the device inside the heads
-kernel; otherwise the reference's top-k / top-p sampler (``llm.py:10-19``) runs on
-the device after it, with the delay masks re-applied (``llm.py:280-286``).
+kernel; otherwise the reference's top-k / top-p sampler (``llm.py:10-19``: text T 1.5,
+top-k 2; audio T 1.7, top-k 25, top-p 0.8) runs as one kernel after it
+(``mt_heads_sample``), delay masks included (``llm.py:280-286``), so a sampled step is a
+graph of this library's kernels with no host round trip. Its draws come from a
+counter-based generator keyed by ``engine.seed`` and the position, not torch's generator:
+the distribution is the reference's, the individual draws are not.
 """
 import torch
 import torch.nn.functional as F
@@ -61,27 +65,14 @@ class FastLLM:
         self.channels = torch.arange(self.cfg.n_vq, device=e.device)
         self.graph = None
         self.prefill_graphs = {}
+        self.prefill_mode = "auto"  # prefill.Prefill modes: "bf16", "dequant", "w4"
 
-    # The heads kernel already wrote greedy ids; sampling overwrites them in place.
-    def _sample(self):
-        e, cfg = self.engine, self.cfg
-        text = e.text_logits.view(1, 2)
-        audio = e.audio_logits.view(-1, cfg.audio_vocab_size)
-        text_index = sample_topk(text, 1.5, 2, 1.0)
-        text_token = e.text_ids[text_index]
-        text_token = torch.where(self.delay_length >= 0, cfg.audio_assistant_delay_slot_token_id, text_token)
-        text_token = torch.where(self.delay_length == 32, cfg.audio_end_token_id, text_token)
-        audio_tokens = sample_topk(audio, 1.7)
-        valid = (self.channels < self.audio_length) & ((self.delay_length < 0) | (self.channels >= self.delay_length))
-        audio_tokens = torch.where(valid, audio_tokens, cfg.audio_pad_code)
-        e.next_ids.copy_(torch.cat([text_token.reshape(1), audio_tokens]))
+    # The sampler settings of FastLLM._decode (llm.py:280, 284): text (T, top-k, top-p), audio.
+    SAMPLING = (1.5, 2, 1.0, 1.7, 25, 0.8)
 
     def _decode(self):
+        self.engine.sampling = None if self.greedy else self.SAMPLING
         self.engine.launch_step()
-        if not self.greedy:
-            if self.engine.tp.world > 1:
-                raise ValueError("Sampling with tensor parallelism is not supported; use greedy=True")
-            self._sample()
         return (self.engine.next_ids.view(1, 1, CONTROL_IDS), self.engine.text_logits.view(1, 2),
                 self.engine.audio_logits.view(-1, self.cfg.audio_vocab_size))
 
@@ -158,8 +149,8 @@ class FastLLM:
             from .prefill import Prefill
             n = ids.shape[1]
             runner = self.prefill_graphs.get("runner")
-            if runner is None or runner.max_tokens < n:
-                runner = self.prefill_graphs["runner"] = Prefill(e, max_tokens=max(512, n))
+            if runner is None or runner.max_tokens < n or runner.mode != self.prefill_mode:
+                runner = self.prefill_graphs["runner"] = Prefill(e, max_tokens=max(512, n), mode=self.prefill_mode)
             return runner.run(ids.to(e.device))
         for t in range(ids.shape[1]):
             e.set_inputs(ids[0, t], t, 1, -1)

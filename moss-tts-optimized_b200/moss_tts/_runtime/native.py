@@ -25,14 +25,17 @@ SIGNATURES = {
     "mt_read_error_word": ([ctypes.POINTER(ctypes.c_int), _I], _I),
     "mt_dequant_w4": ([_P, _P, _P, _P, _I, _I, _I, _P], _I),
     "mt_static_scales": ([_P, _I, _P, _I, _I, _P], _I),
+    "mt_gptq_block": ([_P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _P], _I),
     "mt_w4a16_linear": ([_P, _P, _P, _F, _P, _P, _P, _P, _P, _I, _I, _I, _I, _I, _I, _P], _I),
     "mt_w4a16_packed_size": ([_I, _I, _I, _I, _LLP, _LLP], _I),
     "mt_w4a16_pack": ([_P, _P, _P, _I, _I, _I, _P, _P], _I),
     "mt_w4a16_linear_packed": ([_P, _P, _P, _F, _P, _P, _I, _P, _I, _I, _I, _P, _I, _P], _I),
+    "mt_w4a16_linear_packed_rows": ([_P, _P, _P, _F, _P, _P, _I, _P, _I, _I, _I, _I, _P, _I, _P], _I),
     "mt_w4a16_linear_packed_tp": ([_P, _P, _P, _F, _P, _P, _I, _P, _I, _I, _I, _P, _P, _I, _P], _I),
     "mt_w4a16_gemm_workspace": ([_I, _I, _I, _I, _LLP], _I),
     "mt_w4a16_gemm": ([_P, _P, _P, _P, _P, _I, _I, _I, _I, _P, _I, _P], _I),
     "mt_heads_select": ([_P, _P, _P, _P, _P, _P] + [_I] * 11 + [_P], _I),
+    "mt_heads_sample": ([_P] * 8 + [_I] * 10 + [_F, _I, _F, _F, _I, _F, _I, _P], _I),
     "mt_w4a16_gemm_pack_size": ([_I, _I, _I, _LLP], _I),
     "mt_w4a16_gemm_pack": ([_P, _P, _P, _I, _I, _I, _P, _P], _I),
     "mt_w4a16_gemm_packed": ([_P, _P, _P, _I, _I, _I, _I, _P, _I, _P], _I),

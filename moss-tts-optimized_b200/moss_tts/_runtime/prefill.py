@@ -14,8 +14,21 @@ library's CUDA:
                -> gate/up GEMM with SiLU*up -> down GEMM
     last row: add + final RMSNorm (mt_rmsnorm) -> full text head and audio heads (bf16 GEMVs)
 
-The projections use the tcgen05 GEMM on the GPTQ layout (``mt_w4a16_gemm``: no second copy of
-the weights), one call per 128-row tile of the prompt.
+Projections, three modes:
+
+* ``"bf16"``: bf16 copies of the projection weights, made once by the bit-exact
+  ``mt_dequant_w4`` on first use and kept resident, multiplied with a plain bf16 GEMM (cuBLAS
+  through ``torch.matmul``, fp32 accumulation); the gate/up product goes through
+  ``mt_silu_mul``. This is the reference's own arrangement: its G32 preset keeps BF16 weights
+  for the prompt pass (``calibrated_quant.py`` header, ``llm.py:204-226``). 2 bytes per weight
+  (13.9 GB for the 8B backbone).
+* ``"dequant"``: the same GEMMs, each projection dequantized into one reused bf16 scratch
+  matrix (201 MB) right before its GEMM.
+* ``"w4"``: the W4A16 tcgen05 GEMM on the GPTQ layout (``mt_w4a16_gemm``), one call per
+  128-row tile of the prompt, with the paired SiLU epilogue (no extra memory).
+
+``"auto"`` picks ``"bf16"`` when the device has room for the copies (with 8 GB to spare),
+else ``"dequant"``.
 """
 import torch
 
@@ -27,8 +40,16 @@ GEMM_ROWS = 128
 class Prefill:
     """Prompt buffers for up to ``max_tokens`` rows over a (single-GPU, W4A16) ``DecodeEngine``."""
 
-    def __init__(self, engine, max_tokens: int = 512):
+    def __init__(self, engine, max_tokens: int = 512, mode: str = "auto"):
+        if mode not in ("auto", "bf16", "dequant", "w4"):
+            raise ValueError("mode must be 'auto', 'bf16', 'dequant' or 'w4'")
         eng = engine
+        if mode == "auto":
+            need = 2 * sum(p.n * p.k for lw in eng.w.layers for p in (lw.qkv, lw.out, lw.gate_up, lw.down))
+            free, _ = torch.cuda.mem_get_info(eng.device)
+            mode = "bf16" if free > need + (8 << 30) else "dequant"
+        self.mode = mode
+        self.resident = {}  # id(projection) -> bf16 weights ("bf16" mode)
         if eng.tp.world != 1:
             raise ValueError("prefill runs on one GPU")
         w, cfg = eng.w, eng.cfg
@@ -50,6 +71,11 @@ class Prefill:
         self.hidden = torch.zeros(h, **bf)
         self.text_logits = torch.zeros(1, w.head_text.shape[0], **bf)
         self.audio_logits = torch.zeros(cfg.n_vq, cfg.audio_vocab_size, **bf)
+        if mode in ("bf16", "dequant"):
+            if mode == "dequant":
+                largest = max(p.n * p.k for lw in w.layers for p in (lw.qkv, lw.out, lw.gate_up, lw.down))
+                self.wscratch = torch.empty(largest, **bf)
+            self.gu = torch.zeros(T, w.layers[0].gate_up.n, **bf)
         ws = 256
         for lw in w.layers:
             for p, paired in ((lw.qkv, False), (lw.out, False), (lw.gate_up, True), (lw.down, False)):
@@ -58,6 +84,21 @@ class Prefill:
 
     def _gemm(self, p, x, y, n, paired=False):
         s = torch.cuda.current_stream(self.eng.device).cuda_stream
+        if self.mode in ("bf16", "dequant"):
+            w = self.resident.get(id(p)) if self.mode == "bf16" else None
+            if w is None:
+                w = (torch.empty((p.n, p.k), device=y.device, dtype=torch.bfloat16) if self.mode == "bf16"
+                     else self.wscratch[: p.n * p.k].view(p.n, p.k))
+                native.call("mt_dequant_w4", p.qweight.data_ptr(), p.scales.data_ptr(), native.ptr(p.qzeros),
+                            w.data_ptr(), p.n, p.k, 32, s)
+                if self.mode == "bf16":
+                    self.resident[id(p)] = w
+            if paired:
+                torch.matmul(x[:n], w.t(), out=self.gu[:n])
+                native.call("mt_silu_mul", self.gu.data_ptr(), y.data_ptr(), n, p.n // 2, 0, s)
+            else:
+                torch.matmul(x[:n], w.t(), out=y[:n])
+            return
         mode = native.LINEAR_PAIRED if paired else 0
         for r0 in range(0, n, GEMM_ROWS):
             rows = min(GEMM_ROWS, n - r0)

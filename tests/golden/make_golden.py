@@ -10,7 +10,7 @@ name is ``moss_tts``); this repository's seeded synthetic-weight generator is
 loaded by file path under a private package name, so both can coexist. Every
 fixture is produced by calling reference functions -- ``calibrated_backend.
 unpack_signed``, ``calibrated_quant.static_scales`` / ``dequantize``,
-``dp4a_packing.pack_interleaved``, ``llm.sample_topk``, the bundled
+``dp4a_packing.pack_interleaved``, ``calibrated_quant.gptq`` (torch backend), ``llm.sample_topk``, the bundled
 ``MossTTSDelayModel`` and transformers' ``Qwen3`` modules -- on seeded inputs,
 or (for the zero-point format, which the reference does not implement) by the
 one-line restatement of ``calibrated_quant.dequantize`` with the zero point
@@ -368,9 +368,50 @@ def decode_fixture(steps=64):
     return out
 
 
+def sampling_fixture(draws=20000):
+    """``llm.sample_topk`` with the decode step's settings (audio: T 1.7, top-k 25, top-p 0.8;
+    text: T 1.5, top-k 2, top-p 1.0) drawn ``draws`` times per row on seeded bf16 logits: the
+    reference's empirical counts per token."""
+    g = torch.Generator().manual_seed(51)
+    audio = (torch.randn(6, 1024, generator=g) * torch.tensor([1.0, 2.0, 3.0, 4.0, 6.0, 0.5])[:, None]).bfloat16()
+    text = (torch.randn(4, 2, generator=g) * 2.0).bfloat16()
+    torch.manual_seed(52)
+    out = {"audio_logits": bits(audio), "text_logits": bits(text), "draws": np.array([draws])}
+    picks = sample_topk(audio.repeat(draws, 1), 1.7).view(draws, 6)
+    out["audio_counts"] = np.stack([np.bincount(picks[:, r].numpy(), minlength=1024) for r in range(6)]).astype(np.int32)
+    picks = sample_topk(text.repeat(draws, 1), 1.5, 2, 1.0).view(draws, 4)
+    out["text_counts"] = np.stack([np.bincount(picks[:, r].numpy(), minlength=2) for r in range(4)]).astype(np.int32)
+    return out
+
+
+def gptq_fixture():
+    """``calibrated_quant.gptq`` (torch backend, the reference's own column loop) on seeded
+    weights and calibration inputs: two 128-column blocks with act-order and one dead input
+    column, and one block without act-order."""
+    out = {}
+    for name, (n, k, actorder, seed) in {"act": (48, 256, True, 41), "plain": (32, 128, False, 42)}.items():
+        g = torch.Generator().manual_seed(seed)
+        w = (torch.randn(n, k, generator=g) * 0.02).bfloat16()
+        x = torch.randn(192, k, generator=g) * torch.linspace(0.2, 2.0, k)
+        if actorder:
+            x[:, 5] = 0  # a dead input column: zero Hessian diagonal
+        signed, scales = calibrated_quant.gptq(w, x, group=32, actorder=actorder, backend="torch")
+        out[f"{name}_weight"] = bits(w)
+        out[f"{name}_inputs"] = x.numpy()
+        out[f"{name}_signed"] = signed.numpy()
+        out[f"{name}_scales"] = bits(scales)
+    return out
+
+
 def main():
     if sys.argv[1:] == ["prefill"]:  # only the prefill fixture
         np.savez_compressed(HERE / "prefill.npz", **prefill_fixture())
+        return
+    if sys.argv[1:] == ["gptq"]:  # only the GPTQ fixture
+        np.savez_compressed(HERE / "gptq.npz", **gptq_fixture())
+        return
+    if sys.argv[1:] == ["sampling"]:  # only the sampler fixture
+        np.savez_compressed(HERE / "sampling.npz", **sampling_fixture())
         return
     q, big, wbig = quant_fixture()
     np.savez_compressed(HERE / "quant.npz", **q)
@@ -381,6 +422,8 @@ def main():
     np.savez_compressed(HERE / "mlp.npz", **mlp_fixture())
     np.savez_compressed(HERE / "decode.npz", **decode_fixture())
     np.savez_compressed(HERE / "prefill.npz", **prefill_fixture())
+    np.savez_compressed(HERE / "gptq.npz", **gptq_fixture())
+    np.savez_compressed(HERE / "sampling.npz", **sampling_fixture())
     for f in sorted(HERE.glob("*.npz")):
         print(f.name, f.stat().st_size)
 

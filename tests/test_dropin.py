@@ -83,3 +83,12 @@ def test_int4_dp4a_and_calibrated_quant_checks():
         calibrated_quant.dequantize(torch.zeros(4, 64, dtype=torch.int8), torch.ones(4, 2), 32)
     with pytest.raises(ValueError, match="CUDA"):
         calibrated_quant.static_scales(torch.zeros(4, 64), 32)
+    w = torch.zeros(4, 256)
+    with pytest.raises(ValueError, match="Dimensions must be divisible"):
+        calibrated_quant.gptq(w[:, :200], torch.zeros(8, 200))
+    with pytest.raises(ValueError, match="Calibration input shape mismatch"):
+        calibrated_quant.gptq(w, torch.zeros(8, 128))
+    with pytest.raises(ValueError, match="Unknown GPTQ backend"):
+        calibrated_quant.gptq(w, torch.zeros(8, 256), backend="torch")
+    with pytest.raises(ValueError, match="CUDA"):
+        calibrated_quant.gptq(w, torch.zeros(8, 256))

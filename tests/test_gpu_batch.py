@@ -3,8 +3,8 @@ engine run sequence by sequence on the same weights and caches.
 
 Hidden states within max-abs 5e-2 / rel 2e-2; greedy ids identical except where the batch-1
 engine's own top-two audio logits are a near-tie (a few bf16 ulps: the two paths sum in a
-different order). Covers the tcgen05 GEMM path (B >= 2), the GPTQ-layout GEMV path (B <= 8
-with the GEMM disabled), ragged positions, per-sequence delay masks, graph capture with the
+different order). Covers the tcgen05 GEMM path, the packed two-row GEMV (B = 2, and B = 3:
+a pair plus one row), the GPTQ-layout GEMV (B <= 8 with both disabled), ragged positions, per-sequence delay masks, graph capture with the
 device-side advance, and the batched greedy selection kernel against a host argmax.
 """
 import numpy as np
@@ -48,12 +48,14 @@ def near_tie_only(got, want, audio_logits, text_logits):
     return int(bad.sum())
 
 
-@pytest.mark.parametrize("batch,gemm_min", [(12, 2), (3, 2), (3, 9)])
-def test_batched_step_matches_batch1_engine(model, cuda_device, batch, gemm_min):
+@pytest.mark.parametrize("batch,gemm_min,packed", [(12, 2, True), (3, 2, True), (2, 5, True), (3, 5, True),
+                                                   (3, 9, False)])
+def test_batched_step_matches_batch1_engine(model, cuda_device, batch, gemm_min, packed):
     dc, w = model
     rng = np.random.Generator(np.random.PCG64(batch * 10 + gemm_min))
     pos = rng.integers(5, MAXLEN - 8, size=batch)
-    eng = BatchDecodeEngine(w, batch, max_length=MAXLEN, gemm_min_batch=gemm_min)
+    eng = BatchDecodeEngine(w, batch, max_length=MAXLEN, gemm_min_batch=gemm_min, packed_gemv=packed)
+    assert eng.rows_packed == (packed and batch < gemm_min)
     g = torch.Generator(device=cuda_device).manual_seed(batch)
     eng.kv.normal_(generator=g)
     singles = []

@@ -109,3 +109,86 @@ def test_norm_projection_against_oracle(cuda_device, fused):
         assert len(out) == 3 and out[2] is None
     assert np.array_equal(out[0].float().cpu().numpy(), summed)
     _check(out[1], ref, f"dp4a_norm_projection.linear fused={fused}")
+
+
+def _gptq_blocks_on_device(dev, weight, inputs, scales, actorder):
+    """Drive ``mt_gptq_block`` and the oracle's column loop from the same block inputs (the
+    oracle's Hessian set-up; the trailing update by the oracle's torch CPU matmul for both), and
+    require identical codes, errors and updated blocks."""
+    from moss_tts._runtime import native
+
+    w, hinv, perm = quant.gptq_prepare(weight, inputs, 0.01, actorder)
+    n, k = w.shape
+    hinv_d = torch.from_numpy(hinv).to(dev)
+    perm_d = torch.from_numpy(perm.astype(np.int64)).to(dev)
+    scales_d = _bf16(scales, dev)
+    codes_d = torch.zeros((n, k), dtype=torch.int8, device=dev)
+    ref_codes = np.zeros((n, k), dtype=np.int8)
+    for start in range(0, k, 128):
+        chunk = np.ascontiguousarray(w[:, start:start + 128])
+        chunk_d = torch.from_numpy(chunk).to(dev)
+        err_d = torch.empty_like(chunk_d)
+        native.call("mt_gptq_block", chunk_d.data_ptr(), err_d.data_ptr(), codes_d.data_ptr(), scales_d.data_ptr(),
+                    hinv_d.data_ptr(), perm_d.data_ptr(), start, 128, n, k, 32, native.stream_of(chunk_d))
+        codes, errors = quant.gptq_block(chunk, hinv, perm, scales, start, 32)
+        ref_codes[:, perm[start:start + 128]] = codes
+        assert np.array_equal(err_d.cpu().numpy().view(np.uint32), errors.view(np.uint32)), start
+        assert np.array_equal(chunk_d.cpu().numpy().view(np.uint32), chunk.view(np.uint32)), start
+        if start + 128 < k:
+            w[:, start + 128:] -= (torch.from_numpy(errors) @ torch.from_numpy(
+                np.ascontiguousarray(hinv[start:start + 128, start + 128:]))).numpy()
+    assert np.array_equal(codes_d.cpu().numpy(), ref_codes)
+    return ref_codes
+
+
+def test_gptq_block_kernel_is_bit_exact(cuda_device):
+    """The column-loop kernel against the oracle's (itself pinned to the reference's gptq): the
+    reference fixture's two cases, then 300 rows (a ragged last 16-row CTA) x 512 columns."""
+    g = golden("gptq")
+    for name, actorder in (("act", True), ("plain", False)):
+        codes = _gptq_blocks_on_device(cuda_device, g[f"{name}_weight"], g[f"{name}_inputs"],
+                                       g[f"{name}_scales"], actorder)
+        assert np.array_equal(codes, g[f"{name}_signed"]), name
+    gen = torch.Generator().manual_seed(77)
+    w = (torch.randn(300, 512, generator=gen) * 0.03).bfloat16()
+    x = (torch.randn(256, 512, generator=gen) * torch.linspace(0.1, 3.0, 512)).numpy()
+    wb = w.view(torch.int16).numpy().view(np.uint16)
+    _gptq_blocks_on_device(cuda_device, wb, x, quant.static_scales(wb), True)
+
+
+def test_gptq_on_device_against_reference(cuda_device):
+    """Whole ``calibrated_quant.gptq`` on the device against the reference's codes. The Hessian
+    factors and trailing updates come from device linear algebra, whose summation order differs
+    from the CPU's, so a code can differ at a rounding near-tie: at most 1% of the codes, by
+    one step, and the layer's calibration loss ``||(W - Q) X^T||`` within 1% of the reference's."""
+    g = golden("gptq")
+    for name, actorder in (("act", True), ("plain", False)):
+        w = _bf16(g[f"{name}_weight"], cuda_device)
+        x = torch.from_numpy(g[f"{name}_inputs"]).to(cuda_device)
+        signed, scales = calibrated_quant.gptq(w, x, actorder=actorder)
+        torch.cuda.synchronize()
+        assert np.array_equal(scales.cpu().view(torch.int16).numpy().view(np.uint16), g[f"{name}_scales"])
+        got, want = signed.cpu().numpy().astype(np.int32), g[f"{name}_signed"].astype(np.int32)
+        differ = int((got != want).sum())
+        wf, xf = from_bf16_bits(g[f"{name}_weight"]).astype(np.float64), g[f"{name}_inputs"].astype(np.float64)
+        loss = [np.linalg.norm((wf - quant.dequantize_signed(c, g[f"{name}_scales"])) @ xf.T)
+                for c in (got, want)]
+        print(f"gptq {name}: {differ} of {got.size} codes differ, loss {loss[0]:.5g} vs reference {loss[1]:.5g}")
+        assert differ <= got.size // 100 and np.abs(got - want).max() <= 1
+        assert loss[0] <= loss[1] * 1.01
+
+
+def test_gptq_layer_timing(cuda_device):
+    """One 4096 x 4096 projection with 512 calibration rows: the 32 block launches and trailing
+    updates, timed (the reference launches its column kernel 4096 times for this layer)."""
+    gen = torch.Generator().manual_seed(3)
+    w = (torch.randn(4096, 4096, generator=gen) * 0.02).bfloat16().to(cuda_device)
+    x = torch.randn(512, 4096, generator=gen).to(cuda_device)
+    calibrated_quant.gptq(w, x)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    signed, _ = calibrated_quant.gptq(w, x)
+    t1.record()
+    torch.cuda.synchronize()
+    print(f"gptq 4096 x 4096, 512 calibration rows: {t0.elapsed_time(t1):.2f} ms")
+    assert int(signed.abs().max()) <= 7

@@ -525,7 +525,7 @@ def test_packed_kernel_matches_oracle_and_register_kernel(cuda_device, n, k, mod
     x, r, w = dev_bf16(xb, cuda_device), dev_bf16(rb, cuda_device), dev_bf16(nw, cuda_device)
     ws = torch.zeros(native.w4a16_packed_size(n, k, qz is not None, mode & 4)[1], dtype=torch.uint8,
                      device=cuda_device)
-    ws[:1024 * 128].fill_(0x7F)  # partial-row slots hold stale data between calls; only tickets must be zero
+    ws[:1024 * 256].fill_(0x7F)  # partial-row slots hold stale data between calls; only tickets must be zero
     outs, ws = packed_linear(native, qw, sc, qz, n, k, mode, x, r, w, 0, cuda_device, ws=ws, calls=2)
     pdl, _ = packed_linear(native, qw, sc, qz, n, k, mode, x, r, w, 1, cuda_device, ws=ws)
     n_out = n // 2 if mode & 4 else n
@@ -555,15 +555,15 @@ def test_packed_kernel_matches_oracle_and_register_kernel(cuda_device, n, k, mod
         a, b = from_bf16_bits(outs[0][0]), from_bf16_bits(host_bits(yreg))
         assert np.all(np.abs(a - b) <= 2.0 ** -6 * np.maximum(np.abs(a), np.abs(b)) + 2.0 ** -14)
     assert np.array_equal(outs[0][0], outs[1][0]) and np.array_equal(outs[0][0], pdl[0][0])
-    # workspace: [1024 CTA boundaries][2][16] f32 partial rows, then [1024] i32 tickets
-    assert int(ws[1024 * 128:].view(torch.int32).abs().sum()) == 0
+    # workspace: [1024 CTA boundaries][2][32] f32 partial rows, then [1024] i32 tickets
+    assert int(ws[1024 * 256:].view(torch.int32).abs().sum()) == 0
     assert native.error_word() == 0
 
 
 def test_packed_size_and_bad_arguments(cuda_device):
     from moss_tts._runtime import native
-    assert native.w4a16_packed_size(4096, 4096, True, 0) == (256 * 16 * 2368, 1024 * (128 + 4))
-    assert native.w4a16_packed_size(24576, 4096, False, 4) == (1536 * 16 * 2304, 1024 * (128 + 4))
+    assert native.w4a16_packed_size(4096, 4096, True, 0) == (256 * 16 * 2368, 1024 * (256 + 4))
+    assert native.w4a16_packed_size(24576, 4096, False, 4) == (1536 * 16 * 2304, 1024 * (256 + 4))
     with pytest.raises(RuntimeError):
         native.w4a16_packed_size(64, 1000, True, 0)  # K not a multiple of 256
     with pytest.raises(RuntimeError):  # null workspace
@@ -598,3 +598,87 @@ def test_heads_tensor_parallel_shard_writes_only_its_codebooks(cuda_device):
     for c in range(8):
         assert got[9 + c] == want[c] or top2[c, 1] - top2[c, 0] <= 0.0625
     assert int(best.abs().sum()) == 0 and int(ticket.item()) == 0
+
+
+@pytest.mark.parametrize("n,k,mode,rows", [(6144, 4096, 1, 2), (24576, 4096, 7, 2), (4096, 12288, 0, 3),
+                                           (4096, 4096, 3, 4), (300, 1024, 4, 2), (1000, 2048, 0, 5),
+                                           (26, 256, 6 | 1, 2)])
+def test_packed_rows_match_oracle_and_batch1(cuda_device, n, k, mode, rows):
+    """mt_w4a16_linear_packed_rows: pairs of activation rows through the two-row kernel (one
+    weight stream), an odd last row through the one-row kernel. Every row against the oracle
+    (the fixed bar), against the batch-1 call on that row alone (same products, the per-group
+    partial sums added in another order: two bf16 ulps), residual sums bit-exact; the PDL
+    launch and a repeat call bitwise equal; the workspace tickets back to zero."""
+    from moss_tts._runtime import native
+    rng = np.random.Generator(np.random.PCG64(n + 5 * k + mode + rows))
+    p = synthetic.quantized(rng, n, k, 32, mode != 0)
+    qw, sc, qz = upload_w4(p, cuda_device)
+    xb = synthetic.activation(21 + n, (rows, k))
+    rb = synthetic.activation(22 + n, (rows, k))
+    xb[rows - 1] = bf16_bits(from_bf16_bits(xb[rows - 1]) * 300.0)  # rows of very different scale
+    nw = bf16_bits(from_bf16_bits(synthetic.activation(23, (k,), 0.02)) + 1.0)
+    x, r, w = dev_bf16(xb, cuda_device), dev_bf16(rb, cuda_device), dev_bf16(nw, cuda_device)
+    nbytes, wbytes = native.w4a16_packed_size(n, k, qz is not None, mode & 4)
+    packed = torch.empty(nbytes, dtype=torch.uint8, device=cuda_device)
+    s = torch.cuda.current_stream().cuda_stream
+    native.call("mt_w4a16_pack", qw.data_ptr(), sc.data_ptr(), native.ptr(qz), n, k, mode & 4, packed.data_ptr(), s)
+    ws = torch.zeros(wbytes, dtype=torch.uint8, device=cuda_device)
+    n_out = n // 2 if mode & 4 else n
+    zeros = 1 if qz is not None else 0
+
+    def run(flags):
+        y = torch.empty((rows, n_out), device=cuda_device, dtype=torch.bfloat16)
+        summed = torch.empty_like(x)
+        native.call("mt_w4a16_linear_packed_rows", x.data_ptr(), r.data_ptr() if mode & 2 else None,
+                    w.data_ptr() if mode & 1 else None, 1e-6, summed.data_ptr() if mode & 2 else None,
+                    packed.data_ptr(), zeros, y.data_ptr(), rows, n, k, mode, ws.data_ptr(), flags, s)
+        return host_bits(y), host_bits(summed)
+
+    y, summed = run(0)
+    y2, _ = run(0)
+    y3, _ = run(1)
+    assert np.array_equal(y, y2) and np.array_equal(y, y3)
+    wd = quant.dequantize_w4(p["qweight"], p["scales"], p["qzeros"])
+    for i in range(rows):
+        xin = from_bf16_bits(xb[i])
+        if mode & 2:
+            s_ref, h = ops.add_rmsnorm(xin, from_bf16_bits(rb[i]), from_bf16_bits(nw), 1e-6)
+            assert np.array_equal(summed[i], bf16_bits(s_ref)), i
+        elif mode & 1:
+            h = ops.rmsnorm(xin, from_bf16_bits(nw), 1e-6)
+        else:
+            h = xin
+        ref = ops.linear(h, wd)
+        gu = None
+        if mode & 4:
+            gu = np.asarray(ref, np.float64)
+            ref = ops.silu_mul(ref)
+        scale = max(1.0, float(np.abs(ref).max()) / 8)  # the scaled row: the bar relative to its size
+        if mode & 4:
+            # y = bf16(bf16(silu(bf16 g)) * bf16 u): fp32 sums in another order can flip the bf16
+            # g or u by one ulp, which moves y by |silu'(g) u| ulp(g) + |silu(g)| ulp(u) (plus
+            # one ulp of y); with a large |u| that exceeds the fixed bar, so the bar adds it
+            def ulp(v):
+                return 2.0 ** (np.floor(np.log2(np.maximum(np.abs(v), 2.0 ** -100))) - 7)
+            g, u = gu[: n_out], gu[n_out:]
+            sg = 1.0 / (1.0 + np.exp(-g))
+            flip = np.abs(sg * (1 + g * (1 - sg)) * u) * ulp(g) + np.abs(g * sg) * ulp(u) + ulp(ref)
+            ref = np.asarray(ref, np.float64)
+            err = np.abs(from_bf16_bits(y[i]).astype(np.float64) - ref)
+            bar = ATOL * scale + RTOL * np.abs(ref) + flip
+            print(f"row {i}: max abs err {err.max():.4g}, max err / bar {np.max(err / bar):.3g}")
+            assert np.all(err <= bar), (i, err.max())
+        else:
+            close(y[i], ref, ATOL * scale)
+        y1 = torch.empty((1, n_out), device=cuda_device, dtype=torch.bfloat16)
+        native.call("mt_w4a16_linear_packed", x[i].data_ptr(), r[i].data_ptr() if mode & 2 else None,
+                    w.data_ptr() if mode & 1 else None, 1e-6, None, packed.data_ptr(), zeros, y1.data_ptr(), n, k,
+                    mode, ws.data_ptr(), 0, s)
+        a, b = from_bf16_bits(y[i]), from_bf16_bits(host_bits(y1)[0])
+        diff = np.abs(a.astype(np.float64) - b)
+        if mode & 4:
+            assert np.all(diff <= 2 * flip), i
+        else:
+            assert np.all(diff <= 2.0 ** -6 * np.maximum(np.abs(a), np.abs(b)) + 2.0 ** -14 * scale), i
+    assert int(ws[1024 * 256:].view(torch.int32).abs().sum()) == 0
+    assert native.error_word() == 0

@@ -8,6 +8,9 @@
 * decode continues from the prefilled cache: the next decode step equals the one after the
   prompt was fed row by row through the decode step (ids except near-ties, hidden within bar).
 
+All three projection modes run: resident bf16 copies from the bit-exact dequantization, the
+same dequantized per call into a scratch, and the W4A16 tcgen05 GEMM.
+
 Bars: the reference runs its prompt pass with bf16 matmul/attention outputs on the CPU, so the
 logits are compared at 0.1 + 2e-2 |ref| with relative RMS <= 2% (the same bar pins the oracle
 to that fixture); against the oracle, whose arithmetic this is up to fp32 summation order,
@@ -49,10 +52,12 @@ def two_layer(cuda_device):
     return dc, host, DecoderWeights.from_host(dc, host, cuda_device)
 
 
-def test_prefill_matches_reference_model(two_layer):
+@pytest.mark.parametrize("mode", ["bf16", "dequant", "w4"])
+def test_prefill_matches_reference_model(two_layer, mode):
     dc, _, w = two_layer
     g = golden("prefill")
     llm = FastLLM(w, max_length=128, greedy=True)
+    llm.prefill_mode = mode
     text, audio = llm.prefill(torch.from_numpy(g["ids"]))
     torch.cuda.synchronize()
     for label, got, want in (("prefill text logits", text, g["text"]), ("prefill audio logits", audio, g["audio"])):
@@ -61,7 +66,8 @@ def test_prefill_matches_reference_model(two_layer):
     assert int(llm.engine.status.item()) == 0
 
 
-def test_prefill_long_prompt_matches_oracle_and_decode_continues(two_layer, cuda_device):
+@pytest.mark.parametrize("mode", ["bf16", "dequant", "w4"])
+def test_prefill_long_prompt_matches_oracle_and_decode_continues(two_layer, cuda_device, mode):
     dc, host, w = two_layer
     n = 300
     rng = np.random.Generator(np.random.PCG64(5))
@@ -69,6 +75,7 @@ def test_prefill_long_prompt_matches_oracle_and_decode_continues(two_layer, cuda
     ids[0, :, 0] = rng.integers(0, dc.vocab_size - 16, size=n)
     ids[0, :, 1:] = rng.integers(0, 1025, size=(n, 32))
     llm = FastLLM(w, max_length=384, greedy=True)
+    llm.prefill_mode = mode
     text, audio = llm.prefill(torch.from_numpy(ids))
     ref = omodel.Decoder(host, dc.as_dict(), max_length=384)
     rtext, raudio, _ = ref.prefill(ids[0])

@@ -12,7 +12,7 @@ import pytest
 
 from conftest import golden
 from oracle import model as omodel
-from oracle import ops, quant
+from oracle import ops, quant, sampling
 from oracle.numerics import bf16_bits, from_bf16_bits, round_bf16
 
 from moss_tts._runtime import synthetic
@@ -52,6 +52,45 @@ def test_zero_point_dequant_bit_exact():
     g = golden("quant")
     w = quant.dequantize_w4(g["zp_qweight"], g["zp_scales"], g["zp_qzeros"], 32)
     assert np.array_equal(bf16_bits(w), g["zp_dequant"])
+
+
+def test_gptq_matches_reference():
+    """The oracle's GPTQ (static scales, Hessian set-up, column loop, trailing updates) gives the
+    reference's torch-backend codes and scales bit for bit: two blocks with act-order and a dead
+    input column, and one block in natural order."""
+    g = golden("gptq")
+    for name, actorder in (("act", True), ("plain", False)):
+        signed, scales = quant.gptq(g[f"{name}_weight"], g[f"{name}_inputs"], actorder=actorder)
+        assert np.array_equal(scales, g[f"{name}_scales"]), name
+        assert np.array_equal(signed, g[f"{name}_signed"]), name
+
+
+def test_philox_known_answers():
+    """Philox4x32-10 against the known-answer vectors published with the generator (Random123)."""
+    assert sampling.philox4x32_10((0, 0, 0, 0), (0, 0)) == (0x6627E8D5, 0xE169C58D, 0xBC57AC4C, 0x9B00DBD8)
+    assert sampling.philox4x32_10((0xFFFFFFFF,) * 4, (0xFFFFFFFF,) * 2) == (0x408F276D, 0x41C83B0E, 0xA20BC7C6,
+                                                                          0x6D5451FD)
+    assert sampling.philox4x32_10((0x243F6A88, 0x85A308D3, 0x13198A2E, 0x03707344), (0xA4093822, 0x299F31D0)) == (
+        0xD16CFE09, 0x94FDCCEB, 0x5001E420, 0x24126EA1)
+
+
+def test_sampling_distribution_matches_reference_draws():
+    """The oracle's sample_topk distribution against 20,000 draws per row of the reference's own
+    sampler (audio: T 1.7, top-k 25, top-p 0.8; text: T 1.5, top-k 2): every drawn token is in
+    the oracle's support and every frequency is within 4.5 standard errors."""
+    g = golden("sampling")
+    n = int(g["draws"][0])
+    for logits, counts, args in ((g["audio_logits"], g["audio_counts"], (1.7, 25, 0.8)),
+                                 (g["text_logits"], g["text_counts"], (1.5, 2, 1.0))):
+        for row in range(logits.shape[0]):
+            idx, q = sampling.sample_distribution(f(logits[row]), *args)
+            c = counts[row]
+            assert c.sum() == n and c[idx].sum() == n, row
+            z = np.abs(c[idx] / n - q) / np.sqrt(q * (1 - q) / n + 1e-12)
+            assert z.max() <= 4.5, (row, z.max())
+    # temperature 0 is the argmax (first index on ties)
+    x = np.array([1.0, 3.0, 3.0, -2.0], np.float32)
+    assert sampling.sample_distribution(x, 0, 25, 0.8)[0].tolist() == [1]
 
 
 def test_config0_dequant_checksum():
