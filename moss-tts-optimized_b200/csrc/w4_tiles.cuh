@@ -10,6 +10,7 @@
 namespace mt {
 
 constexpr int kSliceCols = 256;   // input columns per slice block
+constexpr int kSliceMax = 64;     // slices of the largest K (16384)
 constexpr int kCodeBytes = 2048;  // 16 rows x 128 bytes
 constexpr int kScaleBytes = 256;  // 16 rows x 8 groups x bf16
 constexpr int kZeroBytes = 64;    // 16 rows x 8 groups x 4 bits

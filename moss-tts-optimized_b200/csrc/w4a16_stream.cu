@@ -114,6 +114,11 @@ struct StreamArgs {
 // error word 2 and computes with what it has (a dead or late peer; far above the microseconds
 // a healthy exchange takes).
 constexpr unsigned long long kExchangeDeadlineNs = 100ull * 1000 * 1000;
+// Ranks whose exchange cells one thread polls at once (loads in flight together).
+#ifndef MT_POLL_RANKS
+#define MT_POLL_RANKS 2
+#endif
+constexpr int kPollRanks = MT_POLL_RANKS;
 
 // NS ring stages of kWarps * BPW slice blocks; consumer warp w takes blocks w + 16 m
 // (m < BPW) of every stage, which share one slice when S divides 16.
@@ -135,6 +140,7 @@ __global__ void __launch_bounds__(kWarps * 32 + 32, 1) w4a16_packed(StreamArgs a
   __shared__ float redw[kWarps];
   __shared__ __align__(16) uint4 zero16[4];
   __shared__ int failed;
+  __shared__ float slice_scale[kSliceMax];  // one row: 2^24 / c of each slice's activation scale
   __shared__ volatile int tp_failed;
   constexpr int RT = PAIRED ? 8 : 16;  // output rows per tile
   constexpr int consumers = kWarps * 32;
@@ -211,11 +217,22 @@ __global__ void __launch_bounds__(kWarps * 32 + 32, 1) w4a16_packed(StreamArgs a
   // ---- activation prologue: x (+ residual, RMSNorm) -> bf16 pairs and group sums in smem ----
   // Thread t owns the 8-value words t, t + 512, ... (kernels.py:57-59, 76-82).
   const int wpt = (K / 8 + consumers - 1) / consumers;  // words per thread, at most 4
+  // Slice-owned activation (one row, no exchange, S a multiple of the warp count): warp w only
+  // ever multiplies slices (b0 + w) mod 16 + 16 i, so it prepares exactly those slices itself --
+  // each with its own power-of-two scale -- and needs no block barrier for them (the RMSNorm
+  // statistic, when there is one, is the only block-wide step).
+  const bool owned = NBR == 1 && TPM == 0 && S % kWarps == 0;
+  const int cls = (b0 + warp) % kWarps, nsl = S / kWarps;  // owned slices cls + 16 i, i < nsl (<= 4)
   uint4 nwv[4];
   if (NORM) {
 #pragma unroll
-    for (int j = 0; j < 4; ++j)
-      if (j < wpt && tid + j * consumers < K / 8) nwv[j] = reinterpret_cast<const uint4*>(a.norm_w)[tid + j * consumers];
+    for (int j = 0; j < 4; ++j) {
+      if (owned) {
+        if (j < nsl) nwv[j] = reinterpret_cast<const uint4*>(a.norm_w)[(cls + kWarps * j) * 32 + lane];
+      } else if (j < wpt && tid + j * consumers < K / 8) {
+        nwv[j] = reinterpret_cast<const uint4*>(a.norm_w)[tid + j * consumers];
+      }
+    }
   }
   // Warm the activation's address translation and L2 lines before the wait (a prefetch is
   // not a read of the data: the loads after the wait see the previous kernel's writes).
@@ -351,6 +368,82 @@ __global__ void __launch_bounds__(kWarps * 32 + 32, 1) w4a16_packed(StreamArgs a
       }
     }
     named_sync(1, consumers);
+  } else if (owned) {
+    const uint4* xsrc = reinterpret_cast<const uint4*>(a.x);
+    const uint4* rsrc = reinterpret_cast<const uint4*>(a.residual);
+    uint4 ow[4];
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      if (i >= nsl) continue;
+      const int word = (cls + kWarps * i) * 32 + lane;
+      uint4 xw = xsrc[word];
+      if (ADD) {
+        const uint4 rw = rsrc[word];
+        const uint32_t xa[4] = {xw.x, xw.y, xw.z, xw.w}, ra[4] = {rw.x, rw.y, rw.z, rw.w};
+        uint32_t o[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          __nv_bfloat162 pr = __floats2bfloat162_rn(round_bf16(bf16_lo(xa[k]) + bf16_lo(ra[k])),
+                                                    round_bf16(bf16_hi(xa[k]) + bf16_hi(ra[k])));
+          o[k] = *reinterpret_cast<uint32_t*>(&pr);
+        }
+        xw = make_uint4(o[0], o[1], o[2], o[3]);
+        if (a.summed && blockIdx.x == 0) reinterpret_cast<uint4*>(a.summed)[word] = xw;
+      }
+      if (NORM) {
+        const uint32_t xa[4] = {xw.x, xw.y, xw.z, xw.w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          ss += bf16_lo(xa[k]) * bf16_lo(xa[k]);
+          ss += bf16_hi(xa[k]) * bf16_hi(xa[k]);
+        }
+      }
+      ow[i] = xw;
+    }
+    float inv = 1.f;
+    if (NORM) {  // kernels.py:57-59, 76-82: sum of squares over all K (every slice is owned once)
+      ss = warp_sum(ss);
+      if (lane == 0) red[warp] = ss;
+      named_sync(1, consumers);
+      float tot = 0.f;
+#pragma unroll
+      for (int w = 0; w < kWarps; ++w) tot += red[w];
+      inv = 1.0f / sqrtf(tot / (float)K + a.eps);
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      if (i >= nsl) continue;
+      const int j = cls + kWarps * i, word = j * 32 + lane;
+      const uint32_t xa[4] = {ow[i].x, ow[i].y, ow[i].z, ow[i].w};
+      float v8[8];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) { v8[2 * k] = bf16_lo(xa[k]); v8[2 * k + 1] = bf16_hi(xa[k]); }
+      if (NORM) {
+        const uint32_t na[4] = {nwv[i].x, nwv[i].y, nwv[i].z, nwv[i].w};
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          v8[2 * k] = round_bf16(round_bf16(v8[2 * k] * inv) * bf16_lo(na[k]));
+          v8[2 * k + 1] = round_bf16(round_bf16(v8[2 * k + 1] * inv) * bf16_hi(na[k]));
+        }
+      }
+      float mx = 0.f, wsum = 0.f;
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        mx = fmaxf(mx, fabsf(v8[k]));
+        wsum += v8[k];
+      }
+      mx = warp_max(mx);  // this slice's max |x|: its scale c = 2^(9 - e)
+      const int ex = mx > 0.f ? min(max((int)((__float_as_uint(mx) >> 23) & 0xFF) - 127, -100), 100) : 0;
+      const float cs = __uint_as_float((uint32_t)(127 + 9 - ex) << 23);
+      xp[word] = make_uint4(pack_half2(v8[0] * cs, v8[4] * cs), pack_half2(v8[1] * cs * 0.0625f, v8[5] * cs * 0.0625f),
+                            pack_half2(v8[2] * cs, v8[6] * cs), pack_half2(v8[3] * cs * 0.0625f, v8[7] * cs * 0.0625f));
+      wsum += __shfl_xor_sync(0xffffffffu, wsum, 1);
+      wsum += __shfl_xor_sync(0xffffffffu, wsum, 2);
+      if ((lane & 3) == 0) xsum[word >> 2] = wsum * cs;
+      if (lane == 0) slice_scale[j] = __uint_as_float((uint32_t)(127 + 24 - 9 + ex) << 23);  // 2^24 / c
+    }
+    __syncwarp();  // the warp reads only the slices it wrote
   } else {
   constexpr int br = 0;
   const uint4* xsrc = reinterpret_cast<const uint4*>(a.x + (size_t)br * K);
@@ -364,33 +457,51 @@ __global__ void __launch_bounds__(kWarps * 32 + 32, 1) w4a16_packed(StreamArgs a
     uint4 xw;
     if (TPM & 1) {  // x = bf16(sum over ranks), ranks in order, fp32 sum; cells polled (bounded)
       float acc8[8] = {};
-      for (int r = 0; r < a.tp_world; ++r) {
-        const unsigned long long* cell =
-            reinterpret_cast<const unsigned long long*>(a.tp_in + (size_t)r * (K / 2) + (size_t)word * 4);
-        uint32_t pa[4] = {0, 0, 0, 0};
-        bool fresh = false;
-        // Each cell is one 64-bit element {flag << 32 | bf16 pair}: a single-copy-atomic access,
-        // so seeing this step's flag means seeing this step's pair. The whole poll of this
-        // kernel is bounded by one deadline; once any thread of the CTA has given up (or an
-        // earlier exchange failed), the others stop polling at their next check.
-        for (long it = 0; !fresh && !tp_failed; ++it) {
-          unsigned long long c[4];
-          asm volatile("ld.relaxed.sys.global.v2.u64 {%0, %1}, [%2];" : "=l"(c[0]), "=l"(c[1]) : "l"(cell) : "memory");
-          asm volatile("ld.relaxed.sys.global.v2.u64 {%0, %1}, [%2];" : "=l"(c[2]), "=l"(c[3]) : "l"(cell + 2)
-                       : "memory");
-          fresh = true;
+      // Each cell is one 64-bit element {flag << 32 | bf16 pair}: a single-copy-atomic access,
+      // so seeing this step's flag means seeing this step's pair. kPollRanks ranks' cells are
+      // polled together (their loads in flight at once: one round trip per group of ranks, not
+      // one per rank); the sum is still taken in rank order. The whole poll of this kernel is bounded
+      // by one deadline; once any thread of the CTA has given up (or an earlier exchange
+      // failed), the others stop polling at their next check.
+      for (int r0 = 0; r0 < a.tp_world; r0 += kPollRanks) {
+        const int nr = min(kPollRanks, a.tp_world - r0);
+        uint32_t pa[kPollRanks][4] = {};
+        uint32_t pending = (1u << nr) - 1u;
+        for (long it = 0; pending && !tp_failed; ++it) {
+          unsigned long long cc[kPollRanks][4];
 #pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            pa[i] = (uint32_t)c[i];
-            fresh = fresh && (uint32_t)(c[i] >> 32) == tp_flag;
+          for (int q = 0; q < kPollRanks; ++q) {
+            if (!(pending >> q & 1u)) continue;
+            const unsigned long long* cell =
+                reinterpret_cast<const unsigned long long*>(a.tp_in + (size_t)(r0 + q) * (K / 2) + (size_t)word * 4);
+            asm volatile("ld.relaxed.sys.global.v2.u64 {%0, %1}, [%2];" : "=l"(cc[q][0]), "=l"(cc[q][1]) : "l"(cell)
+                         : "memory");
+            asm volatile("ld.relaxed.sys.global.v2.u64 {%0, %1}, [%2];" : "=l"(cc[q][2]), "=l"(cc[q][3]) : "l"(cell + 2)
+                         : "memory");
           }
-          if (!fresh && (it & 63) == 63 &&
+#pragma unroll
+          for (int q = 0; q < kPollRanks; ++q) {
+            if (!(pending >> q & 1u)) continue;
+            bool fresh = true;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) fresh = fresh && (uint32_t)(cc[q][i] >> 32) == tp_flag;
+            if (fresh) {
+#pragma unroll
+              for (int i = 0; i < 4; ++i) pa[q][i] = (uint32_t)cc[q][i];
+              pending &= ~(1u << q);
+            }
+          }
+          if (pending && (it & 63) == 63 &&
               (globaltimer_ns() - tp_t0 > kExchangeDeadlineNs || *(volatile int*)&g_error_word == 2))
             tp_failed = 1;
         }
-        if (!fresh) atomicExch(&g_error_word, 2);
+        if (pending) atomicExch(&g_error_word, 2);
 #pragma unroll
-        for (int i = 0; i < 4; ++i) { acc8[2 * i] += bf16_lo(pa[i]); acc8[2 * i + 1] += bf16_hi(pa[i]); }
+        for (int q = 0; q < kPollRanks; ++q) {
+          if (q >= nr) continue;
+#pragma unroll
+          for (int i = 0; i < 4; ++i) { acc8[2 * i] += bf16_lo(pa[q][i]); acc8[2 * i + 1] += bf16_hi(pa[q][i]); }
+        }
       }
       uint32_t o4[4];
 #pragma unroll
@@ -465,6 +576,8 @@ __global__ void __launch_bounds__(kWarps * 32 + 32, 1) w4a16_packed(StreamArgs a
   const float cs = __uint_as_float((uint32_t)(127 + 9 - ex) << 23);  // c
   const float ic = __uint_as_float((uint32_t)(127 + 24 - 9 + ex) << 23);  // 2^24 / c
   if (br == 0) inv_c0 = ic; else inv_c1 = ic;
+  if (NBR == 1)
+    for (int j = tid; j < S; j += consumers) slice_scale[j] = ic;  // one scale for every slice
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
     const int word = tid + j * consumers;
@@ -491,6 +604,7 @@ __global__ void __launch_bounds__(kWarps * 32 + 32, 1) w4a16_packed(StreamArgs a
   uint32_t bz0 = 0, bz1 = 0;   // B operands of the zero-point mma (hi and lo fp16 parts)
   uint32_t bz2 = 0, bz3 = 0;   // two rows: the zero-point mma of group 2c + 1
   int cur_j = -1;
+  float cur_scale = 1.f;       // one row: 2^24 / c of slice cur_j
   auto load_b = [&](int j) {   // B fragments of slice j: real data for the designated lanes only
     if (NBR == 2) {            // column 2c + hsel carries activation row hsel, both groups
       const bool live = hsel == 0 || hsel == 1;
@@ -526,6 +640,7 @@ __global__ void __launch_bounds__(kWarps * 32 + 32, 1) w4a16_packed(StreamArgs a
     const float h0 = __half2float(__float2half_rn(z0)), h1 = __half2float(__float2half_rn(z1));
     bz0 = pack_half2(h0, h1);
     bz1 = pack_half2(z0 - h0, z1 - h1);
+    cur_scale = slice_scale[j];
     cur_j = j;
   };
 
@@ -580,9 +695,9 @@ __global__ void __launch_bounds__(kWarps * 32 + 32, 1) w4a16_packed(StreamArgs a
         } else {
           float va, vb;
           block_dot<MT_NACC>(bk, bl, bh, bz0, bz1, va, vb);
-          if (c == 0) {
-            pp[r] += va;
-            pp[r + 8] += vb;
+          if (c == 0) {  // in units of the row: the slice's 2^24 / c (a power of two, exact)
+            pp[r] += va * cur_scale;
+            pp[r + 8] += vb * cur_scale;
           }
         }
       }
@@ -601,7 +716,7 @@ __global__ void __launch_bounds__(kWarps * 32 + 32, 1) w4a16_packed(StreamArgs a
     float sum = 0.f;
 #pragma unroll 4
     for (int w = 0; w < kWarps; ++w) sum += partial[((size_t)w * max_tiles + lt) * 16 * NBR + tr];
-    partial[(size_t)lt * 16 * NBR + tr] = sum * ((NBR == 2 && tr >= 16) ? inv_c1 : inv_c0);
+    partial[(size_t)lt * 16 * NBR + tr] = NBR == 1 ? sum : sum * (tr >= 16 ? inv_c1 : inv_c0);
   }
   named_sync(1, consumers);
   // tiles wholly inside this CTA's range

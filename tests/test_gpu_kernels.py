@@ -156,6 +156,14 @@ def test_silu_mul(cuda_device):
     y = kernels.silu_mul(dev_bf16(g["silu_in"], cuda_device))
     assert np.mean(host_bits(y) == g["silu_out"]) > 0.995
     close(host_bits(y), from_bf16_bits(g["silu_out"]))
+    # the 8-wide kernel (n % 8 == 0) and the scalar one (n = 1004): the same bits as the oracle but
+    # where expf and numpy's exp round differently before the bf16 rounding
+    for rows, n in ((37, 12288), (3, 1004)):
+        xb = synthetic.activation(rows + n, (rows, 2 * n), 2.0)
+        y = host_bits(kernels.silu_mul(dev_bf16(xb, cuda_device)))
+        ref = ops.silu_mul(from_bf16_bits(xb))
+        assert np.mean(y == bf16_bits(ref)) > 0.995, (rows, n)
+        close(y, ref)
 
 
 def test_embedding_sum_exact(cuda_device):

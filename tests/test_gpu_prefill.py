@@ -105,3 +105,34 @@ def test_prefill_long_prompt_matches_oracle_and_decode_continues(two_layer, cuda
     print(f"decode after prefill: {differ} of 33 ids differ from the row-by-row path")
     assert differ <= 2
     assert int(llm.engine.status.item()) == 0
+
+
+@pytest.mark.parametrize("start,n", [(0, 512), (100, 150), (0, 1), (37, 64)])
+def test_prefill_attention_kernels_agree_with_oracle(cuda_device, start, n):
+    """The tensor-core prefill attention (default) and the CUDA-core kernel (flags bit 1) against
+    the oracle's causal attention (fp32 softmax, the reference's 1/sqrt(128) scale) on random
+    q / cache rows: a cached prefix (start > 0), a partial last 64-row tile, a single row. The
+    tensor-core kernel rounds the probabilities to bf16 before P V: within 2e-2 + 1e-2 |ref|."""
+    from moss_tts._runtime import native
+    nq, nkv, L = 32, 8, 640
+    g = torch.Generator(device=cuda_device).manual_seed(start + n)
+    q = torch.randn(n, nq, 128, device=cuda_device, generator=g).bfloat16()
+    k = torch.randn(nkv, L, 128, device=cuda_device, generator=g).bfloat16()
+    v = torch.randn(nkv, L, 128, device=cuda_device, generator=g).bfloat16()
+    outs = []
+    for flags in (0, 2):
+        o = torch.full((n, nq * 128), float("nan"), device=cuda_device, dtype=torch.bfloat16)
+        native.call("mt_prefill_attention", q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), start, n, nq, nkv,
+                    L, flags, torch.cuda.current_stream(cuda_device).cuda_stream)
+        outs.append(_host(o))
+    qh, kh, vh = _host(q), _host(k), _host(v)
+    ref = np.zeros((n, nq, 128))
+    for h in range(nq):
+        kk, vv = kh[h // 4], vh[h // 4]
+        for t in range(n):
+            lg = kk[: start + t + 1] @ qh[t, h] * (1 / np.sqrt(128))
+            p = np.exp(lg - lg.max())
+            ref[t, h] = (p / p.sum()) @ vv[: start + t + 1]
+    for name, got in zip(("tensor-core", "CUDA-core"), outs):
+        ok, _ = _report(f"prefill attention {name} start {start} n {n}", got, ref.reshape(n, -1), 2e-2, 1e-2)
+        assert ok, name
