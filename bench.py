@@ -57,6 +57,8 @@ def parse():
                     help="config 0 alone: the 12288 x 4096 W4A16 G32 GEMV (zero points), 8 rotating weight sets "
                          "(233 MB > L2, every launch L2-cold), CUDA events; prints one JSON line with its roofline")
     ap.add_argument("--config0-sets", type=int, default=8, help=argparse.SUPPRESS)
+    ap.add_argument("--profile-prefill", action="store_true",
+                    help="per-kernel device time of one 512-token prefill (CUPTI through torch.profiler)")
     ap.add_argument("--profile-kernel", action="store_true",
                     help="only launch the dominant kernel (packed add+norm+gate/up+SiLU GEMV), once per "
                          "layer per step, for an ncu capture; prints its mean launch time")
@@ -505,6 +507,48 @@ def batch_sweep(args, rank, world, local):
         dist.destroy_process_group()
 
 
+def profile_prefill(args):
+    """Per-kernel device time of one 512-token ``FastLLM.prefill`` of the config-3 model (full
+    text head), each projection mode after two warm-up prompts, from CUPTI kernel records
+    (torch.profiler): where the prompt pass spends its time. Not a bench line."""
+    import torch
+    from torch.profiler import ProfilerActivity, profile
+
+    from moss_tts._runtime.config import DecoderConfig
+    from moss_tts._runtime.llm import FastLLM
+    from moss_tts._runtime.weights import DecoderWeights
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    cfg = DecoderConfig().with_(num_layers=args.layers)
+    with torch.inference_mode():
+        w = DecoderWeights.random(cfg, dev, seed=0, preset="gptq", full_text_head=True)
+        llm = FastLLM(w, max_length=1024, greedy=True)
+        g = torch.Generator().manual_seed(3)
+        ids = torch.full((1, PROMPT, 33), 1024, dtype=torch.long)
+        ids[0, :, 0] = torch.randint(0, cfg.vocab_size, (PROMPT,), generator=g)
+        ids[0, :, 1:] = torch.randint(0, 1025, (PROMPT, 32), generator=g)
+        ids = ids.to(dev)
+        for mode in ("bf16", "dequant", "w4"):
+            llm.prefill_mode = mode
+            for _ in range(2):
+                llm.prefill(ids)
+            torch.cuda.synchronize(dev)
+            with profile(activities=[ProfilerActivity.CUDA]) as prof:
+                llm.prefill(ids)
+                torch.cuda.synchronize(dev)
+            rows = {}
+            for e in prof.key_averages():
+                t = getattr(e, "device_time_total", None) or getattr(e, "cuda_time_total", 0)
+                if t > 0 and e.count > 0 and not e.key.startswith("cuda"):
+                    rows[e.key] = (e.count, t)
+            total = sum(t for _, t in rows.values())
+            print(f"== prefill mode {mode}: {total / 1000:.3f} ms of kernel time, {PROMPT} tokens, {args.layers} layers")
+            for name, (n, t) in sorted(rows.items(), key=lambda kv: -kv[1][1])[:12]:
+                print(f"{t / 1000:9.3f} ms {100 * t / total:5.1f}% {n:5d} x {t / n:8.2f} us  {name[:90]}")
+            llm.prefill_graphs.clear()
+
+
 def main():
     args = parse()
     rank = int(os.environ.get("RANK", "0"))
@@ -524,6 +568,9 @@ def main():
         return
     if args.config0:
         config0(args)
+        return
+    if args.profile_prefill:
+        profile_prefill(args)
         return
     import torch
     import torch.distributed as dist
@@ -637,6 +684,32 @@ def main():
         kernel_us = k0.elapsed_time(k1) * 1000 / (reps * len(weights.layers))
         del kgraph
 
+        # ---------------- the 32 steps after audio_start as one graph (FirstAudioGraph)
+        first_audio = None
+        if world == 1:
+            from moss_tts._runtime.first_audio_graph import FirstAudioGraph
+            fa = FirstAudioGraph(llm, 1024)
+            fa.warmup()
+            start_row = torch.full((1, 1, 33), cfg.audio_pad_code, dtype=torch.long, device=dev)
+            start_row[0, 0, 0] = cfg.audio_start_token_id
+            for _ in range(2):
+                fa.run(start_row, PROMPT)
+            torch.cuda.synchronize(dev)
+            a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a0.record(stream)
+            for _ in range(5):
+                fa.run(start_row, PROMPT)
+            a1.record(stream)
+            torch.cuda.synchronize(dev)
+            fms = a0.elapsed_time(a1) / 5
+            first_audio = {"ms_per_32_steps": round(fms, 3), "ms_per_step": round(fms / 32, 4),
+                           "positions": f"{PROMPT}..{PROMPT + 31}", "sampling": "greedy",
+                           "reference_published_ms": 60.39,
+                           "reference_note": "H200 NVL, G32 W4A8, first 32 decode steps after audio start "
+                                             "(docs/benchmark.json:86)"}
+            fa.graph = None
+            del fa
+
         # ---------------- prefill of the 512-token prompt (FastLLM.prefill, one GPU)
         prefill = None
         if world == 1 and not args.no_prefill:
@@ -712,6 +785,7 @@ def main():
         "cpu_baseline": cpu,
         "bf16": bf16,
         "prefill": prefill,
+        "first_audio": first_audio,
         "clocks": clocks.summary(),
         "gpu_launches": launches * args.steps,
         "status": status,
