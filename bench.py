@@ -57,6 +57,8 @@ def parse():
                     help="config 0 alone: the 12288 x 4096 W4A16 G32 GEMV (zero points), 8 rotating weight sets "
                          "(233 MB > L2, every launch L2-cold), CUDA events; prints one JSON line with its roofline")
     ap.add_argument("--config0-sets", type=int, default=8, help=argparse.SUPPRESS)
+    ap.add_argument("--profile-attention", default=None, metavar="B,CTX",
+                    help="decode attention alone: B sequences at CTX cached tokens, one layer (GB/s line)")
     ap.add_argument("--profile-prefill", action="store_true",
                     help="per-kernel device time of one 512-token prefill (CUPTI through torch.profiler)")
     ap.add_argument("--profile-kernel", action="store_true",
@@ -507,6 +509,60 @@ def batch_sweep(args, rank, world, local):
         dist.destroy_process_group()
 
 
+def profile_attention(batch: int, ctx: int):
+    """The fused decode attention (``mt_attention_decode``: QK-norm, RoPE, KV-row write, cluster
+    split-K attention) alone for one layer: ``batch`` sequences at position ``ctx - 1`` (``ctx``
+    cached tokens each, the last one written by the call), 32 query / 8 KV heads of 128, random
+    cache. Algorithmic bytes per launch: the K and V rows read (batch x 8 x ctx x 512 B) plus the
+    q|k|v rows and outputs; with more than 126 MB of cache every launch reads it from HBM.
+    Eight timed launches after three warm-up ones, CUDA events."""
+    import torch
+
+    from moss_tts._runtime import native
+    from moss_tts._runtime.engine import rope_tables
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    nq, nkv, d = 32, 8, 128
+    max_len = (ctx + 127) // 128 * 128
+    g = torch.Generator(device=dev).manual_seed(0)
+    k = torch.randn(batch, nkv, max_len, d, device=dev, generator=g).to(torch.bfloat16)
+    v = torch.randn(batch, nkv, max_len, d, device=dev, generator=g).to(torch.bfloat16)
+    qkv = torch.randn(batch, (nq + 2 * nkv) * d, device=dev, generator=g).to(torch.bfloat16)
+    qn = torch.ones(d, device=dev, dtype=torch.bfloat16)
+    cos, sin = (t.to(dev) for t in rope_tables(max_len, d, 1e6))
+    pos = torch.full((batch,), ctx - 1, dtype=torch.long, device=dev)
+    out = torch.empty(batch, nq * d, device=dev, dtype=torch.bfloat16)
+    splits = max_len // 32
+    partial = torch.empty(batch * nkv * splits * (nq // nkv) * d, device=dev, dtype=torch.float32)
+    lse = torch.empty(batch * nkv * splits * (nq // nkv), device=dev, dtype=torch.float32)
+    tickets = torch.zeros(batch * nkv, device=dev, dtype=torch.int32)
+    status = torch.zeros(1, device=dev, dtype=torch.int32)
+    s = torch.cuda.current_stream(dev).cuda_stream
+
+    def launch():
+        native.call("mt_attention_decode", qkv.data_ptr(), qn.data_ptr(), qn.data_ptr(), cos.data_ptr(),
+                    sin.data_ptr(), pos.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), partial.data_ptr(),
+                    lse.data_ptr(), tickets.data_ptr(), batch, nq, nkv, max_len, 1, 1e-6, status.data_ptr(), 0, s)
+
+    for _ in range(3):
+        launch()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(8):
+        launch()
+    e1.record()
+    torch.cuda.synchronize(dev)
+    us = e0.elapsed_time(e1) * 1000 / 8
+    nbytes = batch * nkv * ctx * d * 2 * 2 + batch * ((nq + 2 * nkv) * d + nq * d) * 2
+    peak, kind = measured_peaks()
+    gbs = nbytes / (us * 1e-6) / 1e9
+    print(json.dumps({"kernel": "mt_attention_decode (cluster)", "batch": batch, "ctx": ctx,
+                      "bytes_per_launch": nbytes, "launch_us": round(us, 3), "achieved_gbs": round(gbs, 1),
+                      "peak_gbs": peak, "peak_kind": kind, "frac": round(gbs / peak, 4),
+                      "status": int(status.item()), "error_word": native.error_word(clear=True)}), flush=True)
+
+
 def profile_prefill(args):
     """Per-kernel device time of one 512-token ``FastLLM.prefill`` of the config-3 model (full
     text head), each projection mode after two warm-up prompts, from CUPTI kernel records
@@ -571,6 +627,10 @@ def main():
         return
     if args.profile_prefill:
         profile_prefill(args)
+        return
+    if args.profile_attention:
+        b, ctx = (int(v) for v in args.profile_attention.split(","))
+        profile_attention(b, ctx)
         return
     import torch
     import torch.distributed as dist
