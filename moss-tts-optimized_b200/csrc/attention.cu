@@ -15,7 +15,12 @@
 // the programmatic-dependency wait.
 // Scratch (fp32 partials, LSE, tickets) is caller-provided global memory.
 #include <cooperative_groups.h>
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <stdlib.h>
+#include <string.h>
+
+#include <mutex>
 
 #include "common.cuh"
 
@@ -295,9 +300,45 @@ constexpr int kClusterCtas = 8;
 constexpr int kAttnThreads = 256;               // 8 warps per CTA (16 measured no faster)
 constexpr int kTokenGroups = kAttnThreads / 64;  // P.V token groups of 64 dim-pair threads
 
-template <int REP, int kChunk>
-__global__ void __launch_bounds__(kAttnThreads) attention_cluster(AttnArgs a) {
-  extern __shared__ __align__(128) uint8_t sm[];  // 2 slots x {K[kChunk][128], V[kChunk][128]} bf16
+// Tensor-core chunk arithmetic (TC): the logits S = Q K^T and O += P V on mma.sync m16n8k16
+// bf16 with the query heads as the (zero-padded) A rows. K and V chunks arrive by TMA tensor
+// copies in two 64-dim boxes with the 128-byte swizzle (16-byte piece c of row r stored at
+// piece c ^ (r & 7)), so the 8-row ldmatrix reads hit eight different bank groups. P is split
+// into bf16 hi + lo parts (two mma), keeping 16 significant bits like the reference's fp32 P.
+__device__ __forceinline__ void attn_ldsm_x2(uint32_t& r0, uint32_t& r1, uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0, %1}, [%2];" : "=r"(r0), "=r"(r1) : "r"(addr));
+}
+__device__ __forceinline__ void attn_ldsm_x4_t(uint32_t (&r)[4], uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+__device__ __forceinline__ void attn_mma(float (&d)[4], uint32_t a0, uint32_t a2, uint32_t b0, uint32_t b1) {
+  // A rows 8..15 (fragments a1, a3) are zero: only rows g < 8 can carry a query head
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t attn_pack(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+// Byte offset of 16-byte piece `piece` (0..15 over the 128 dims) of staged row r in a chunk of
+// kChunk rows: box piece / 8 (dims 0-63 | 64-127), swizzled piece within the box's row.
+template <int kChunk>
+__device__ __forceinline__ uint32_t attn_swz(int r, int piece) {
+  return (uint32_t)((piece >> 3) * kChunk * 128 + r * 128 + (((piece & 7) ^ (r & 7)) << 4));
+}
+
+template <int REP, int kChunk, bool TC>
+__global__ void __launch_bounds__(kAttnThreads)
+    attention_cluster(AttnArgs a, const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap) {
+  extern __shared__ __align__(128) uint8_t sm_raw[];  // 2 slots x {K[kChunk][128], V[kChunk][128]} bf16
+  // TC: the swizzled TMA boxes need 1024-byte alignment (the launch adds 1 KB of slack)
+  uint8_t* sm = TC ? reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(sm_raw) + 1023) & ~uintptr_t(1023))
+                   : sm_raw;
   constexpr int kQStride = 36;                     // floats per 32-dim quarter of q (+4 pad)
   __shared__ __align__(16) float qs[REP * 4 * kQStride];
   __shared__ __align__(16) float pr[kChunk][REP];  // logits, then probabilities
@@ -329,6 +370,21 @@ __global__ void __launch_bounds__(kAttnThreads) attention_cluster(AttnArgs a) {
     const int slot = c & 1, cs = t0 + c * kChunk, rows = min(kChunk, t1 - cs);
     const unsigned bytes = (unsigned)(rows * kRowBytes);
     uint8_t* kdst = sm + (size_t)slot * kSlotBytes;
+    if (TC) {  // four boxes of 64 dims x kChunk rows (whole boxes, also for a short last chunk)
+      const int y = (int)(((size_t)b * a.nkv + kh) * a.max_len) + cs;
+      asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(attn_smem_u32(&full[slot])),
+                   "r"((unsigned)(4 * kChunk * 128)) : "memory");
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const CUtensorMap* map = q < 2 ? &kmap : &vmap;
+        asm volatile(
+            "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+                attn_smem_u32(kdst + (size_t)q * kChunk * 128)),
+            "l"(reinterpret_cast<uint64_t>(map)), "r"((q & 1) * 64), "r"(y), "r"(attn_smem_u32(&full[slot]))
+            : "memory");
+      }
+      return;
+    }
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(attn_smem_u32(&full[slot])),
                  "r"(2 * bytes) : "memory");
     asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
@@ -412,7 +468,21 @@ __global__ void __launch_bounds__(kAttnThreads) attention_cluster(AttnArgs a) {
   float acc[REP][2];
 #pragma unroll
   for (int h = 0; h < REP; ++h) acc[h][0] = acc[h][1] = 0.f;
+  // TC: lane (g, t4) of every warp carries query head g < REP as A row g; o[jd] accumulates
+  // that head's dims 16 warp + 8 jd + 2 t4 (+1), the warp's two 8-dim n-tiles.
+  const int g = lane >> 2, t4 = lane & 3;
+  const bool hrow = g < REP;
+  uint32_t qa[8][2];
+  float o[2][4] = {};
   __syncthreads();
+  if (TC) {
+#pragma unroll
+    for (int kk = 0; kk < 8; ++kk) {  // dims 16 kk + 2 t4 (+1) and + 8: quarter kk / 2 of qs
+      const float* qrow = &qs[((hrow ? g : 0) * 4 + (kk >> 1)) * kQStride + (kk & 1) * 16 + 2 * t4];
+      qa[kk][0] = hrow ? attn_pack(qrow[0], qrow[1]) : 0u;
+      qa[kk][1] = hrow ? attn_pack(qrow[8], qrow[9]) : 0u;
+    }
+  }
 
   int c = 0;
   for (; c < chunks; ++c) {
@@ -422,13 +492,46 @@ __global__ void __launch_bounds__(kAttnThreads) attention_cluster(AttnArgs a) {
     const int slot = c & 1, cs = t0 + c * kChunk, rows = min(kChunk, t1 - cs);
     const __nv_bfloat16* ks = reinterpret_cast<const __nv_bfloat16*>(sm + (size_t)slot * kSlotBytes);
     const __nv_bfloat16* vs = ks + (size_t)kChunk * kHeadDim;
-    if (owner && p >= cs && p < cs + rows) {  // the chunk holding this step's row (CTA-uniform)
-      if (warp == REP) {
+    const bool fresh_here = owner && p >= cs && p < cs + rows;  // this step's row (CTA-uniform)
+    if (fresh_here && warp == REP) {
+      if (TC) {  // dims 4 lane .. +3: piece lane / 2 (swizzled), byte 8 (lane & 1) within it
+        const uint32_t off = attn_swz<kChunk>(p - cs, lane >> 1) + 8 * (lane & 1);
+        *reinterpret_cast<uint2*>(reinterpret_cast<uint8_t*>(const_cast<__nv_bfloat16*>(ks)) + off) = krow;
+        *reinterpret_cast<uint2*>(reinterpret_cast<uint8_t*>(const_cast<__nv_bfloat16*>(vs)) + off) = vrow;
+      } else {
         *reinterpret_cast<uint2*>(const_cast<__nv_bfloat16*>(ks) + (size_t)(p - cs) * kHeadDim + 4 * lane) = krow;
         *reinterpret_cast<uint2*>(const_cast<__nv_bfloat16*>(vs) + (size_t)(p - cs) * kHeadDim + 4 * lane) = vrow;
       }
-      __syncthreads();
     }
+    // TC: a short last chunk's box rows past `rows` hold other cache rows (or the fill): the V
+    // rows meet zero weights in P V, so make them zero (whole 128-byte rows: swizzle-agnostic)
+    const bool pad_v = TC && rows < kChunk;
+    if (pad_v) {
+      uint8_t* vb = reinterpret_cast<uint8_t*>(const_cast<__nv_bfloat16*>(vs));
+      for (int i = tid; i < 2 * (kChunk - rows) * 8; i += kAttnThreads) {
+        const int box = i / ((kChunk - rows) * 8), rem = i - box * (kChunk - rows) * 8;
+        *reinterpret_cast<uint4*>(vb + (size_t)box * kChunk * 128 + (size_t)(rows + rem / 8) * 128 + (rem & 7) * 16) =
+            make_uint4(0, 0, 0, 0);
+      }
+    }
+    if (fresh_here || pad_v) __syncthreads();
+    if (TC) {  // logits on the tensor cores: warp w takes 8-token n-tiles w, w + 8, ...
+      const uint32_t kb = attn_smem_u32(ks);
+      for (int j = warp; j * 8 < rows; j += kAttnThreads / 32) {
+        float sacc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          uint32_t b0, b1;
+          attn_ldsm_x2(b0, b1, kb + attn_swz<kChunk>(8 * j + (lane & 7), 2 * kk + ((lane >> 3) & 1)));
+          attn_mma(sacc, qa[kk][0], qa[kk][1], b0, b1);
+        }
+        const int t = 8 * j + 2 * t4;
+        if (hrow) {
+          if (t < rows) pr[t][g] = sacc[0] * kScale;
+          if (t + 1 < rows) pr[t + 1][g] = sacc[1] * kScale;
+        }
+      }
+    } else {
     // logits: item = ((t * REP) + h) * 4 + quarter; four consecutive lanes share (t, h)
     const int items = rows * REP * 4;
     for (int base = 0; base < items; base += kAttnThreads) {
@@ -458,6 +561,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_cluster(AttnArgs a) {
       v += __shfl_xor_sync(0xffffffffu, v, 2);
       if (item < items && qt == 0) pr[t][h] = v * kScale;
     }
+    }
     __syncthreads();
     // online softmax: warp h owns query head h
     if (warp < REP) {
@@ -481,7 +585,33 @@ __global__ void __launch_bounds__(kAttnThreads) attention_cluster(AttnArgs a) {
       }
     }
     __syncthreads();
-    {
+    if (TC) {  // O += P V: warp w owns dims 16 w .. 16 w + 15 (two n-tiles) of every head
+      const float sc = hrow ? scale[g] : 0.f;
+#pragma unroll
+      for (int jd = 0; jd < 2; ++jd)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) o[jd][e] *= sc;
+      const uint32_t vb = attn_smem_u32(vs);
+      for (int kk = 0; kk * 16 < rows; ++kk) {
+        const int t = 16 * kk + 2 * t4;
+        float p4[4] = {0.f, 0.f, 0.f, 0.f};  // P[g][t], [t + 1], [t + 8], [t + 9]; zero past the chunk
+        if (hrow) {
+          if (t < rows) p4[0] = pr[t][g];
+          if (t + 1 < rows) p4[1] = pr[t + 1][g];
+          if (t + 8 < rows) p4[2] = pr[t + 8][g];
+          if (t + 9 < rows) p4[3] = pr[t + 9][g];
+        }
+        const uint32_t h0 = attn_pack(p4[0], p4[1]), h2 = attn_pack(p4[2], p4[3]);
+        const uint32_t l0 = attn_pack(p4[0] - bf16_lo(h0), p4[1] - bf16_hi(h0));
+        const uint32_t l2 = attn_pack(p4[2] - bf16_lo(h2), p4[3] - bf16_hi(h2));
+        uint32_t bv[4];
+        attn_ldsm_x4_t(bv, vb + attn_swz<kChunk>(16 * kk + (lane & 7) + 8 * ((lane >> 3) & 1), 2 * warp + (lane >> 4)));
+        attn_mma(o[0], h0, h2, bv[0], bv[1]);
+        attn_mma(o[1], h0, h2, bv[2], bv[3]);
+        attn_mma(o[0], l0, l2, bv[0], bv[1]);
+        attn_mma(o[1], l0, l2, bv[2], bv[3]);
+      }
+    } else {
       float scl[REP];
 #pragma unroll
       for (int h = 0; h < REP; ++h) scl[h] = scale[h];
@@ -509,16 +639,29 @@ __global__ void __launch_bounds__(kAttnThreads) attention_cluster(AttnArgs a) {
     }
     __syncthreads();
   }
-  // sum the token groups, push each 16-dim slice to its owner rank's inbox
+  // sum the token groups (TC: every warp's dim slices are complete), push each 16-dim slice
+  // to its owner rank's inbox
+  if (TC) {
+    if (hrow) {
 #pragma unroll
-  for (int h = 0; h < REP; ++h) *reinterpret_cast<float2*>(&red[tg][h][2 * dp]) = make_float2(acc[h][0], acc[h][1]);
+      for (int jd = 0; jd < 2; ++jd)
+        *reinterpret_cast<float2*>(&red[0][g][16 * warp + 8 * jd + 2 * t4]) = make_float2(o[jd][0], o[jd][1]);
+    }
+  } else {
+#pragma unroll
+    for (int h = 0; h < REP; ++h) *reinterpret_cast<float2*>(&red[tg][h][2 * dp]) = make_float2(acc[h][0], acc[h][1]);
+  }
   __syncthreads();
   for (int item = tid; item < REP * kHeadDim; item += kAttnThreads) {
     const int h = item / kHeadDim, d = item - h * kHeadDim;
-    float o = 0.f;
+    float ov = 0.f;
+    if (TC) {
+      ov = red[0][h][d];
+    } else {
 #pragma unroll
-    for (int g = 0; g < kTokenGroups; ++g) o += red[g][h][d];
-    *cluster.map_shared_rank(&inbox[rank][h][d & 15], d >> 4) = o;
+      for (int gg = 0; gg < kTokenGroups; ++gg) ov += red[gg][h][d];
+    }
+    *cluster.map_shared_rank(&inbox[rank][h][d & 15], d >> 4) = ov;
   }
   if (tid < REP * kClusterCtas) {
     const int h = tid % REP, dst = tid / REP;
@@ -543,13 +686,72 @@ __global__ void __launch_bounds__(kAttnThreads) attention_cluster(AttnArgs a) {
   }
 }
 
+// MT_ATTN_TC = 0 selects the CUDA-core chunk arithmetic (fp32 FMAs on shared memory); the
+// default is the tensor-core one.
+static bool attention_tc() {
+  static int v = -1;
+  if (v < 0) {
+    const char* env = getenv("MT_ATTN_TC");
+    v = (env && env[0] == '0' && env[1] == 0) ? 0 : 1;
+  }
+  return v == 1;
+}
+
+// TMA map of a cache [rows, 128] bf16 (rows = batch x nkv x max_len): boxes of 64 dims x ch
+// rows with the 128-byte swizzle; rows past the end read as zeros. Encoded maps are kept per
+// (pointer, rows, box) so that eager decode steps do not re-encode them every layer.
+static bool cache_map(CUtensorMap* map, const void* base, long long rows, int ch) {
+  struct Entry {
+    const void* base;
+    long long rows;
+    int ch;
+    CUtensorMap map;
+  };
+  static std::mutex mu;
+  static Entry cache[64];
+  static int used = 0, next = 0;
+  std::lock_guard<std::mutex> lock(mu);
+  for (int i = 0; i < used; ++i)
+    if (cache[i].base == base && cache[i].rows == rows && cache[i].ch == ch) {
+      *map = cache[i].map;
+      return true;
+    }
+  static PFN_cuTensorMapEncodeTiled_v12000 encode = nullptr;
+  if (!encode) {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess || !fn)
+      return false;
+    encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  }
+  const cuuint64_t dims[2] = {(cuuint64_t)kHeadDim, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)kHeadDim * 2};
+  const cuuint32_t box[2] = {64, (cuuint32_t)ch};
+  const cuuint32_t estr[2] = {1, 1};
+  if (encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    return false;
+  cache[next] = Entry{base, rows, ch, *map};
+  next = (next + 1) % 64;
+  if (used < 64) ++used;
+  return true;
+}
+
 template <int REP, int CH>
-static cudaError_t launch_cluster_rep(cudaLaunchConfig_t& cfg, const AttnArgs& a) {
-  cfg.dynamicSmemBytes = 2 * (size_t)CH * kHeadDim * 2 * 2;
-  cudaError_t e = cudaFuncSetAttribute(attention_cluster<REP, CH>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)cfg.dynamicSmemBytes);
+static cudaError_t launch_cluster_rep(cudaLaunchConfig_t& cfg, const AttnArgs& a, int batch) {
+  CUtensorMap kmap, vmap;
+  memset(&kmap, 0, sizeof(kmap));
+  memset(&vmap, 0, sizeof(vmap));
+  const long long rows = (long long)batch * a.nkv * a.max_len;
+  const bool tc = attention_tc() && rows < (1LL << 31) && cache_map(&kmap, a.k_cache, rows, CH) &&
+                  cache_map(&vmap, a.v_cache, rows, CH);
+  cfg.dynamicSmemBytes = 2 * (size_t)CH * kHeadDim * 2 * 2 + (tc ? 1024 : 0);
+  auto kern = tc ? attention_cluster<REP, CH, true> : attention_cluster<REP, CH, false>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)cfg.dynamicSmemBytes);
   if (e != cudaSuccess) return e;
-  return cudaLaunchKernelEx(&cfg, attention_cluster<REP, CH>, a);
+  return cudaLaunchKernelEx(&cfg, kern, a, kmap, vmap);
 }
 
 // Chunk size of the cluster kernel: MT_ATTN_CHUNK (32, 64 or 128) overrides the default:
@@ -585,12 +787,12 @@ static cudaError_t launch_cluster_attention(const AttnArgs& a, int batch, int re
   cfg.numAttrs = (flags & kFlagPdl) ? 2 : 1;
   const int ch = attention_chunk(batch, a.nkv);
   switch (rep) {
-    case 4: return ch == 128 ? launch_cluster_rep<4, 128>(cfg, a) : ch == 64 ? launch_cluster_rep<4, 64>(cfg, a)
-                                                                           : launch_cluster_rep<4, 32>(cfg, a);
-    case 2: return ch == 128 ? launch_cluster_rep<2, 128>(cfg, a) : ch == 64 ? launch_cluster_rep<2, 64>(cfg, a)
-                                                                           : launch_cluster_rep<2, 32>(cfg, a);
-    default: return ch == 128 ? launch_cluster_rep<1, 128>(cfg, a) : ch == 64 ? launch_cluster_rep<1, 64>(cfg, a)
-                                                                            : launch_cluster_rep<1, 32>(cfg, a);
+    case 4: return ch == 128 ? launch_cluster_rep<4, 128>(cfg, a, batch) : ch == 64 ? launch_cluster_rep<4, 64>(cfg, a, batch)
+                                                                           : launch_cluster_rep<4, 32>(cfg, a, batch);
+    case 2: return ch == 128 ? launch_cluster_rep<2, 128>(cfg, a, batch) : ch == 64 ? launch_cluster_rep<2, 64>(cfg, a, batch)
+                                                                           : launch_cluster_rep<2, 32>(cfg, a, batch);
+    default: return ch == 128 ? launch_cluster_rep<1, 128>(cfg, a, batch) : ch == 64 ? launch_cluster_rep<1, 64>(cfg, a, batch)
+                                                                            : launch_cluster_rep<1, 32>(cfg, a, batch);
   }
 }
 
