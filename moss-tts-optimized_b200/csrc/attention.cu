@@ -300,11 +300,10 @@ constexpr int kClusterCtas = 8;
 constexpr int kAttnThreads = 256;               // 8 warps per CTA (16 measured no faster)
 constexpr int kTokenGroups = kAttnThreads / 64;  // P.V token groups of 64 dim-pair threads
 
-// Tensor-core chunk arithmetic (TC): the logits S = Q K^T and O += P V on mma.sync m16n8k16
-// bf16 with the query heads as the (zero-padded) A rows. K and V chunks arrive by TMA tensor
-// copies in two 64-dim boxes with the 128-byte swizzle (16-byte piece c of row r stored at
-// piece c ^ (r & 7)), so the 8-row ldmatrix reads hit eight different bank groups. P is split
-// into bf16 hi + lo parts (two mma), keeping 16 significant bits like the reference's fp32 P.
+// Helpers of the tensor-core kernel (attention_ws below): ldmatrix, mma.sync m16n8k16 bf16
+// with zero A rows 8..15, bf16 packing, and the 128-byte swizzle of the TMA boxes (16-byte
+// piece c of row r stored at piece c ^ (r & 7)), which keeps 8-row ldmatrix reads on eight
+// different bank groups.
 __device__ __forceinline__ void attn_ldsm_x2(uint32_t& r0, uint32_t& r1, uint32_t addr) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0, %1}, [%2];" : "=r"(r0), "=r"(r1) : "r"(addr));
 }
@@ -332,13 +331,9 @@ __device__ __forceinline__ uint32_t attn_swz(int r, int piece) {
   return (uint32_t)((piece >> 3) * kChunk * 128 + r * 128 + (((piece & 7) ^ (r & 7)) << 4));
 }
 
-template <int REP, int kChunk, bool TC>
-__global__ void __launch_bounds__(kAttnThreads)
-    attention_cluster(AttnArgs a, const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap) {
-  extern __shared__ __align__(128) uint8_t sm_raw[];  // 2 slots x {K[kChunk][128], V[kChunk][128]} bf16
-  // TC: the swizzled TMA boxes need 1024-byte alignment (the launch adds 1 KB of slack)
-  uint8_t* sm = TC ? reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(sm_raw) + 1023) & ~uintptr_t(1023))
-                   : sm_raw;
+template <int REP, int kChunk>
+__global__ void __launch_bounds__(kAttnThreads) attention_cluster(AttnArgs a) {
+  extern __shared__ __align__(128) uint8_t sm[];  // 2 slots x {K[kChunk][128], V[kChunk][128]} bf16
   constexpr int kQStride = 36;                     // floats per 32-dim quarter of q (+4 pad)
   __shared__ __align__(16) float qs[REP * 4 * kQStride];
   __shared__ __align__(16) float pr[kChunk][REP];  // logits, then probabilities
@@ -370,21 +365,6 @@ __global__ void __launch_bounds__(kAttnThreads)
     const int slot = c & 1, cs = t0 + c * kChunk, rows = min(kChunk, t1 - cs);
     const unsigned bytes = (unsigned)(rows * kRowBytes);
     uint8_t* kdst = sm + (size_t)slot * kSlotBytes;
-    if (TC) {  // four boxes of 64 dims x kChunk rows (whole boxes, also for a short last chunk)
-      const int y = (int)(((size_t)b * a.nkv + kh) * a.max_len) + cs;
-      asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(attn_smem_u32(&full[slot])),
-                   "r"((unsigned)(4 * kChunk * 128)) : "memory");
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const CUtensorMap* map = q < 2 ? &kmap : &vmap;
-        asm volatile(
-            "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
-                attn_smem_u32(kdst + (size_t)q * kChunk * 128)),
-            "l"(reinterpret_cast<uint64_t>(map)), "r"((q & 1) * 64), "r"(y), "r"(attn_smem_u32(&full[slot]))
-            : "memory");
-      }
-      return;
-    }
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(attn_smem_u32(&full[slot])),
                  "r"(2 * bytes) : "memory");
     asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
@@ -468,21 +448,7 @@ __global__ void __launch_bounds__(kAttnThreads)
   float acc[REP][2];
 #pragma unroll
   for (int h = 0; h < REP; ++h) acc[h][0] = acc[h][1] = 0.f;
-  // TC: lane (g, t4) of every warp carries query head g < REP as A row g; o[jd] accumulates
-  // that head's dims 16 warp + 8 jd + 2 t4 (+1), the warp's two 8-dim n-tiles.
-  const int g = lane >> 2, t4 = lane & 3;
-  const bool hrow = g < REP;
-  uint32_t qa[8][2];
-  float o[2][4] = {};
   __syncthreads();
-  if (TC) {
-#pragma unroll
-    for (int kk = 0; kk < 8; ++kk) {  // dims 16 kk + 2 t4 (+1) and + 8: quarter kk / 2 of qs
-      const float* qrow = &qs[((hrow ? g : 0) * 4 + (kk >> 1)) * kQStride + (kk & 1) * 16 + 2 * t4];
-      qa[kk][0] = hrow ? attn_pack(qrow[0], qrow[1]) : 0u;
-      qa[kk][1] = hrow ? attn_pack(qrow[8], qrow[9]) : 0u;
-    }
-  }
 
   int c = 0;
   for (; c < chunks; ++c) {
@@ -492,46 +458,13 @@ __global__ void __launch_bounds__(kAttnThreads)
     const int slot = c & 1, cs = t0 + c * kChunk, rows = min(kChunk, t1 - cs);
     const __nv_bfloat16* ks = reinterpret_cast<const __nv_bfloat16*>(sm + (size_t)slot * kSlotBytes);
     const __nv_bfloat16* vs = ks + (size_t)kChunk * kHeadDim;
-    const bool fresh_here = owner && p >= cs && p < cs + rows;  // this step's row (CTA-uniform)
-    if (fresh_here && warp == REP) {
-      if (TC) {  // dims 4 lane .. +3: piece lane / 2 (swizzled), byte 8 (lane & 1) within it
-        const uint32_t off = attn_swz<kChunk>(p - cs, lane >> 1) + 8 * (lane & 1);
-        *reinterpret_cast<uint2*>(reinterpret_cast<uint8_t*>(const_cast<__nv_bfloat16*>(ks)) + off) = krow;
-        *reinterpret_cast<uint2*>(reinterpret_cast<uint8_t*>(const_cast<__nv_bfloat16*>(vs)) + off) = vrow;
-      } else {
+    if (owner && p >= cs && p < cs + rows) {  // the chunk holding this step's row (CTA-uniform)
+      if (warp == REP) {
         *reinterpret_cast<uint2*>(const_cast<__nv_bfloat16*>(ks) + (size_t)(p - cs) * kHeadDim + 4 * lane) = krow;
         *reinterpret_cast<uint2*>(const_cast<__nv_bfloat16*>(vs) + (size_t)(p - cs) * kHeadDim + 4 * lane) = vrow;
       }
+      __syncthreads();
     }
-    // TC: a short last chunk's box rows past `rows` hold other cache rows (or the fill): the V
-    // rows meet zero weights in P V, so make them zero (whole 128-byte rows: swizzle-agnostic)
-    const bool pad_v = TC && rows < kChunk;
-    if (pad_v) {
-      uint8_t* vb = reinterpret_cast<uint8_t*>(const_cast<__nv_bfloat16*>(vs));
-      for (int i = tid; i < 2 * (kChunk - rows) * 8; i += kAttnThreads) {
-        const int box = i / ((kChunk - rows) * 8), rem = i - box * (kChunk - rows) * 8;
-        *reinterpret_cast<uint4*>(vb + (size_t)box * kChunk * 128 + (size_t)(rows + rem / 8) * 128 + (rem & 7) * 16) =
-            make_uint4(0, 0, 0, 0);
-      }
-    }
-    if (fresh_here || pad_v) __syncthreads();
-    if (TC) {  // logits on the tensor cores: warp w takes 8-token n-tiles w, w + 8, ...
-      const uint32_t kb = attn_smem_u32(ks);
-      for (int j = warp; j * 8 < rows; j += kAttnThreads / 32) {
-        float sacc[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-          uint32_t b0, b1;
-          attn_ldsm_x2(b0, b1, kb + attn_swz<kChunk>(8 * j + (lane & 7), 2 * kk + ((lane >> 3) & 1)));
-          attn_mma(sacc, qa[kk][0], qa[kk][1], b0, b1);
-        }
-        const int t = 8 * j + 2 * t4;
-        if (hrow) {
-          if (t < rows) pr[t][g] = sacc[0] * kScale;
-          if (t + 1 < rows) pr[t + 1][g] = sacc[1] * kScale;
-        }
-      }
-    } else {
     // logits: item = ((t * REP) + h) * 4 + quarter; four consecutive lanes share (t, h)
     const int items = rows * REP * 4;
     for (int base = 0; base < items; base += kAttnThreads) {
@@ -561,7 +494,6 @@ __global__ void __launch_bounds__(kAttnThreads)
       v += __shfl_xor_sync(0xffffffffu, v, 2);
       if (item < items && qt == 0) pr[t][h] = v * kScale;
     }
-    }
     __syncthreads();
     // online softmax: warp h owns query head h
     if (warp < REP) {
@@ -585,33 +517,7 @@ __global__ void __launch_bounds__(kAttnThreads)
       }
     }
     __syncthreads();
-    if (TC) {  // O += P V: warp w owns dims 16 w .. 16 w + 15 (two n-tiles) of every head
-      const float sc = hrow ? scale[g] : 0.f;
-#pragma unroll
-      for (int jd = 0; jd < 2; ++jd)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) o[jd][e] *= sc;
-      const uint32_t vb = attn_smem_u32(vs);
-      for (int kk = 0; kk * 16 < rows; ++kk) {
-        const int t = 16 * kk + 2 * t4;
-        float p4[4] = {0.f, 0.f, 0.f, 0.f};  // P[g][t], [t + 1], [t + 8], [t + 9]; zero past the chunk
-        if (hrow) {
-          if (t < rows) p4[0] = pr[t][g];
-          if (t + 1 < rows) p4[1] = pr[t + 1][g];
-          if (t + 8 < rows) p4[2] = pr[t + 8][g];
-          if (t + 9 < rows) p4[3] = pr[t + 9][g];
-        }
-        const uint32_t h0 = attn_pack(p4[0], p4[1]), h2 = attn_pack(p4[2], p4[3]);
-        const uint32_t l0 = attn_pack(p4[0] - bf16_lo(h0), p4[1] - bf16_hi(h0));
-        const uint32_t l2 = attn_pack(p4[2] - bf16_lo(h2), p4[3] - bf16_hi(h2));
-        uint32_t bv[4];
-        attn_ldsm_x4_t(bv, vb + attn_swz<kChunk>(16 * kk + (lane & 7) + 8 * ((lane >> 3) & 1), 2 * warp + (lane >> 4)));
-        attn_mma(o[0], h0, h2, bv[0], bv[1]);
-        attn_mma(o[1], h0, h2, bv[2], bv[3]);
-        attn_mma(o[0], l0, l2, bv[0], bv[1]);
-        attn_mma(o[1], l0, l2, bv[2], bv[3]);
-      }
-    } else {
+    {
       float scl[REP];
 #pragma unroll
       for (int h = 0; h < REP; ++h) scl[h] = scale[h];
@@ -639,28 +545,323 @@ __global__ void __launch_bounds__(kAttnThreads)
     }
     __syncthreads();
   }
-  // sum the token groups (TC: every warp's dim slices are complete), push each 16-dim slice
-  // to its owner rank's inbox
-  if (TC) {
-    if (hrow) {
+  // sum the token groups, push each 16-dim slice to its owner rank's inbox
 #pragma unroll
-      for (int jd = 0; jd < 2; ++jd)
-        *reinterpret_cast<float2*>(&red[0][g][16 * warp + 8 * jd + 2 * t4]) = make_float2(o[jd][0], o[jd][1]);
+  for (int h = 0; h < REP; ++h) *reinterpret_cast<float2*>(&red[tg][h][2 * dp]) = make_float2(acc[h][0], acc[h][1]);
+  __syncthreads();
+  for (int item = tid; item < REP * kHeadDim; item += kAttnThreads) {
+    const int h = item / kHeadDim, d = item - h * kHeadDim;
+    float o = 0.f;
+#pragma unroll
+    for (int g = 0; g < kTokenGroups; ++g) o += red[g][h][d];
+    *cluster.map_shared_rank(&inbox[rank][h][d & 15], d >> 4) = o;
+  }
+  if (tid < REP * kClusterCtas) {
+    const int h = tid % REP, dst = tid / REP;
+    *cluster.map_shared_rank(&minbox[rank][h], dst) = m_run[h];
+    *cluster.map_shared_rank(&linbox[rank][h], dst) = l_run[h];
+  }
+  cluster.sync();  // publishes every push; afterwards only local shared memory is read
+  if (tid < REP * 16) {
+    const int h = tid >> 4, dd = tid & 15;
+    float M = -INFINITY;
+#pragma unroll
+    for (int r = 0; r < kClusterCtas; ++r) M = fmaxf(M, minbox[r][h]);
+    float S = 0.f, O = 0.f;
+#pragma unroll
+    for (int r = 0; r < kClusterCtas; ++r) {
+      const float mr = minbox[r][h];
+      const float w = mr == -INFINITY ? 0.f : expf(mr - M);
+      S = fmaf(w, linbox[r][h], S);
+      O = fmaf(w, inbox[r][h][dd], O);
     }
-  } else {
+    a.out[(size_t)b * a.nq * kHeadDim + (kh * REP + h) * kHeadDim + 16 * rank + dd] = to_bf16(O / S);
+  }
+}
+
+// ----------------------------------------------------------------------------
+// Warp-split tensor-core decode attention (default): the same cluster, copies, QK-norm / RoPE
+// and distributed-shared-memory merge as attention_cluster, but inside a CTA every warp keeps
+// its own online softmax over 16-token sub-blocks of each chunk (sub-block i of a chunk goes to
+// warp i mod 8): S = Q K^T for its 16 tokens (2 n-tiles x 8 k-steps of mma.sync with the query
+// heads as zero-padded A rows), the max / exp / sum over its lane quad, P straight from the S
+// accumulator registers into the A fragments of O += P V (P as bf16 hi + lo), O for all 128
+// dims in registers. No CTA barrier per chunk: each warp releases a slot through an mbarrier
+// ("empty", one arrival per warp) and the last warp refills it; the warps' (m, l, O) are
+// merged once at the end, then the cluster merge as before. K and V chunks arrive as four TMA
+// tensor boxes with the 128-byte swizzle (attn_swz), so every ldmatrix is conflict-free.
+constexpr int kWsWarps = kAttnThreads / 32;
+
+template <int REP, int kChunk>
+__global__ void __launch_bounds__(kAttnThreads, 2)
+    attention_ws(AttnArgs a, const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap) {
+  extern __shared__ __align__(128) uint8_t sm_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(sm_raw) + 1023) & ~uintptr_t(1023));
+  constexpr int kQStride = 36;  // floats per 32-dim quarter of q (+4 pad)
+  constexpr size_t kSlotBytes = (size_t)kChunk * kHeadDim * 2 * 2;
+  __shared__ __align__(16) float qs[REP * 4 * kQStride];
+  __shared__ __align__(16) float wo[kWsWarps][REP][kHeadDim];  // each warp's unnormalised O
+  __shared__ float wm[kWsWarps][REP], wl[kWsWarps][REP];
+  __shared__ __align__(16) float inbox[kClusterCtas][REP][16];
+  __shared__ float minbox[kClusterCtas][REP], linbox[kClusterCtas][REP];
+  __shared__ float m_run[REP], l_run[REP];
+  __shared__ __align__(8) uint64_t full[2];
+  __shared__ __align__(8) uint64_t empty[2];
+  __shared__ int failed;
+  __shared__ int issued;  // chunks whose copies were issued (drained on failure)
+  cg::cluster_group cluster = cg::this_cluster();
+  const int rank = (int)cluster.block_rank();
+  const int kh = blockIdx.x / kClusterCtas, b = blockIdx.z;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int qkv_w = (a.nq + 2 * a.nkv) * kHeadDim;
+
+  int64_t pos = a.positions[b];
+  const bool bad_pos = pos < 0 || pos >= a.max_len;
+  if (bad_pos) pos = pos < 0 ? 0 : a.max_len - 1;
+  const int p = (int)pos, len = p + 1;
+  const int span = (len + kClusterCtas - 1) / kClusterCtas;
+  const int t0 = rank * span, t1 = min(t0 + span, len);
+  const int n = t1 > t0 ? t1 - t0 : 0;
+  const int chunks = (n + kChunk - 1) / kChunk;
+  const size_t kv_base = ((size_t)b * a.nkv + kh) * a.max_len * kHeadDim;
+  const bool owner = t0 <= p && p < t1;
+
+  auto issue = [&](int c) {  // one thread: four boxes of 64 dims x kChunk rows
+    const int slot = c & 1, cs = t0 + c * kChunk;
+    const int y = (int)(((size_t)b * a.nkv + kh) * a.max_len) + cs;
+    uint8_t* dst = sm + (size_t)slot * kSlotBytes;
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(attn_smem_u32(&full[slot])),
+                 "r"((unsigned)(4 * kChunk * 128)) : "memory");
 #pragma unroll
-    for (int h = 0; h < REP; ++h) *reinterpret_cast<float2*>(&red[tg][h][2 * dp]) = make_float2(acc[h][0], acc[h][1]);
+    for (int q = 0; q < 4; ++q) {
+      const CUtensorMap* map = q < 2 ? &kmap : &vmap;
+      asm volatile(
+          "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+              attn_smem_u32(dst + (size_t)q * kChunk * 128)),
+          "l"(reinterpret_cast<uint64_t>(map)), "r"((q & 1) * 64), "r"(y), "r"(attn_smem_u32(&full[slot]))
+          : "memory");
+    }
+  };
+  auto wait_bar = [&](uint64_t* bar, unsigned parity) -> bool {
+    for (long it = 0; it < (1L << 22); ++it) {
+      uint32_t done;
+      asm volatile("{\n .reg .pred q;\n mbarrier.try_wait.parity.shared::cta.b64 q, [%1], %2;\n selp.u32 %0, 1, 0, q;\n}"
+                   : "=r"(done) : "r"(attn_smem_u32(bar)), "r"(parity) : "memory");
+      if (done) return true;
+    }
+    return false;
+  };
+
+  if (tid == 0) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(attn_smem_u32(&full[0])) : "memory");
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(attn_smem_u32(&full[1])) : "memory");
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(attn_smem_u32(&empty[0])), "r"(kWsWarps) : "memory");
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(attn_smem_u32(&empty[1])), "r"(kWsWarps) : "memory");
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    failed = 0;
+    issued = min(2, chunks);
+    // rows before `position` were written by earlier steps: fetch before the wait
+    for (int c = 0; c < 2 && c < chunks; ++c) issue(c);
+  }
+  // Inputs that do not depend on the previous kernel: this row's RoPE factors and the
+  // head-norm weights, for warps that rotate a head (q heads: warps < REP; k: warp REP).
+  const bool rotates = warp < REP || (warp == REP && owner);
+  uint2 cw = make_uint2(0, 0), sw = make_uint2(0, 0), nw = make_uint2(0, 0);
+  if (rotates) {
+    cw = *reinterpret_cast<const uint2*>(a.cos_tab + (size_t)p * kHeadDim + 4 * lane);
+    sw = *reinterpret_cast<const uint2*>(a.sin_tab + (size_t)p * kHeadDim + 4 * lane);
+    nw = *reinterpret_cast<const uint2*>((warp < REP ? a.q_norm : a.k_norm) + 4 * lane);
+  }
+  __syncthreads();
+  pdl_wait();
+  pdl_trigger();
+  if (bad_pos && a.status && tid == 0 && rank == 0) atomicExch(a.status, 1);
+  const __nv_bfloat16* src = a.qkv + (size_t)b * qkv_w;
+
+  // Head RMSNorm + rotate-half RoPE (kernels.py:158-163); q rounded to bf16 as the reference
+  // stores it (kernels.py:165); the new K / V row goes to the cache (and, below, to the chunk).
+  uint2 krow = make_uint2(0, 0), vrow = make_uint2(0, 0);
+  if (rotates) {
+    const int row = warp < REP ? kh * REP + warp : a.nq + kh;
+    const uint2 r = *reinterpret_cast<const uint2*>(src + (size_t)row * kHeadDim + 4 * lane);
+    if (warp == REP) vrow = *reinterpret_cast<const uint2*>(src + (size_t)(a.nq + a.nkv + kh) * kHeadDim + 4 * lane);
+    float x[4] = {bf16_lo(r.x), bf16_hi(r.x), bf16_lo(r.y), bf16_hi(r.y)};
+    const float wv[4] = {bf16_lo(nw.x), bf16_hi(nw.x), bf16_lo(nw.y), bf16_hi(nw.y)};
+    const float cv[4] = {bf16_lo(cw.x), bf16_hi(cw.x), bf16_lo(cw.y), bf16_hi(cw.y)};
+    const float sv[4] = {bf16_lo(sw.x), bf16_hi(sw.x), bf16_lo(sw.y), bf16_hi(sw.y)};
+    float ss = x[0] * x[0] + x[1] * x[1] + x[2] * x[2] + x[3] * x[3];
+    ss = warp_sum(ss);
+    const float inv = 1.0f / sqrtf(ss / 128.f + a.eps);
+    float y[4], part[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) y[i] = round_bf16(round_bf16(x[i] * inv) * wv[i]);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) part[i] = __shfl_xor_sync(0xffffffffu, y[i], 16);  // partner d +- 64
+    const float sign = lane < 16 ? -1.f : 1.f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) x[i] = round_bf16(round_bf16(y[i] * cv[i]) + round_bf16(sign * part[i] * sv[i]));
+    if (warp < REP) {
+      *reinterpret_cast<float4*>(&qs[(warp * 4 + (lane >> 3)) * kQStride + 4 * (lane & 7)]) =
+          make_float4(x[0], x[1], x[2], x[3]);
+    } else {
+      __nv_bfloat162 lo = __floats2bfloat162_rn(x[0], x[1]), hi = __floats2bfloat162_rn(x[2], x[3]);
+      krow.x = *reinterpret_cast<uint32_t*>(&lo);
+      krow.y = *reinterpret_cast<uint32_t*>(&hi);
+      *reinterpret_cast<uint2*>(a.k_cache + kv_base + (size_t)p * kHeadDim + 4 * lane) = krow;
+      *reinterpret_cast<uint2*>(a.v_cache + kv_base + (size_t)p * kHeadDim + 4 * lane) = vrow;
+    }
+  }
+  __syncthreads();
+
+  // lane (g, t4): query head g < REP is A row g; S / P / O fragments hold rows g (and g + 8:
+  // zero A rows, never read)
+  const int g = lane >> 2, t4 = lane & 3;
+  const bool hrow = g < REP;
+  uint32_t qa[8][2];
+#pragma unroll
+  for (int kk = 0; kk < 8; ++kk) {  // dims 16 kk + 2 t4 (+1) and + 8: quarter kk / 2 of qs
+    const float* qrow = &qs[((hrow ? g : 0) * 4 + (kk >> 1)) * kQStride + (kk & 1) * 16 + 2 * t4];
+    qa[kk][0] = hrow ? attn_pack(qrow[0], qrow[1]) : 0u;
+    qa[kk][1] = hrow ? attn_pack(qrow[8], qrow[9]) : 0u;
+  }
+  float o[16][4] = {};
+  float mrow = -INFINITY, lrow = 0.f;  // head g's running max and sum over this warp's tokens
+  constexpr int kSub = kChunk / 16;     // 16-token sub-blocks per chunk
+  volatile int* vfailed = &failed;
+  for (int c = 0; c < chunks; ++c) {
+    const int slot = c & 1, cs = t0 + c * kChunk, rows = min(kChunk, t1 - cs);
+    const bool got = !*vfailed && __all_sync(0xffffffffu, wait_bar(&full[slot], (unsigned)((c >> 1) & 1)));
+    if (!got && lane == 0) *vfailed = 1;
+    uint8_t* kbase = sm + (size_t)slot * kSlotBytes;
+    uint8_t* vbase = kbase + kSlotBytes / 2;
+    // this step's row (the copy may predate its write) and, in a short last chunk, zero V rows
+    // past the end (they meet zero weights); both CTA-uniform, the only barriers in the loop
+    const bool fresh_here = owner && p >= cs && p < cs + rows;
+    const bool pad_v = rows < kChunk;
+    if (fresh_here || pad_v) {
+      if (got) {
+        if (fresh_here && warp == REP) {
+          const uint32_t off = attn_swz<kChunk>(p - cs, lane >> 1) + 8 * (lane & 1);
+          *reinterpret_cast<uint2*>(kbase + off) = krow;
+          *reinterpret_cast<uint2*>(vbase + off) = vrow;
+        }
+        if (pad_v)
+          for (int i = tid; i < 2 * (kChunk - rows) * 8; i += kAttnThreads) {
+            const int box = i / ((kChunk - rows) * 8), rem = i - box * (kChunk - rows) * 8;
+            *reinterpret_cast<uint4*>(vbase + (size_t)box * kChunk * 128 + (size_t)(rows + rem / 8) * 128 +
+                                      (rem & 7) * 16) = make_uint4(0, 0, 0, 0);
+          }
+      }
+      __syncthreads();
+    }
+    if (got) {
+      const uint32_t kb = attn_smem_u32(kbase), vb = attn_smem_u32(vbase);
+      for (int i = warp; i < kSub && 16 * i < rows; i += kWsWarps) {
+        const int tok0 = 16 * i;
+        float s[2][4] = {};
+#pragma unroll
+        for (int jn = 0; jn < 2; ++jn)
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk) {
+            uint32_t b0, b1;
+            attn_ldsm_x2(b0, b1, kb + attn_swz<kChunk>(tok0 + 8 * jn + (lane & 7), 2 * kk + ((lane >> 3) & 1)));
+            attn_mma(s[jn], qa[kk][0], qa[kk][1], b0, b1);
+          }
+        // logits of tokens tok0 + 8 jn + 2 t4 + e (rows past the chunk: -inf), the quad's max
+        float bm = -INFINITY;
+#pragma unroll
+        for (int jn = 0; jn < 2; ++jn)
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const bool live = tok0 + 8 * jn + 2 * t4 + e < rows;
+            s[jn][e] = live ? s[jn][e] * kScale : -INFINITY;
+            bm = fmaxf(bm, s[jn][e]);
+          }
+        bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, 1));
+        bm = fmaxf(bm, __shfl_xor_sync(0xffffffffu, bm, 2));
+        const float mnew = fmaxf(mrow, bm);  // finite: every sub-block holds a live token
+        const float corr = mrow == -INFINITY ? 0.f : expf(mrow - mnew);
+        float pv[2][2], psum = 0.f;
+#pragma unroll
+        for (int jn = 0; jn < 2; ++jn)
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            pv[jn][e] = s[jn][e] == -INFINITY ? 0.f : expf(s[jn][e] - mnew);
+            psum += pv[jn][e];
+          }
+        psum += __shfl_xor_sync(0xffffffffu, psum, 1);
+        psum += __shfl_xor_sync(0xffffffffu, psum, 2);
+        lrow = lrow * corr + psum;
+        mrow = mnew;
+#pragma unroll
+        for (int jd = 0; jd < 16; ++jd) {
+          o[jd][0] *= corr;
+          o[jd][1] *= corr;
+        }
+        // P (k = the sub-block's 16 tokens) as A fragments, bf16 hi + lo; zero for rows g >= REP
+        const uint32_t h0 = hrow ? attn_pack(pv[0][0], pv[0][1]) : 0u, h2 = hrow ? attn_pack(pv[1][0], pv[1][1]) : 0u;
+        const uint32_t l0 = hrow ? attn_pack(pv[0][0] - bf16_lo(h0), pv[0][1] - bf16_hi(h0)) : 0u;
+        const uint32_t l2 = hrow ? attn_pack(pv[1][0] - bf16_lo(h2), pv[1][1] - bf16_hi(h2)) : 0u;
+#pragma unroll
+        for (int jp = 0; jp < 8; ++jp) {  // dims 16 jp .. 16 jp + 15: n-tiles 2 jp, 2 jp + 1
+          uint32_t bv[4];
+          attn_ldsm_x4_t(bv, vb + attn_swz<kChunk>(tok0 + (lane & 7) + 8 * ((lane >> 3) & 1), 2 * jp + (lane >> 4)));
+          attn_mma(o[2 * jp], h0, h2, bv[0], bv[1]);
+          attn_mma(o[2 * jp + 1], h0, h2, bv[2], bv[3]);
+          attn_mma(o[2 * jp], l0, l2, bv[0], bv[1]);
+          attn_mma(o[2 * jp + 1], l0, l2, bv[2], bv[3]);
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(attn_smem_u32(&empty[slot])) : "memory");
+    // the last warp refills this slot with chunk c + 2 once every warp has released it
+    if (warp == kWsWarps - 1 && lane == 0 && c + 2 < chunks && !*vfailed) {
+      if (wait_bar(&empty[slot], (unsigned)((c >> 1) & 1))) {
+        issue(c + 2);
+        issued = c + 3;
+      } else {
+        *vfailed = 1;
+      }
+    }
+  }
+  __syncthreads();
+  if (failed) {  // a copy or a slot release did not come within the bound: drain, flag, merge what there is
+    if (tid == 0) {
+      if (a.status) atomicExch(a.status, 3);
+      // at most the last copy of each slot can still be in flight
+      for (int k = max(0, issued - 2); k < issued; ++k) wait_bar(&full[k & 1], (unsigned)((k >> 1) & 1));
+    }
+    __syncthreads();
+  }
+  // the warps' (m, l, O) -> the CTA's
+  if (hrow && t4 == 0) {
+    wm[warp][g] = mrow;
+    wl[warp][g] = lrow;
+  }
+  if (hrow) {
+#pragma unroll
+    for (int jd = 0; jd < 16; ++jd)
+      *reinterpret_cast<float2*>(&wo[warp][g][8 * jd + 2 * t4]) = make_float2(o[jd][0], o[jd][1]);
+  }
+  __syncthreads();
+  if (tid < REP) {
+    float M = -INFINITY, L = 0.f;
+    for (int w = 0; w < kWsWarps; ++w) M = fmaxf(M, wm[w][tid]);
+    for (int w = 0; w < kWsWarps; ++w) {
+      const float f = wm[w][tid] == -INFINITY ? 0.f : expf(wm[w][tid] - M);
+      wm[w][tid] = f;  // now the warp's weight
+      L = fmaf(f, wl[w][tid], L);
+    }
+    m_run[tid] = M;
+    l_run[tid] = L;
   }
   __syncthreads();
   for (int item = tid; item < REP * kHeadDim; item += kAttnThreads) {
     const int h = item / kHeadDim, d = item - h * kHeadDim;
     float ov = 0.f;
-    if (TC) {
-      ov = red[0][h][d];
-    } else {
 #pragma unroll
-      for (int gg = 0; gg < kTokenGroups; ++gg) ov += red[gg][h][d];
-    }
+    for (int w = 0; w < kWsWarps; ++w) ov = fmaf(wm[w][h], wo[w][h][d], ov);
     *cluster.map_shared_rank(&inbox[rank][h][d & 15], d >> 4) = ov;
   }
   if (tid < REP * kClusterCtas) {
@@ -745,13 +946,23 @@ static cudaError_t launch_cluster_rep(cudaLaunchConfig_t& cfg, const AttnArgs& a
   memset(&kmap, 0, sizeof(kmap));
   memset(&vmap, 0, sizeof(vmap));
   const long long rows = (long long)batch * a.nkv * a.max_len;
-  const bool tc = attention_tc() && rows < (1LL << 31) && cache_map(&kmap, a.k_cache, rows, CH) &&
+  const bool tc = CH >= 64 && attention_tc() && rows < (1LL << 31) && cache_map(&kmap, a.k_cache, rows, CH) &&
                   cache_map(&vmap, a.v_cache, rows, CH);
-  cfg.dynamicSmemBytes = 2 * (size_t)CH * kHeadDim * 2 * 2 + (tc ? 1024 : 0);
-  auto kern = tc ? attention_cluster<REP, CH, true> : attention_cluster<REP, CH, false>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)cfg.dynamicSmemBytes);
+  cudaError_t e;
+  if constexpr (CH >= 64) {
+    if (tc) {
+      cfg.dynamicSmemBytes = 2 * (size_t)CH * kHeadDim * 2 * 2 + 1024;
+      e = cudaFuncSetAttribute(attention_ws<REP, CH>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               (int)cfg.dynamicSmemBytes);
+      if (e != cudaSuccess) return e;
+      return cudaLaunchKernelEx(&cfg, attention_ws<REP, CH>, a, kmap, vmap);
+    }
+  }
+  cfg.dynamicSmemBytes = 2 * (size_t)CH * kHeadDim * 2 * 2;
+  e = cudaFuncSetAttribute(attention_cluster<REP, CH>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)cfg.dynamicSmemBytes);
   if (e != cudaSuccess) return e;
-  return cudaLaunchKernelEx(&cfg, kern, a, kmap, vmap);
+  return cudaLaunchKernelEx(&cfg, attention_cluster<REP, CH>, a);
 }
 
 // Chunk size of the cluster kernel: MT_ATTN_CHUNK (32, 64 or 128) overrides the default:
@@ -768,6 +979,7 @@ static int attention_chunk(int batch, int nkv) {
   }
   if (forced) return forced;
   if (batch == 1) return 128;
+  if (attention_tc()) return 64;  // the tensor-core kernel: 4 sub-blocks of 16 tokens per chunk
   return (long long)batch * nkv * kClusterCtas <= 3LL * sm_count() ? 64 : 32;
 }
 
