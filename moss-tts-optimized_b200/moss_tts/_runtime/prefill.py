@@ -81,6 +81,10 @@ class Prefill:
             for p, paired in ((lw.qkv, False), (lw.out, False), (lw.gate_up, True), (lw.down, False)):
                 ws = max(ws, native.w4a16_gemm_workspace(GEMM_ROWS, p.n, p.k, native.LINEAR_PAIRED if paired else 0))
         self.workspace = torch.zeros(ws, device=dev, dtype=torch.uint8)
+        # one CUDA graph per prompt length (the launches depend on n), captured after the first
+        # eager pass of that length (as the reference captures its prefill buckets, llm.py:204-226)
+        self.graphs = {}
+        self.max_graphs = 8
 
     def _gemm(self, p, x, y, n, paired=False):
         s = torch.cuda.current_stream(self.eng.device).cuda_stream
@@ -116,6 +120,30 @@ class Prefill:
         if not 1 <= n <= self.max_tokens or n >= eng.max_length:
             raise ValueError("Batch must be one and prompt must fit the KV capacity")
         self.ids[:n].copy_(ids[0])
+        g = self.graphs.get(n)
+        if g is not None:
+            g.replay()
+            return self.text_logits, self.audio_logits
+        if self.mode == "w4" or len(self.graphs) >= self.max_graphs:
+            self._launch(n)
+            return self.text_logits, self.audio_logits
+        # an eager pass on a side stream (it makes the bf16 copies and the GEMM library's state on
+        # that stream, and gives this call's result), then the same launches captured there
+        cur = torch.cuda.current_stream(eng.device)
+        stream = torch.cuda.Stream(eng.device)
+        stream.wait_stream(cur)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(stream):
+            self._launch(n)
+            with torch.cuda.graph(graph, stream=stream):
+                self._launch(n)
+        cur.wait_stream(stream)
+        self.graphs[n] = graph
+        return self.text_logits, self.audio_logits
+
+    def _launch(self, n: int) -> None:
+        """Enqueue the prompt pass over ``self.ids[:n]`` on the current stream."""
+        eng, cfg, w = self.eng, self.cfg, self.eng.w
         s = torch.cuda.current_stream(eng.device).cuda_stream
         eps = float(cfg.rms_norm_eps)
         h, d = cfg.hidden_size, cfg.head_dim
@@ -153,4 +181,3 @@ class Prefill:
                     self.text_logits.data_ptr(), 1, w.head_text.shape[0], h, 0, 0, s)
         native.call("mt_bf16_linear", self.hidden.data_ptr(), None, None, 0.0, None, w.head_audio.data_ptr(),
                     self.audio_logits.data_ptr(), 1, w.head_audio.shape[0], h, 0, 0, s)
-        return self.text_logits, self.audio_logits

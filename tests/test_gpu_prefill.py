@@ -77,6 +77,10 @@ def test_prefill_long_prompt_matches_oracle_and_decode_continues(two_layer, cuda
     llm = FastLLM(w, max_length=384, greedy=True)
     llm.prefill_mode = mode
     text, audio = llm.prefill(torch.from_numpy(ids))
+    text, audio = text.clone(), audio.clone()
+    # a second prompt of this length replays the captured graph: the same bits
+    again = llm.prefill(torch.from_numpy(ids))
+    assert torch.equal(again[0], text) and torch.equal(again[1], audio)
     ref = omodel.Decoder(host, dc.as_dict(), max_length=384)
     rtext, raudio, _ = ref.prefill(ids[0])
     for label, got, want in (("long prefill text logits", text, rtext), ("long prefill audio logits", audio, raudio)):
