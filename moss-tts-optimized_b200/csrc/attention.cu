@@ -588,11 +588,12 @@ __global__ void __launch_bounds__(kAttnThreads) attention_cluster(AttnArgs a) {
 // accumulator registers into the A fragments of O += P V (P as bf16 hi + lo), O for all 128
 // dims in registers. No CTA barrier per chunk: each warp releases a slot through an mbarrier
 // ("empty", one arrival per warp) and the last warp refills it; the warps' (m, l, O) are
-// merged once at the end, then the cluster merge as before. K and V chunks arrive as four TMA
+// merged once at the end, then the cluster merge as before over CL = 8, 4 or 2 CTAs per KV
+// head (fewer for large batches: longer spans per CTA). K and V chunks arrive as four TMA
 // tensor boxes with the 128-byte swizzle (attn_swz), so every ldmatrix is conflict-free.
 constexpr int kWsWarps = kAttnThreads / 32;
 
-template <int REP, int kChunk>
+template <int REP, int kChunk, int CL>
 __global__ void __launch_bounds__(kAttnThreads, 2)
     attention_ws(AttnArgs a, const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap) {
   extern __shared__ __align__(128) uint8_t sm_raw[];
@@ -602,8 +603,9 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
   __shared__ __align__(16) float qs[REP * 4 * kQStride];
   __shared__ __align__(16) float wo[kWsWarps][REP][kHeadDim];  // each warp's unnormalised O
   __shared__ float wm[kWsWarps][REP], wl[kWsWarps][REP];
-  __shared__ __align__(16) float inbox[kClusterCtas][REP][16];
-  __shared__ float minbox[kClusterCtas][REP], linbox[kClusterCtas][REP];
+  constexpr int kSl = kHeadDim / CL;  // output dims each rank finishes
+  __shared__ __align__(16) float inbox[CL][REP][kSl];
+  __shared__ float minbox[CL][REP], linbox[CL][REP];
   __shared__ float m_run[REP], l_run[REP];
   __shared__ __align__(8) uint64_t full[2];
   __shared__ __align__(8) uint64_t empty[2];
@@ -611,7 +613,7 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
   __shared__ int issued;  // chunks whose copies were issued (drained on failure)
   cg::cluster_group cluster = cg::this_cluster();
   const int rank = (int)cluster.block_rank();
-  const int kh = blockIdx.x / kClusterCtas, b = blockIdx.z;
+  const int kh = blockIdx.x / CL, b = blockIdx.z;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int qkv_w = (a.nq + 2 * a.nkv) * kHeadDim;
 
@@ -619,7 +621,7 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
   const bool bad_pos = pos < 0 || pos >= a.max_len;
   if (bad_pos) pos = pos < 0 ? 0 : a.max_len - 1;
   const int p = (int)pos, len = p + 1;
-  const int span = (len + kClusterCtas - 1) / kClusterCtas;
+  const int span = (len + CL - 1) / CL;
   const int t0 = rank * span, t1 = min(t0 + span, len);
   const int n = t1 > t0 ? t1 - t0 : 0;
   const int chunks = (n + kChunk - 1) / kChunk;
@@ -862,28 +864,28 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
     float ov = 0.f;
 #pragma unroll
     for (int w = 0; w < kWsWarps; ++w) ov = fmaf(wm[w][h], wo[w][h][d], ov);
-    *cluster.map_shared_rank(&inbox[rank][h][d & 15], d >> 4) = ov;
+    *cluster.map_shared_rank(&inbox[rank][h][d % kSl], d / kSl) = ov;
   }
-  if (tid < REP * kClusterCtas) {
+  if (tid < REP * CL) {
     const int h = tid % REP, dst = tid / REP;
     *cluster.map_shared_rank(&minbox[rank][h], dst) = m_run[h];
     *cluster.map_shared_rank(&linbox[rank][h], dst) = l_run[h];
   }
   cluster.sync();  // publishes every push; afterwards only local shared memory is read
-  if (tid < REP * 16) {
-    const int h = tid >> 4, dd = tid & 15;
+  for (int item = tid; item < REP * kSl; item += kAttnThreads) {
+    const int h = item / kSl, dd = item % kSl;
     float M = -INFINITY;
 #pragma unroll
-    for (int r = 0; r < kClusterCtas; ++r) M = fmaxf(M, minbox[r][h]);
+    for (int r = 0; r < CL; ++r) M = fmaxf(M, minbox[r][h]);
     float S = 0.f, O = 0.f;
 #pragma unroll
-    for (int r = 0; r < kClusterCtas; ++r) {
+    for (int r = 0; r < CL; ++r) {
       const float mr = minbox[r][h];
       const float w = mr == -INFINITY ? 0.f : expf(mr - M);
       S = fmaf(w, linbox[r][h], S);
       O = fmaf(w, inbox[r][h][dd], O);
     }
-    a.out[(size_t)b * a.nq * kHeadDim + (kh * REP + h) * kHeadDim + 16 * rank + dd] = to_bf16(O / S);
+    a.out[(size_t)b * a.nq * kHeadDim + (kh * REP + h) * kHeadDim + kSl * rank + dd] = to_bf16(O / S);
   }
 }
 
@@ -951,11 +953,25 @@ static cudaError_t launch_cluster_rep(cudaLaunchConfig_t& cfg, const AttnArgs& a
   cudaError_t e;
   if constexpr (CH >= 64) {
     if (tc) {
+      // CTAs per KV head: the fewest of 8, 4, 2 that still put at least 1.5 CTAs on every SM
+      // (longer spans per CTA amortise its fixed cost; fewer CTAs leave SMs idle). Measured at
+      // 32 x 2048: 8 -> 85.5 us, 4 -> 63.7, 2 -> 55.6; at 4 x 2048: 8 -> 14.2, 4 -> 16.5.
+      // MT_ATTN_CLUSTER = 2, 4 or 8 overrides.
+      static int forced = -1;
+      if (forced < 0) {
+        const char* env = getenv("MT_ATTN_CLUSTER");
+        forced = (env && (env[0] == '2' || env[0] == '4' || env[0] == '8') && env[1] == 0) ? env[0] - '0' : 0;
+      }
+      int cl = forced ? forced : 8;
+      if (!forced)
+        while (cl > 2 && 2LL * batch * a.nkv * (cl / 2) >= 3LL * sm_count()) cl /= 2;
+      cfg.gridDim.x = (unsigned)(cl * a.nkv);
+      cfg.attrs[0].val.clusterDim.x = (unsigned)cl;
       cfg.dynamicSmemBytes = 2 * (size_t)CH * kHeadDim * 2 * 2 + 1024;
-      e = cudaFuncSetAttribute(attention_ws<REP, CH>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               (int)cfg.dynamicSmemBytes);
+      auto kern = cl == 2 ? attention_ws<REP, CH, 2> : cl == 4 ? attention_ws<REP, CH, 4> : attention_ws<REP, CH, 8>;
+      e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)cfg.dynamicSmemBytes);
       if (e != cudaSuccess) return e;
-      return cudaLaunchKernelEx(&cfg, attention_ws<REP, CH>, a, kmap, vmap);
+      return cudaLaunchKernelEx(&cfg, kern, a, kmap, vmap);
     }
   }
   cfg.dynamicSmemBytes = 2 * (size_t)CH * kHeadDim * 2 * 2;
