@@ -383,32 +383,53 @@ def config0(args):
 
 
 def profile_gemm(rows: int):
-    """The batched projection alone: mt_w4a16_gemm on gate/up (N = 24576, K = 4096, fused pair)
-    with `rows` activation rows, random codes / scales / zero points, 4 launches."""
+    """The batched projection alone: the tcgen05 GEMM on gate/up (N = 24576, K = 4096, fused
+    pair) with `rows` activation rows, random codes / scales / zero points, in both weight
+    layouts (GPTQ: mt_w4a16_gemm; packed: mt_w4a16_gemm_packed, what the batched engine runs).
+    Three weight sets are rotated (175 MB per layout, more than the 126 MB L2), so every launch
+    streams its weights from HBM; CUDA events over 6 launches after 3."""
     import torch
 
     from moss_tts._runtime import native
 
     dev = torch.device("cuda", 0)
     g = torch.Generator(device=dev).manual_seed(0)
-    n, k = 24576, 4096
-    qw = torch.randint(0, 256, (n, k // 2), dtype=torch.uint8, device=dev, generator=g)
-    sc = (torch.rand(n, k // 32, device=dev, generator=g) * 0.01 + 1e-4).to(torch.bfloat16)
-    qz = torch.randint(0, 256, (n, k // 64), dtype=torch.uint8, device=dev, generator=g)
+    n, k, sets = 24576, 4096, 3
+    peak, peak_kind = measured_peaks()
+    qw = [torch.randint(0, 256, (n, k // 2), dtype=torch.uint8, device=dev, generator=g) for _ in range(sets)]
+    sc = [(torch.rand(n, k // 32, device=dev, generator=g) * 0.01 + 1e-4).to(torch.bfloat16) for _ in range(sets)]
+    qz = [torch.randint(0, 256, (n, k // 64), dtype=torch.uint8, device=dev, generator=g) for _ in range(sets)]
+    s = torch.cuda.current_stream(dev).cuda_stream
+    pk_bytes = native.w4a16_gemm_pack_size(n, k, native.LINEAR_PAIRED)
+    pk = [torch.empty(pk_bytes, dtype=torch.uint8, device=dev) for _ in range(sets)]
+    for i in range(sets):
+        native.call("mt_w4a16_gemm_pack", qw[i].data_ptr(), sc[i].data_ptr(), qz[i].data_ptr(), n, k,
+                    native.LINEAR_PAIRED, pk[i].data_ptr(), s)
     x = torch.randn(rows, k, device=dev, generator=g).to(torch.bfloat16)
     y = torch.empty(rows, n // 2, device=dev, dtype=torch.bfloat16)
     ws = torch.zeros(native.w4a16_gemm_workspace(rows, n, k, native.LINEAR_PAIRED), dtype=torch.uint8, device=dev)
-    s = torch.cuda.current_stream(dev).cuda_stream
+    weight_bytes = n * k // 2 + n * k // 32 * 2 + n * k // 64  # codes, scales, zero points
+    flops = 2.0 * rows * n * k
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    for i in range(4):
-        if i == 2:
-            e0.record()
-        native.call("mt_w4a16_gemm", x.data_ptr(), qw.data_ptr(), sc.data_ptr(), qz.data_ptr(), y.data_ptr(), rows,
-                    n, k, native.LINEAR_PAIRED, ws.data_ptr(), 0, s)
-    e1.record()
-    torch.cuda.synchronize(dev)
-    print(json.dumps({"kernel": "mt_w4a16_gemm gate/up", "rows": rows, "launch_us": round(e0.elapsed_time(e1) * 500, 2),
-                      "error_word": native.error_word(clear=True)}), flush=True)
+    for layout in ("gptq", "packed"):
+        for i in range(9):
+            if i == 3:
+                e0.record()
+            j = i % sets
+            if layout == "gptq":
+                native.call("mt_w4a16_gemm", x.data_ptr(), qw[j].data_ptr(), sc[j].data_ptr(), qz[j].data_ptr(),
+                            y.data_ptr(), rows, n, k, native.LINEAR_PAIRED, ws.data_ptr(), 0, s)
+            else:
+                native.call("mt_w4a16_gemm_packed", x.data_ptr(), pk[j].data_ptr(), y.data_ptr(), rows, n, k,
+                            native.LINEAR_PAIRED, ws.data_ptr(), 0, s)
+        e1.record()
+        torch.cuda.synchronize(dev)
+        us = e0.elapsed_time(e1) * 1000 / 6
+        print(json.dumps({"kernel": f"tcgen05 gate/up GEMM ({layout} layout)", "rows": rows, "launch_us": round(us, 2),
+                          "weight_gbs": round(weight_bytes / us / 1e3, 1),
+                          "frac_hbm": round(weight_bytes / us / 1e3 / peak, 4), "tflops": round(flops / us / 1e6, 1),
+                          "peak_gbs": peak, "peak_kind": peak_kind, "error_word": native.error_word(clear=True)}),
+              flush=True)
 
 
 def batch_sweep(args, rank, world, local):

@@ -11,11 +11,14 @@
 // * A tile is 128 weight rows (the 128 TMEM lanes). One persistent CTA per SM owns a
 //   balanced contiguous range of the (tile, 256-wide K chunk) work list, so every SM streams
 //   the same number of weight bytes; a range cuts at most two tiles (its first and last).
-// * Two loader warps fill a ring of up to eight shared-memory stages with TMA tensor loads:
-//   the chunk's 4-bit codes (128 rows x 128 bytes, 128-byte swizzle) and the activation chunk
-//   (B x 256 bf16 in four 64-column boxes with the 128-byte swizzle: the canonical K-major
-//   SWIZZLE_128B operand layout; rows past B read as zeros). The code loads do not depend
-//   on the previous kernel and start before griddepcontrol.wait.
+// * Two loader warps fill two shared-memory rings with TMA loads: the code ring holds the
+//   chunk's 4-bit codes (128 rows x 128 bytes, 128-byte swizzle), scales and zero points and
+//   is released by the dequantisation group as soon as it has read them; the activation ring
+//   holds the activation chunk (B x 256 bf16 in four 64-column boxes with the 128-byte
+//   swizzle: the canonical K-major SWIZZLE_128B operand layout; rows past B read as zeros) and
+//   is released by the MMAs. Separate rings keep up to eight code chunks in flight even when
+//   the activation chunks are large (32 KB at B = 64). The code loads do not depend on the
+//   previous kernel and start before griddepcontrol.wait.
 // * The dequantised weights never touch shared memory: sixteen dequantisation warps in two
 //   groups taking alternate chunks (so one group computes while the other waits; in a group
 //   warp w owns TMEM lanes 32 (w % 4) .. +31, one weight row per thread, and one half of the
@@ -23,11 +26,15 @@
 //   scales and zero points from L1-cached loads issued three chunks ahead, turn each code pair
 //   into an exact bf16 pair (bf16(128 + q) by bit insertion, minus bf16(128 + z) exactly,
 //   times the bf16 scale with one round to nearest: the oracle's bf16((q - z) * s) bit for
-//   bit) and store them into one of two or three TMEM slots with tcgen05.st.
-// * One thread issues tcgen05.mma.kind::f16 with A in TMEM and B in shared memory into one
-//   of two fp32 accumulators D[128, B] in TMEM (alternating per tile segment); tcgen05.commit
-//   frees a stage of the four-deep ring and hands a finished accumulator to four epilogue
-//   warps, which read it with tcgen05.ld while the next segment accumulates.
+//   bit) and store them into one of two or three TMEM slots with tcgen05.st; each K half of a
+//   slot has its own full / empty barrier pair, so the two MMA warps run independently.
+// * Two MMA warps issue tcgen05.mma.kind::f16 with A in TMEM and B in shared memory: warp i
+//   the 8 K steps of half i of every chunk, into its own fp32 accumulator D_i[128, B] in TMEM
+//   (one thread issues at most one MMA per ~70 cycles whatever N, so a single issuer paced
+//   the kernel at small batches). Up to 32 batch columns each warp double-buffers its
+//   accumulator per tile segment. tcgen05.commit frees the TMEM slot half and the activation
+//   stage and hands finished accumulators to four epilogue warps, which read D_0 + D_1 with
+//   tcgen05.ld.
 // * A tile cut between CTAs is finished by the last contributor (ticket), which sums the
 //   contributions in CTA order, so results are deterministic.
 // Every mbarrier wait is bounded; an expired wait sets an error word and the kernel still
@@ -49,13 +56,14 @@ using namespace pipe;
 constexpr int kTileM = 128;        // weight rows per tile = TMEM lanes
 constexpr int kChunk = 256;        // K elements per pipeline stage
 constexpr int kMaxSlots = 3;       // TMEM A slots (3 when the batch fits 64 columns, else 2)
-constexpr int kMaxStages = 8;      // shared-memory stages (codes + activations) in flight
+constexpr int kMaxStages = 8;      // shared-memory stages per ring (codes; activations)
 constexpr int kDequantWarps = 16;  // two groups of 8 (alternate chunks); lane quarter w % 4, K half (w / 4) % 2
-constexpr int kMmaWarp = 16;
-constexpr int kEpiWarp0 = 17;      // warps 17..20 read the accumulators
-constexpr int kCodeWarp = 21;      // TMA loads of the 4-bit codes
-constexpr int kActWarp = 22;       // TMA loads of the activation chunks
-constexpr int kThreads = 23 * 32;
+constexpr int kMmaWarp = 16;       // warps 16 and 17 issue the MMAs of K halves 0 and 1
+constexpr int kMmaWarps = 2;
+constexpr int kEpiWarp0 = 18;      // warps 18..21 read the accumulators
+constexpr int kCodeWarp = 22;      // TMA loads of the 4-bit codes
+constexpr int kActWarp = 23;       // TMA loads of the activation chunks
+constexpr int kThreads = 24 * 32;
 constexpr int kMaxBatch = 128;
 constexpr int kMaxTiles = 4096;    // 128-row tiles per projection (n <= 524288)
 constexpr int kSlotCols = kChunk / 2;  // TMEM columns of one A slot (two bf16 per column)
@@ -78,10 +86,10 @@ struct GemmArgs {
   __nv_bfloat16* y;              // [batch, N] or [batch, N/2] (paired)
   float* partial;                // [2 * grid][batch][128] contributions to cut tiles
   unsigned* tickets;             // [tiles], zero on entry and exit
-  int batch, n, k, n_mma, tiles, chunks, stages;
+  int batch, n, k, n_mma, tiles, chunks, cstages, xstages;  // code and activation ring stages
   int zt;             // zero points arrive by TMA with the codes ((k / 64) % 16 == 0), else per thread
   const uint8_t* packed;  // packed layout: [tiles * chunks][kPackedBlock] (PACKED kernels)
-  int d_cols, slots;  // accumulator columns (64 or 128) and TMEM A slots after the two accumulators
+  int d_cols, nbuf, slots;  // accumulator columns (32, 64 or 128), buffers per MMA warp, TMEM A slots
 };
 
 __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
@@ -194,15 +202,16 @@ template <bool PAIRED, bool PACKED>
 __global__ void __launch_bounds__(kThreads, 1)
     w4a16_gemm_tc(GemmArgs a, const __grid_constant__ CUtensorMap xmap, const __grid_constant__ CUtensorMap wmap,
                   const __grid_constant__ CUtensorMap smap, const __grid_constant__ CUtensorMap zmap) {
-  // dynamic shared memory, from the first 1024-byte boundary: [stages] x {codes [128][128 B]
-  // (128-byte swizzle), activations [4][n_mma][64] bf16 (128-byte swizzle)}, then [16][64] f32
-  // for the paired epilogue
+  // dynamic shared memory, from the first 1024-byte boundary: [cstages] x codes [128][128 B]
+  // (128-byte swizzle) with scales and zero points, [xstages] x activations [4][n_mma][64]
+  // bf16 (128-byte swizzle), then [16][64] f32 for the paired epilogue
   extern __shared__ __align__(1024) uint8_t smem_raw[];
-  __shared__ __align__(8) uint64_t full[kMaxSlots];    // dequantised chunk in TMEM slot
-  __shared__ __align__(8) uint64_t aempty[kMaxSlots];  // MMAs done with TMEM slot
-  __shared__ __align__(8) uint64_t wfull[kMaxStages];  // codes landed
-  __shared__ __align__(8) uint64_t xfull[kMaxStages];  // activations landed
-  __shared__ __align__(8) uint64_t sempty[kMaxStages];  // MMAs done with the stage
+  __shared__ __align__(8) uint64_t full[2][kMaxSlots];    // K half of a dequantised chunk in TMEM slot
+  __shared__ __align__(8) uint64_t aempty[2][kMaxSlots];  // that half's MMAs done with the TMEM slot
+  __shared__ __align__(8) uint64_t wfull[kMaxStages];   // codes landed
+  __shared__ __align__(8) uint64_t cempty[kMaxStages];  // dequantisation group done with the codes
+  __shared__ __align__(8) uint64_t xfull[kMaxStages];   // activations landed
+  __shared__ __align__(8) uint64_t xempty[kMaxStages];  // MMAs done with the activations
   __shared__ __align__(8) uint64_t dfull[2];
   __shared__ __align__(8) uint64_t dfree[2];
   __shared__ uint32_t tmem_base_s;
@@ -210,19 +219,20 @@ __global__ void __launch_bounds__(kThreads, 1)
   __shared__ unsigned last_s;
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int K = a.k, n_mma = a.n_mma, B = a.batch, chunks = a.chunks, ctas = gridDim.x, nst = a.stages;
+  const int K = a.k, n_mma = a.n_mma, B = a.batch, chunks = a.chunks, ctas = gridDim.x;
+  const int ncs = a.cstages, nxs = a.xstages;
   const int n_out = PAIRED ? a.n / 2 : a.n;
   const long work = (long)a.tiles * chunks;
   const int w0 = range_start(blockIdx.x, work, ctas), w1 = range_start(blockIdx.x + 1, work, ctas);
   const int nwork = w1 - w0;
   const int t_first = w0 / chunks;
   const int nseg = nwork > 0 ? (w1 - 1) / chunks - t_first + 1 : 0;
-  const int nslot = a.slots, a_col0 = 2 * a.d_cols;
+  const int nslot = a.slots, nbuf = a.nbuf, a_col0 = kMmaWarps * nbuf * a.d_cols;
   const uint32_t x_bytes = (uint32_t)n_mma * kChunk * 2, x_box = (uint32_t)n_mma * 128;  // 64-column boxes
-  constexpr uint32_t kStageXOff = PACKED ? kPackedXOff : kXOff;
-  const uint32_t stage_bytes = kStageXOff + x_bytes;
+  constexpr uint32_t kCodeStage = PACKED ? kPackedXOff : kXOff;  // 1024-byte multiples
   uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
-  float* exch = reinterpret_cast<float*>(smem + nst * stage_bytes);
+  uint8_t* xring = smem + (size_t)ncs * kCodeStage;
+  float* exch = reinterpret_cast<float*>(xring + (size_t)nxs * x_bytes);
 
   if (warp == kMmaWarp) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base_s)),
@@ -230,17 +240,19 @@ __global__ void __launch_bounds__(kThreads, 1)
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     if (lane == 0) {
-      for (int i = 0; i < kMaxSlots; ++i) {
-        mbar_init(&full[i], kDequantWarps / 2 * 32);  // one group's lanes
-        mbar_init(&aempty[i], 1);
-      }
+      for (int i = 0; i < kMaxSlots; ++i)
+        for (int hh = 0; hh < 2; ++hh) {
+          mbar_init(&full[hh][i], kDequantWarps / 4 * 32);  // the lanes of one K half of a group
+          mbar_init(&aempty[hh][i], 1);
+        }
       for (int i = 0; i < kMaxStages; ++i) {
         mbar_init(&wfull[i], 1);
+        mbar_init(&cempty[i], kDequantWarps / 2 * 32);
         mbar_init(&xfull[i], 1);
-        mbar_init(&sempty[i], 1);
+        mbar_init(&xempty[i], kMmaWarps);
       }
       for (int i = 0; i < 2; ++i) {
-        mbar_init(&dfull[i], 1);
+        mbar_init(&dfull[i], kMmaWarps);
         mbar_init(&dfree[i], 128);
       }
       abort_s = 0;
@@ -272,16 +284,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int sw = m & 7;  // 128-byte swizzle of row m: 16-byte piece p sits at p ^ sw
     const uint32_t code_off = (uint32_t)m * 128;
 
+    // this group's chunks are grp, grp + 2, ...: TMEM slot and code stage of the next one, and
+    // the phase parities, kept as counters (no runtime division in the loop)
+    int slot = grp, spar = 0, st = grp, cpar = 0;
     auto process = [&](int j, const RowLoads& r) {
-      const int slot = j % nslot, st = j % nst;
       bool ok = true;
       if (j >= nslot) {  // the MMAs of chunk j - nslot have released this TMEM slot
-        ok = mbar_wait_bounded(&aempty[slot], (unsigned)(((j / nslot) - 1) & 1));
+        ok = mbar_wait_bounded(&aempty[h][slot], (unsigned)(spar ^ 1));
         tc_fence_after();
       }
-      ok = mbar_wait_bounded(&wfull[st], (unsigned)((j / nst) & 1)) && ok;
+      ok = mbar_wait_bounded(&wfull[st], (unsigned)cpar) && ok;
       if (!ok) abort_s = 1;
-      const uint8_t* stage = smem + st * stage_bytes;
+      const uint8_t* stage = smem + st * kCodeStage;
       const uint8_t* cs = stage + code_off;
       const uint2 sc = *reinterpret_cast<const uint2*>(stage + kScaleOff + m * 16 + h * 8);
       uint32_t zpair = 0x8888u;
@@ -317,9 +331,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_st16(ta + 32 * half, v);
         tmem_st16(ta + 32 * half + 16, v + 16);
       }
+      mbar_arrive(&cempty[st]);  // codes, scales and zero points consumed: the stage may refill
       asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
       tc_fence_before();
-      mbar_arrive(&full[slot]);
+      mbar_arrive(&full[h][slot]);
+      slot += 2;  // nslot, ncs >= 2: at most one wrap
+      if (slot >= nslot) {
+        slot -= nslot;
+        spar ^= 1;
+      }
+      st += 2;
+      if (st >= ncs) {
+        st -= ncs;
+        cpar ^= 1;
+      }
     };
     RowLoads buf[3];
     load(grp, buf[0]);
@@ -337,60 +362,77 @@ __global__ void __launch_bounds__(kThreads, 1)
         process(j + 4, buf[2]);
       }
     }
-  } else if (warp == kMmaWarp) {
-    // warp-uniform loop; one elected lane issues the MMAs and commits
+  } else if (warp < kMmaWarp + kMmaWarps) {
+    // MMA warp i: the 8 K steps of half i of every chunk into its own accumulator (the epilogue
+    // adds the two); two issuing warps because one thread issues at most one tcgen05.mma per
+    // ~70 cycles whatever N, and 16 per chunk would pace the kernel. Warp-uniform loop; one
+    // elected lane issues the MMAs and commits.
+    const int i = warp - kMmaWarp;
     const uint32_t idesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(n_mma >> 3) << 17) |
                            ((uint32_t)(kTileM >> 4) << 24);
-    const uint32_t b0 = smem_u32(smem) + kStageXOff;
-    int seg = -1;
+    const uint32_t b0 = smem_u32(xring);
+    // ring positions, parities and the chunk index inside the tile kept as counters
+    int seg = -1, buf = 0, c = w0 % chunks, slot = 0, spar = 0, st = 0, xpar = 0;
+    uint32_t d = tmem;
     for (int j = 0; j < nwork; ++j) {
-      const int w = w0 + j, c = w % chunks;
       const bool first = j == 0 || c == 0, last = j == nwork - 1 || c == chunks - 1;
       if (first) {
         ++seg;
-        if (seg >= 2) {  // the epilogue must have read this accumulator's previous segment
-          if (!mbar_wait_bounded(&dfree[seg & 1], (unsigned)(((seg >> 1) - 1) & 1))) abort_s = 1;
+        buf = nbuf == 2 ? (seg & 1) : 0;
+        if (seg >= nbuf) {  // the epilogue must have read this buffer's previous segment
+          if (!mbar_wait_bounded(&dfree[buf], (unsigned)(((seg / nbuf) - 1) & 1))) abort_s = 1;
           tc_fence_after();
         }
+        d = tmem + (uint32_t)((i * nbuf + buf) * a.d_cols);
       }
-      const int slot = j % nslot, st = j % nst;
-      const bool ok = mbar_wait_bounded(&xfull[st], (unsigned)((j / nst) & 1)) &&
-                      mbar_wait_bounded(&full[slot], (unsigned)((j / nslot) & 1));
+      const bool ok = mbar_wait_bounded(&xfull[st], (unsigned)xpar) &&
+                      mbar_wait_bounded(&full[i][slot], (unsigned)spar);
       tc_fence_after();
       if (!ok) abort_s = 1;
-      const uint32_t d = tmem + (uint32_t)((seg & 1) * a.d_cols);
       const uint32_t a_col = tmem + (uint32_t)(a_col0 + slot * kSlotCols);
-      const uint32_t x0 = b0 + st * stage_bytes;
+      const uint32_t x0 = b0 + st * x_bytes;
       __syncwarp();
       if (elect_one()) {
         if (ok && !abort_s) {
 #pragma unroll
-          for (int kk = 0; kk < kChunk / 16; ++kk)
+          for (int u = 0; u < kChunk / 32; ++u) {
+            const int kk = (kChunk / 32) * i + u;
             mma_ts(d, a_col + kk * 8, smem_desc_sw128(x0 + (kk >> 2) * x_box + (kk & 3) * 32), idesc,
-                   (first && kk == 0) ? 0u : 1u);
+                   (first && u == 0) ? 0u : 1u);
+          }
         }
-        mma_commit(&aempty[slot]);
-        mma_commit(&sempty[st]);
-        if (last) mma_commit(&dfull[seg & 1]);
+        mma_commit(&aempty[i][slot]);
+        mma_commit(&xempty[st]);
+        if (last) mma_commit(&dfull[buf]);
       }
       __syncwarp();
+      if (++c == chunks) c = 0;
+      if (++slot == nslot) {
+        slot = 0;
+        spar ^= 1;
+      }
+      if (++st == nxs) {
+        st = 0;
+        xpar ^= 1;
+      }
     }
   } else if (warp == kCodeWarp || warp == kActWarp) {
     // codes (independent of the previous kernel) and activations; warp-uniform loops, one
     // elected lane issues each stage's TMA loads
     const bool codes = warp == kCodeWarp;
     if (!codes) pdl_wait();
-    const uint32_t b0 = smem_u32(smem);
+    const int ns = codes ? ncs : nxs;
+    uint64_t* empty = codes ? cempty : xempty;
+    int st = 0, par = 0, tile = w0 / chunks, c = w0 - tile * chunks;  // counters, no division in the loop
     for (int j = 0; j < nwork; ++j) {
-      const int st = j % nst;
-      if (j >= nst && !mbar_wait_idle(&sempty[st], (unsigned)(((j / nst) - 1) & 1))) abort_s = 1;
-      const int w = w0 + j, tile = w / chunks, c = w - tile * chunks;
-      const uint32_t base = b0 + st * stage_bytes;
+      if (j >= ns && !mbar_wait_idle(&empty[st], (unsigned)(par ^ 1))) abort_s = 1;
+      const int w = w0 + j;
+      const uint32_t base = codes ? smem_u32(smem) + st * kCodeStage : smem_u32(xring) + st * x_bytes;
       __syncwarp();
       if (elect_one()) {
         if (codes && PACKED) {
           mbar_expect_tx(&wfull[st], kPackedBlock);
-          bulk_copy(smem + st * stage_bytes, a.packed + (size_t)w * kPackedBlock, kPackedBlock, &wfull[st]);
+          bulk_copy(smem + st * kCodeStage, a.packed + (size_t)w * kPackedBlock, kPackedBlock, &wfull[st]);
         } else if (codes) {
           const int r0 = PAIRED ? tile * 64 : tile * kTileM, r1 = PAIRED ? n_out + tile * 64 : r0 + 64;
           mbar_expect_tx(&wfull[st], kZeroOff + (a.zt ? kTileM * 16 : 0));
@@ -406,10 +448,18 @@ __global__ void __launch_bounds__(kThreads, 1)
           mbar_expect_tx(&xfull[st], x_bytes);
 #pragma unroll
           for (int bx = 0; bx < kChunk / 64; ++bx)
-            tma_load_2d(base + kStageXOff + bx * x_box, &xmap, c * kChunk + 64 * bx, 0, &xfull[st]);
+            tma_load_2d(base + bx * x_box, &xmap, c * kChunk + 64 * bx, 0, &xfull[st]);
         }
       }
       __syncwarp();
+      if (++st == ns) {
+        st = 0;
+        par ^= 1;
+      }
+      if (++c == chunks) {
+        c = 0;
+        ++tile;
+      }
     }
   } else {
     // Epilogue warps: lane quarter warp % 4; e = 0..127 indexes the named barrier group.
@@ -442,14 +492,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int tile = t_first + s;
       const int ca = max(w0, tile * chunks) - tile * chunks, ce = min(w1, (tile + 1) * chunks) - tile * chunks;
       const bool whole = ca == 0 && ce == chunks;
-      if (!mbar_wait_idle(&dfull[s & 1], (unsigned)((s >> 1) & 1))) abort_s = 1;
+      if (!mbar_wait_idle(&dfull[s % nbuf], (unsigned)((s / nbuf) & 1))) abort_s = 1;
       tc_fence_after();
-      const uint32_t d = tmem + t_lane + (uint32_t)((s & 1) * a.d_cols);
+      // the two MMA warps' accumulators of this segment (K halves 0 and 1)
+      const uint32_t d = tmem + t_lane + (uint32_t)((s % nbuf) * a.d_cols);
+      const uint32_t d1 = d + (uint32_t)(nbuf * a.d_cols);
       float* mine = a.partial + (size_t)(2 * blockIdx.x + (s == 0 ? 0 : 1)) * B * kTileM;
       for (int cb = 0; cb < n_mma; cb += 16) {
-        float v[16];
+        float v[16], v1[16];
         __syncwarp();
         tmem_ld16(d + (uint32_t)cb, v);
+        tmem_ld16(d1 + (uint32_t)cb, v1);
+#pragma unroll
+        for (int t = 0; t < 16; ++t) v[t] += v1[t];
         if (whole) {
           emit(tile, cb, v);
         } else {
@@ -459,7 +514,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       tc_fence_before();
-      mbar_arrive(&dfree[s & 1]);
+      mbar_arrive(&dfree[s % nbuf]);
       if (whole) continue;
       // A cut tile: the last contributor sums the contributions in CTA order.
       const int b_first = owner_of(tile * chunks, work, ctas), b_last = owner_of(tile * chunks + chunks - 1, work, ctas);
@@ -525,7 +580,7 @@ __global__ void __launch_bounds__(256) w4a16_gemm_pack_kernel(const uint8_t* __r
 }
 
 struct Plan {
-  int tiles, chunks, n_mma, ctas, stages, d_cols, slots;
+  int tiles, chunks, n_mma, ctas, cstages, xstages, d_cols, nbuf, slots;
   size_t smem, partial_bytes, ticket_bytes;
 };
 
@@ -535,16 +590,25 @@ static bool make_plan(int batch, int n, int k, int mode, Plan* p, bool packed = 
   p->tiles = paired ? (n / 2) / 64 : n / kTileM;
   p->chunks = k / kChunk;
   p->n_mma = (batch + 15) / 16 * 16;
-  p->d_cols = p->n_mma <= 64 ? 64 : 128;
-  p->slots = (kTmemCols - 2 * p->d_cols) / kSlotCols;
+  // two MMA warps, each with its own accumulator per buffer: double-buffered up to 32 columns
+  // (3 A slots either way up to 64 columns, 2 at 128)
+  p->d_cols = p->n_mma <= 32 ? 32 : p->n_mma <= 64 ? 64 : 128;
+  p->nbuf = p->d_cols <= 32 ? 2 : 1;
+  p->slots = (kTmemCols - kMmaWarps * p->nbuf * p->d_cols) / kSlotCols;
+  if (p->slots > kMaxSlots) p->slots = kMaxSlots;
   const long work = (long)p->tiles * p->chunks;
   p->ctas = (int)(work < sm_count() ? work : sm_count());
-  const size_t stage = (packed ? kPackedXOff : kXOff) + (size_t)p->n_mma * kChunk * 2,
-               fixed = 1024 + 16 * 64 * sizeof(float);
-  p->stages = (int)((200 * 1024 - fixed) / stage);
-  if (p->stages > kMaxStages) p->stages = kMaxStages;
-  if (p->stages < 2) return false;
-  p->smem = fixed + (size_t)p->stages * stage;
+  // activation stages: up to four in at most ~45 % of the budget (two at least); the code
+  // ring takes the rest, up to eight stages
+  const size_t cstage = packed ? kPackedXOff : kXOff, xstage = (size_t)p->n_mma * kChunk * 2,
+               fixed = 1024 + 16 * 64 * sizeof(float), budget = 220 * 1024 - fixed;
+  p->xstages = (int)(budget * 45 / 100 / xstage);
+  if (p->xstages > 4) p->xstages = 4;
+  if (p->xstages < 2) p->xstages = 2;
+  p->cstages = (int)((budget - p->xstages * xstage) / cstage);
+  if (p->cstages > kMaxStages) p->cstages = kMaxStages;
+  if (p->cstages < 2) return false;
+  p->smem = fixed + (size_t)p->cstages * cstage + (size_t)p->xstages * xstage;
   // a fixed ticket region, so that calls of different shapes can share one workspace: one
   // call's partials never overlap another call's tickets
   if (p->tiles > kMaxTiles) return false;
@@ -664,8 +728,10 @@ MT_API int mt_w4a16_gemm(const void* x, const void* qweight, const void* scales,
   a.n_mma = p.n_mma;
   a.tiles = p.tiles;
   a.chunks = p.chunks;
-  a.stages = p.stages;
+  a.cstages = p.cstages;
+  a.xstages = p.xstages;
   a.d_cols = p.d_cols;
+  a.nbuf = p.nbuf;
   a.slots = p.slots;
   a.zt = qzeros && (k / 64) % 16 == 0;
   alignas(64) CUtensorMap xmap, wmap, smap, zmap;
@@ -728,8 +794,10 @@ MT_API int mt_w4a16_gemm_packed(const void* x, const void* packed, void* y, int 
   a.n_mma = p.n_mma;
   a.tiles = p.tiles;
   a.chunks = p.chunks;
-  a.stages = p.stages;
+  a.cstages = p.cstages;
+  a.xstages = p.xstages;
   a.d_cols = p.d_cols;
+  a.nbuf = p.nbuf;
   a.slots = p.slots;
   alignas(64) CUtensorMap xmap, none;
   memset(&none, 0, sizeof(none));
