@@ -849,7 +849,9 @@ def main():
         v, setup = cpu_oracle_run(args.layers, cpu_steps, 1, threads)
         cpu = {"value": round(v, 4), "unit": UNIT, "cores": threads, "kind": "port",
                "sample": cpu_sample_text(args.layers, cpu_steps, threads), "setup_s": round(setup, 1)}
-    launches = 3 + 5 * args.layers  # embedding, 5 per layer, heads, the device advance
+    # embedding, per layer q/k/v, attention (+ o_proj when folded), o_proj, gate/up, down; heads; advance
+    per_layer = 4 if getattr(eng, "fused_oproj", False) else 5
+    launches = 3 + per_layer * args.layers
     line = {
         "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True,

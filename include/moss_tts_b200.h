@@ -304,6 +304,24 @@ int mt_attention_decode(const void* qkv, const void* q_norm, const void* k_norm,
                         float eps, void* status, int flags, void* stream);
 
 /*
+ * mt_attention_decode of one sequence with the attention output projection folded into the
+ * kernel's tail: out = attention (as mt_attention_decode), proj = bf16(W_o . out), W_o
+ * [n_out, nq*128] in the packed layout of mt_w4a16_pack (wo_zeros != 0: blocks carry zero
+ * points). Replaces the attention + o_proj pair of the reference's decode layer
+ * (src/moss_tts/_runtime/llm.py:246-252: attention, then the quantized o_proj of
+ * dp4a_packing.project). Each KV head's 8-CTA cluster multiplies its head group's columns of
+ * W_o (blocks fetched into shared memory before the dependency wait); the KV heads'
+ * partials are summed in KV-head order by the last CTA of each row block (deterministic).
+ * workspace: nkv*n_out*4 + 64 bytes, zero-filled once; calls leave it reusable. Requires
+ * nq/nkv = 2 or 4, n_out % 128 == 0, 16-byte aligned wo_packed and workspace.
+ */
+int mt_attention_oproj_decode(const void* qkv, const void* q_norm, const void* k_norm, const void* cos_tab,
+                              const void* sin_tab, const void* positions, void* k_cache, void* v_cache,
+                              void* out, const void* wo_packed, int wo_zeros, void* proj, int n_out,
+                              void* workspace, int nq, int nkv, int max_len, float eps, void* status,
+                              int flags, void* stream);
+
+/*
  * mt_attention_decode for callers that cannot allocate device memory: real-time audio
  * callbacks that must not block on an allocator, and plugin or FFI hosts that own no device
  * allocator of their own. No counterpart in the reference.

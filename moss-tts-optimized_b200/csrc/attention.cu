@@ -23,6 +23,7 @@
 #include <mutex>
 
 #include "common.cuh"
+#include "w4_tiles.cuh"
 
 namespace cg = cooperative_groups;
 
@@ -47,6 +48,14 @@ struct AttnArgs {
   int nq, nkv, max_len, splits;
   float eps;
   int* status;                   // optional: set to 1 when a position is out of range
+  // o_proj folded into the tail (mt_attention_oproj_decode, one sequence): W_o in the packed
+  // slice-block layout of mt_w4a16_pack, fp32 partials [nkv][n_out] (one per KV head), merge
+  // counters [cluster ranks] (zero on entry and exit) and the bf16 projection [n_out]
+  const uint8_t* wo;
+  int wo_zeros, n_out;
+  float* opart;
+  unsigned* otickets;
+  __nv_bfloat16* oout;
 };
 
 // Head RMSNorm + RoPE for one 128-wide head held as 4 values per lane
@@ -593,15 +602,28 @@ __global__ void __launch_bounds__(kAttnThreads) attention_cluster(AttnArgs a) {
 // tensor boxes with the 128-byte swizzle (attn_swz), so every ldmatrix is conflict-free.
 constexpr int kWsWarps = kAttnThreads / 32;
 
-template <int REP, int kChunk, int CL>
-__global__ void __launch_bounds__(kAttnThreads, 2)
+template <int REP, int kChunk, int CL, bool OPROJ = false>
+__global__ void __launch_bounds__(kAttnThreads, OPROJ ? 1 : 2)
     attention_ws(AttnArgs a, const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap) {
   extern __shared__ __align__(128) uint8_t sm_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(sm_raw) + 1023) & ~uintptr_t(1023));
   constexpr int kQStride = 36;  // floats per 32-dim quarter of q (+4 pad)
   constexpr size_t kSlotBytes = (size_t)kChunk * kHeadDim * 2 * 2;
   __shared__ __align__(16) float qs[REP * 4 * kQStride];
-  __shared__ __align__(16) float wo[kWsWarps][REP][kHeadDim];  // each warp's unnormalised O
+  // each warp's unnormalised O; with the o_proj tail it lives in the K/V slots (free by then),
+  // which leaves the shared memory to this CTA's W_o blocks
+  __shared__ __align__(16) float wo_s[OPROJ ? 1 : kWsWarps][REP][OPROJ ? 1 : kHeadDim];
+  float (*wo)[REP][kHeadDim] = OPROJ ? reinterpret_cast<float (*)[REP][kHeadDim]>(sm)
+                                     : reinterpret_cast<float (*)[REP][kHeadDim]>(&wo_s[0][0][0]);
+  constexpr int kOw = OPROJ ? REP * kHeadDim : 1;  // this KV head's slice of the o_proj input
+  constexpr int kSpk = OPROJ ? REP * kHeadDim / kSliceCols : 1;  // its 256-column slices
+  __shared__ __align__(16) float att_s[kOw];          // the gathered attention output (bf16 values)
+  __shared__ __align__(16) uint4 oxp[OPROJ ? kOw / 8 : 1];  // fp16 operand pairs (GEMV layout)
+  __shared__ float oxsum[OPROJ ? kOw / 32 : 1];       // c * sum of each 32-column group
+  __shared__ float oscale[kSpk];                      // 2^24 / c per slice
+  __shared__ __align__(16) uint4 ozero16[4];
+  __shared__ __align__(8) uint64_t wbar;              // W_o blocks landed
+  __shared__ int olast;
   __shared__ float wm[kWsWarps][REP], wl[kWsWarps][REP];
   constexpr int kSl = kHeadDim / CL;  // output dims each rank finishes
   __shared__ __align__(16) float inbox[CL][REP][kSl];
@@ -664,7 +686,27 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
     issued = min(2, chunks);
     // rows before `position` were written by earlier steps: fetch before the wait
     for (int c = 0; c < 2 && c < chunks; ++c) issue(c);
+    if constexpr (OPROJ) {
+      // this CTA's W_o blocks never depend on the previous kernel either: tiles
+      // [rank * tpc, +tpc) of the output, slices [kh * kSpk, +kSpk) of the input (the query
+      // heads of this KV head), one bulk copy of kSpk consecutive blocks per tile
+      const int S = a.nq * kHeadDim / kSliceCols, tpc = a.n_out / 16 / CL;
+      const unsigned bb = (unsigned)(kCodeBytes + kScaleBytes + (a.wo_zeros ? kZeroBytes : 0));
+      uint8_t* wdst = sm + 2 * kSlotBytes;
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(attn_smem_u32(&wbar)) : "memory");
+      asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+      asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(attn_smem_u32(&wbar)),
+                   "r"((unsigned)(tpc * kSpk) * bb) : "memory");
+      for (int t = 0; t < tpc; ++t) {
+        const uint8_t* src = a.wo + ((size_t)(rank * tpc + t) * S + (size_t)kh * kSpk) * bb;
+        asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                         attn_smem_u32(wdst + (size_t)t * kSpk * bb)),
+                     "l"(src), "r"(kSpk * bb), "r"(attn_smem_u32(&wbar))
+                     : "memory");
+      }
+    }
   }
+  if (OPROJ && tid < 4) ozero16[tid] = make_uint4(0, 0, 0, 0);
   // Inputs that do not depend on the previous kernel: this row's RoPE factors and the
   // head-norm weights, for warps that rotate a head (q heads: warps < REP; k: warp REP).
   const bool rotates = warp < REP || (warp == REP && owner);
@@ -885,7 +927,107 @@ __global__ void __launch_bounds__(kAttnThreads, 2)
       S = fmaf(w, linbox[r][h], S);
       O = fmaf(w, inbox[r][h][dd], O);
     }
-    a.out[(size_t)b * a.nq * kHeadDim + (kh * REP + h) * kHeadDim + kSl * rank + dd] = to_bf16(O / S);
+    const __nv_bfloat16 ob = to_bf16(O / S);
+    a.out[(size_t)b * a.nq * kHeadDim + (kh * REP + h) * kHeadDim + kSl * rank + dd] = ob;
+    if constexpr (OPROJ) {  // every CTA of the cluster needs the whole head group as o_proj input
+      const float ov = __bfloat162float(ob);
+#pragma unroll
+      for (int r = 0; r < CL; ++r) *cluster.map_shared_rank(&att_s[h * kHeadDim + kSl * rank + dd], r) = ov;
+    }
+  }
+  if constexpr (OPROJ) {
+    cluster.sync();  // the gathered input is complete in every CTA (and no CTA writes remote memory later)
+    // ---- o_proj, split-K over the KV heads: y_kh = W_o[:, kh's columns] . attention(kh) ----
+    // The input slices as the packed GEMV takes them (w4a16_stream.cu): per 256-column slice a
+    // power-of-two scale c, fp16 pairs (x_j c, x_{j+4} c) / (x_{j+1} c / 16, x_{j+5} c / 16)
+    // and c times each 32-column group's sum for the zero-point term.
+    if (warp < kSpk) {
+      const int word = warp * 32 + lane;
+      float v8[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v8[i] = att_s[word * 8 + i];
+      float mx = 0.f, wsum = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        mx = fmaxf(mx, fabsf(v8[i]));
+        wsum += v8[i];
+      }
+      mx = warp_max(mx);
+      const int ex = mx > 0.f ? min(max((int)((__float_as_uint(mx) >> 23) & 0xFF) - 127, -100), 100) : 0;
+      const float cs = __uint_as_float((uint32_t)(127 + 9 - ex) << 23);
+      oxp[word] = make_uint4(pack_half2(v8[0] * cs, v8[4] * cs), pack_half2(v8[1] * cs * 0.0625f, v8[5] * cs * 0.0625f),
+                             pack_half2(v8[2] * cs, v8[6] * cs), pack_half2(v8[3] * cs * 0.0625f, v8[7] * cs * 0.0625f));
+      wsum += __shfl_xor_sync(0xffffffffu, wsum, 1);
+      wsum += __shfl_xor_sync(0xffffffffu, wsum, 2);
+      if ((lane & 3) == 0) oxsum[word >> 2] = wsum * cs;
+      if (lane == 0) oscale[warp] = __uint_as_float((uint32_t)(127 + 24 - 9 + ex) << 23);
+    }
+    __syncthreads();
+    const bool wok = __all_sync(0xffffffffu, wait_bar(&wbar, 0u));
+    if (!wok && lane == 0 && a.status) atomicExch(a.status, 3);
+    const int tpc = a.n_out / 16 / CL, S = a.nq * kHeadDim / kSliceCols;
+    (void)S;
+    const bool zeros = a.wo_zeros != 0;
+    const int bb = kCodeBytes + kScaleBytes + (zeros ? kZeroBytes : 0);
+    const uint8_t* wsrc = sm + 2 * kSlotBytes;
+    const int r = lane >> 2, c = lane & 3, hsel = r - 2 * c;
+    constexpr int kTpw = 4;  // tiles per warp per pass
+    for (int t0 = warp; t0 < tpc; t0 += kWsWarps * kTpw) {
+      float acc[kTpw][2] = {};
+#pragma unroll
+      for (int sl = 0; sl < kSpk; ++sl) {
+        uint32_t bl[16], bh[16];
+        const uint4* pl = hsel == 0 ? oxp + sl * 32 + 8 * c : ozero16;
+        const uint4* ph = hsel == 1 ? oxp + sl * 32 + 8 * c + 4 : ozero16;
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const uint4 ql = pl[u], qh = ph[u];
+          bl[4 * u] = ql.x; bl[4 * u + 1] = ql.y; bl[4 * u + 2] = ql.z; bl[4 * u + 3] = ql.w;
+          bh[4 * u] = qh.x; bh[4 * u + 1] = qh.y; bh[4 * u + 2] = qh.z; bh[4 * u + 3] = qh.w;
+        }
+        const float z0 = hsel == 0 ? -oxsum[sl * 8 + 2 * c] : 0.f;
+        const float z1 = hsel == 1 ? -oxsum[sl * 8 + 2 * c + 1] * 0.0625f : 0.f;
+        const float h0 = __half2float(__float2half_rn(z0)), h1 = __half2float(__float2half_rn(z1));
+        const uint32_t bz0 = pack_half2(h0, h1), bz1 = pack_half2(z0 - h0, z1 - h1);
+        const float scale = oscale[sl];
+#pragma unroll
+        for (int i = 0; i < kTpw; ++i) {
+          const int t = t0 + kWsWarps * i;
+          if (t >= tpc || !wok) continue;
+          const BlockRegs bk = load_block(wsrc + ((size_t)t * kSpk + sl) * bb, lane, zeros);
+          float va, vb;
+          block_dot<2>(bk, bl, bh, bz0, bz1, va, vb);
+          acc[i][0] += va * scale;
+          acc[i][1] += vb * scale;
+        }
+      }
+      if (c == 0) {
+#pragma unroll
+        for (int i = 0; i < kTpw; ++i) {
+          const int t = t0 + kWsWarps * i;
+          if (t >= tpc) continue;
+          const int row = (rank * tpc + t) * 16 + r;
+          a.opart[(size_t)kh * a.n_out + row] = acc[i][0];
+          a.opart[(size_t)kh * a.n_out + row + 8] = acc[i][1];
+        }
+      }
+    }
+    // The KV heads' partials of this CTA's rows are summed by the last of their nkv CTAs, in
+    // KV-head order (deterministic); the counter is left at zero for the next call.
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) olast = atomicAdd(&a.otickets[rank], 1u) == (unsigned)(a.nkv - 1) ? 1 : 0;
+    __syncthreads();
+    if (olast) {
+      __threadfence();
+      for (int i = tid; i < tpc * 16; i += kAttnThreads) {
+        const int row = rank * tpc * 16 + i;
+        float y = 0.f;
+        for (int k = 0; k < a.nkv; ++k) y += __ldcg(a.opart + (size_t)k * a.n_out + row);
+        a.oout[row] = to_bf16(y);
+      }
+      if (tid == 0) a.otickets[rank] = 0u;
+    }
   }
 }
 
@@ -1022,6 +1164,39 @@ static cudaError_t launch_cluster_attention(const AttnArgs& a, int batch, int re
     default: return ch == 128 ? launch_cluster_rep<1, 128>(cfg, a, batch) : ch == 64 ? launch_cluster_rep<1, 64>(cfg, a, batch)
                                                                             : launch_cluster_rep<1, 32>(cfg, a, batch);
   }
+}
+
+// The warp-split kernel with the o_proj tail (one sequence, 8-CTA clusters, 64-token chunks:
+// the two K/V slots and this CTA's W_o blocks share the shared memory).
+template <int REP>
+static cudaError_t launch_attention_oproj(const AttnArgs& a, cudaStream_t s, int flags) {
+  constexpr int CH = 64, CL = 8;
+  const long long rows = (long long)a.nkv * a.max_len;
+  CUtensorMap kmap, vmap;
+  memset(&kmap, 0, sizeof(kmap));
+  memset(&vmap, 0, sizeof(vmap));
+  if (!(rows < (1LL << 31) && cache_map(&kmap, a.k_cache, rows, CH) && cache_map(&vmap, a.v_cache, rows, CH)))
+    return cudaErrorNotSupported;
+  const size_t bb = kCodeBytes + kScaleBytes + (a.wo_zeros ? kZeroBytes : 0);
+  const size_t wbytes = (size_t)(a.n_out / 16 / CL) * (REP * kHeadDim / kSliceCols) * bb;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(CL * a.nkv, 1, 1);
+  cfg.blockDim = dim3(kAttnThreads);
+  cfg.stream = s;
+  cfg.dynamicSmemBytes = 2 * (size_t)CH * kHeadDim * 2 * 2 + wbytes + 1024;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = CL;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = (flags & kFlagPdl) ? 2 : 1;
+  auto kern = attention_ws<REP, CH, CL, true>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)cfg.dynamicSmemBytes);
+  if (e != cudaSuccess) return e;
+  return cudaLaunchKernelEx(&cfg, kern, a, kmap, vmap);
 }
 
 static size_t attn_smem_bytes(int rep, int max_len, int splits) {
@@ -1202,6 +1377,52 @@ cudaError_t scratch_for_current_device(NoAllocScratch** out) {
 }  // namespace mt
 
 // No counterpart in the reference: mt_attention_decode without caller-provided scratch.
+// Decode attention of one sequence with the attention output projection folded into its
+// tail: out = attention (as mt_attention_decode), proj = bf16(W_o . out) with W_o [n_out,
+// nq * 128] in the packed layout of mt_w4a16_pack (wo_zeros: blocks carry zero points). The
+// o_proj is split over the KV heads: each 8-CTA cluster multiplies its head group's 512
+// columns (the blocks fetched into shared memory before the dependency wait), and the
+// partials are summed in KV-head order by the last CTA per row block. workspace:
+// nkv * n_out * 4 + 64 bytes, zero-filled once (calls leave it reusable). Requires nq / nkv
+// = 2 or 4, n_out % 128 == 0, and the tensor-core attention path (MT_ATTN_TC unset).
+// Replaces the reference's attention + o_proj pair of FastLLM.hidden (llm.py:246-252).
+MT_API int mt_attention_oproj_decode(const void* qkv, const void* q_norm, const void* k_norm, const void* cos_tab,
+                                     const void* sin_tab, const void* positions, void* k_cache, void* v_cache,
+                                     void* out, const void* wo_packed, int wo_zeros, void* proj, int n_out,
+                                     void* workspace, int nq, int nkv, int max_len, float eps, void* status,
+                                     int flags, void* stream) {
+  AttnArgs a;
+  memset(&a, 0, sizeof(a));
+  a.qkv = (const __nv_bfloat16*)qkv;
+  a.q_norm = (const __nv_bfloat16*)q_norm;
+  a.k_norm = (const __nv_bfloat16*)k_norm;
+  a.cos_tab = (const __nv_bfloat16*)cos_tab;
+  a.sin_tab = (const __nv_bfloat16*)sin_tab;
+  a.positions = (const int64_t*)positions;
+  a.k_cache = (__nv_bfloat16*)k_cache;
+  a.v_cache = (__nv_bfloat16*)v_cache;
+  a.out = (__nv_bfloat16*)out;
+  a.nq = nq;
+  a.nkv = nkv;
+  a.max_len = max_len;
+  a.splits = 1;
+  a.eps = eps;
+  a.status = (int*)status;
+  a.wo = (const uint8_t*)wo_packed;
+  a.wo_zeros = wo_zeros ? 1 : 0;
+  a.n_out = n_out;
+  a.opart = (float*)workspace;
+  a.otickets = (unsigned*)((uint8_t*)workspace + (size_t)nkv * n_out * sizeof(float));
+  a.oout = (__nv_bfloat16*)proj;
+  if (attn_check(a, 1) || !out || !wo_packed || !proj || !workspace || n_out < 128 || n_out % 128 ||
+      n_out > (1 << 20) || !aligned(wo_packed, 16) || !aligned(workspace, 16))
+    return kBadArgument;
+  const int rep = nq / nkv;
+  if ((rep != 4 && rep != 2) || !attention_tc()) return kBadArgument;
+  cudaStream_t s = (cudaStream_t)stream;
+  return (int)(rep == 4 ? launch_attention_oproj<4>(a, s, flags & kFlagPdl) : launch_attention_oproj<2>(a, s, flags & kFlagPdl));
+}
+
 MT_API int mt_attention_decode_noalloc(const void* qkv, const void* q_norm, const void* k_norm,
                                        const void* cos_tab, const void* sin_tab, const void* positions,
                                        void* k_cache, void* v_cache, void* out, int batch, int nq, int nkv,

@@ -207,6 +207,16 @@ class DecodeEngine:
             for p, paired in ((lw.qkv, False), (lw.out, False), (lw.gate_up, True), (lw.down, False)))
         if self.persistent:
             self._build_layer_table()
+        # One GPU, packed W4 o_proj, MT_FUSED_OPROJ=1: the attention kernel also runs the o_proj
+        # (split over the KV heads, mt_attention_oproj_decode), one launch fewer per layer. Off by
+        # default: measured slower (594 against 669 steps/s), since the o_proj weights then stream
+        # into the 64 attention SMs only, while the separate GEMV prefetches them on all 148.
+        rep_ = self.nq // self.nkv
+        self.fused_oproj = (world == 1 and os.environ.get("MT_FUSED_OPROJ", "0") == "1"
+                            and os.environ.get("MT_ATTN_TC", "1") != "0" and rep_ in (2, 4)
+                            and h % 128 == 0 and all(self._packed_ok(lw.out, False) for lw in weights.layers))
+        if self.fused_oproj:
+            self.oproj_ws = torch.zeros(self.nkv * h * 4 + 64, device=dev, dtype=torch.uint8)
 
     # ------------------------------------------------------------------ kernels
     def _build_layer_table(self) -> None:
@@ -291,12 +301,22 @@ class DecodeEngine:
                 self._linear(lw.qkv, self.mlp, self.qkv, residual=res, norm=lw.input_norm, summed=out, tp=tp_in)
                 res, nxt = out, 1 - nxt
             k, v = self.kv[i, 0], self.kv[i, 1]
-            native.call("mt_attention_decode", self.qkv.data_ptr(), lw.q_norm.data_ptr(), lw.k_norm.data_ptr(),
-                        self.cos.data_ptr(), self.sin.data_ptr(), self.position.data_ptr(), k.data_ptr(),
-                        v.data_ptr(), self.attn.data_ptr(), self.partial.data_ptr(), self.lse.data_ptr(),
-                        self.tickets.data_ptr(), 1, self.nq, self.nkv, self.max_length, self.splits, eps,
-                        self.status.data_ptr(), self.flags, s)
-            if ex is not None:
+            if self.fused_oproj:
+                native.call("mt_attention_oproj_decode", self.qkv.data_ptr(), lw.q_norm.data_ptr(),
+                            lw.k_norm.data_ptr(), self.cos.data_ptr(), self.sin.data_ptr(), self.position.data_ptr(),
+                            k.data_ptr(), v.data_ptr(), self.attn.data_ptr(), lw.out.packed_tiles(False).data_ptr(),
+                            1 if lw.out.qzeros is not None else 0, self.proj.data_ptr(), cfg.hidden_size,
+                            self.oproj_ws.data_ptr(), self.nq, self.nkv, self.max_length, eps,
+                            self.status.data_ptr(), self.flags, s)
+            else:
+                native.call("mt_attention_decode", self.qkv.data_ptr(), lw.q_norm.data_ptr(), lw.k_norm.data_ptr(),
+                            self.cos.data_ptr(), self.sin.data_ptr(), self.position.data_ptr(), k.data_ptr(),
+                            v.data_ptr(), self.attn.data_ptr(), self.partial.data_ptr(), self.lse.data_ptr(),
+                            self.tickets.data_ptr(), 1, self.nq, self.nkv, self.max_length, self.splits, eps,
+                            self.status.data_ptr(), self.flags, s)
+            if self.fused_oproj:  # the projection is already in self.proj
+                pass
+            elif ex is not None:
                 self._linear(lw.out, self.attn, self.proj, tp=ex.desc(out_slot=2 * i))
             else:
                 self._linear(lw.out, self.attn, self.proj)

@@ -47,6 +47,7 @@ SIGNATURES = {
     "mt_qk_rope_kv": ([_P, _P, _P, _P, _P, _P, _P, _P, _P, _I, _I, _I, _I, _F, _P, _I, _P], _I),
     "mt_attention_decode": ([_P] * 12 + [_I] * 5 + [_F, _P, _I, _P], _I),
     "mt_attention_decode_noalloc": ([_P] * 9 + [_I] * 5 + [_F, _P, _I, _P], _I),
+    "mt_attention_oproj_decode": ([_P] * 10 + [_I, _P, _I, _P, _I, _I, _I, _F, _P, _I, _P], _I),
     "mt_decode_layers_workspace": ([_I, _I, _LLP], _I),
     "mt_decode_layers": ([_P, _I, _I, _I, _P, _P, _P, _P, _I, _F, _P, _P, _P, _P, _I, _P], _I),
     "mt_prefill_qk_rope_kv": ([_P, _P, _P, _P, _P, _I, _P, _P, _P, _I, _I, _I, _I, _F, _I, _P], _I),

@@ -452,6 +452,69 @@ def test_attention_ragged_batch(cuda_device, flags):
         close(host_bits(out[b]), ops.attention_decode(q, kf, vf, p))
 
 
+@pytest.mark.parametrize("ctx,zeros", [(0, True), (95, True), (600, True), (2048, False), (4095, True)])
+def test_attention_oproj_fused_against_oracle(cuda_device, ctx, zeros):
+    """Attention with o_proj folded into its tail (mt_attention_oproj_decode): the attention
+    output against the oracle as mt_attention_decode's, the projection against the oracle's
+    o_proj of the oracle attention (GEMV bar), and against the unfused packed GEMV on the
+    kernel's own attention output; repeat calls bitwise equal (the merge counters return to
+    zero)."""
+    from moss_tts._runtime import native
+    L = max(ctx + 1, 128)
+    g = golden("ops")
+    kc = synthetic.activation(900 + ctx, (1, 8, L, 128))
+    vc = synthetic.activation(901 + ctx, (1, 8, L, 128))
+    qkv = synthetic.activation(902 + ctx, (6144,))
+    rng = np.random.Generator(np.random.PCG64(903 + ctx))
+    p = synthetic.quantized(rng, 4096, 4096, 32, zeros)
+    qw, sc, qz = upload_w4(p, cuda_device)
+    nbytes, _ = native.w4a16_packed_size(4096, 4096, qz is not None, 0)
+    packed = torch.empty(nbytes, dtype=torch.uint8, device=cuda_device)
+    s = torch.cuda.current_stream().cuda_stream
+    native.call("mt_w4a16_pack", qw.data_ptr(), sc.data_ptr(), native.ptr(qz), 4096, 4096, 0, packed.data_ptr(), s)
+    cos, sin = _rope(cuda_device, L)
+    qn, kn = dev_bf16(g["rope_qn"], cuda_device), dev_bf16(g["rope_kn"], cuda_device)
+    pos = torch.tensor([ctx], device=cuda_device)
+    ws = torch.zeros(8 * 4096 * 4 + 64, dtype=torch.uint8, device=cuda_device)
+    outs = []
+    for flags in (0, 0, 1):
+        kd, vd = dev_bf16(kc, cuda_device), dev_bf16(vc, cuda_device)
+        att = torch.empty(4096, device=cuda_device, dtype=torch.bfloat16)
+        proj = torch.empty(4096, device=cuda_device, dtype=torch.bfloat16)
+        status = torch.zeros(1, device=cuda_device, dtype=torch.int32)
+        rc = native.library().mt_attention_oproj_decode(
+            dev_bf16(qkv, cuda_device).data_ptr(), qn.data_ptr(), kn.data_ptr(), cos.data_ptr(), sin.data_ptr(),
+            pos.data_ptr(), kd.data_ptr(), vd.data_ptr(), att.data_ptr(), packed.data_ptr(), 1 if zeros else 0,
+            proj.data_ptr(), 4096, ws.data_ptr(), 32, 8, L, 1e-6, status.data_ptr(), flags, s)
+        assert rc == 0
+        torch.cuda.synchronize()
+        assert int(status.item()) == 0
+        outs.append((host_bits(att), host_bits(proj), host_bits(kd), host_bits(vd)))
+    assert int(ws[8 * 4096 * 4:].abs().sum()) == 0  # merge counters back at zero
+    for o in outs[1:]:
+        assert all(np.array_equal(x, y) for x, y in zip(outs[0], o))
+    att_bits, proj_bits, kbits, vbits = outs[0]
+    c_ref, s_ref = ops.rope_table([ctx])
+    q, krow, vrow = ops.qk_rope(from_bf16_bits(qkv), from_bf16_bits(g["rope_qn"]), from_bf16_bits(g["rope_kn"]),
+                                c_ref[0], s_ref[0], 1e-6)
+    kf, vf = from_bf16_bits(kc)[0].copy(), from_bf16_bits(vc)[0].copy()
+    kf[:, ctx], vf[:, ctx] = krow, vrow
+    assert np.array_equal(vbits[0, :, ctx], bf16_bits(vrow))
+    ref_att = ops.attention_decode(q, kf, vf, ctx)
+    close(att_bits.reshape(-1), ref_att)
+    wdq = quant.dequantize_w4(p["qweight"], p["scales"], p["qzeros"])
+    close(proj_bits, ops.linear(from_bf16_bits(att_bits.reshape(-1)), wdq))
+    # the unfused packed GEMV on the same attention output: same rows up to summation order
+    y = torch.empty((1, 4096), device=cuda_device, dtype=torch.bfloat16)
+    gws = torch.zeros(native.w4a16_packed_size(4096, 4096, qz is not None, 0)[1], dtype=torch.uint8,
+                      device=cuda_device)
+    native.call("mt_w4a16_linear_packed", dev_bf16(att_bits.reshape(1, -1), cuda_device).data_ptr(), None, None,
+                1e-6, None, packed.data_ptr(), 1 if zeros else 0, y.data_ptr(), 4096, 4096, 0, gws.data_ptr(), 0, s)
+    diff = np.abs(from_bf16_bits(host_bits(y)).reshape(-1) - from_bf16_bits(proj_bits))
+    scale = np.abs(from_bf16_bits(proj_bits)) + 1e-3
+    assert float((diff / scale).max()) <= 2 ** -7, float((diff / scale).max())
+
+
 # ------------------------------------------------------------------ heads
 def test_heads_greedy_against_oracle(cuda_device):
     from moss_tts._runtime import native
