@@ -152,7 +152,7 @@ int mt_w4a16_linear_packed_rows(const void* x, const void* residual, const void*
  *                  rank r (flag = low 32 bits of *epoch) -- plain stores, no TMA multicast;
  *   in_slot >= 0:  the consumer polls its recv[rank][in_slot][r] cells until every flag equals
  *                  *epoch, and uses x = bf16(sum over ranks r in order) in place of `x`.
- * The poll of one call is bounded by a 100 ms deadline for the whole kernel: a cell still stale
+ * The poll of one call is bounded by a 1 s deadline for the whole kernel: a cell still stale
  * then (a dead or late peer) sets error word 2 (mt_read_error_word), the kernel finishes with
  * what it read, and later calls give up at once while the word is 2.
  * `epoch` is the caller's device step counter, incremented once per step on every rank before

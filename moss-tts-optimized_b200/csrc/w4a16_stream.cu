@@ -111,9 +111,11 @@ struct StreamArgs {
 
 
 // Longest time one kernel polls its tensor-parallel input cells before it gives up, raises
-// error word 2 and computes with what it has (a dead or late peer; far above the microseconds
-// a healthy exchange takes).
-constexpr unsigned long long kExchangeDeadlineNs = 100ull * 1000 * 1000;
+// error word 2 and computes with what it has (a dead or late peer). Far above the microseconds
+// a healthy exchange takes, and above the host-side skew ranks can legitimately have when
+// they enter a step (one rank still doing host work while the others have launched): at
+// 100 ms a rank that started its first step 0.1 s late made its peers give up.
+constexpr unsigned long long kExchangeDeadlineNs = 1000ull * 1000 * 1000;
 // Ranks whose exchange cells one thread polls at once (loads in flight together).
 #ifndef MT_POLL_RANKS
 #define MT_POLL_RANKS 2

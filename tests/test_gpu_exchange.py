@@ -87,4 +87,4 @@ def test_exchange_gives_up_on_a_silent_peer(setup):
         native.error_word(clear=True)  # later calls give up at once while the word is 2
     print(f"silent peer: call returned after {elapsed * 1e3:.1f} ms, error word {word}")
     assert word == 2
-    assert elapsed < 2.0  # one 100 ms deadline for the whole kernel, not one per cell
+    assert elapsed < 3.0  # one 1 s deadline for the whole kernel, not one per cell

@@ -32,7 +32,7 @@ def test_tp_decode_matches_single_gpu(tmp_path, world):
     r = subprocess.run(["timeout", "-k", "30", "300"] + cmd, env=env, capture_output=True, text=True)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
     rep = json.loads(out.read_text())
-    assert rep["status"] == 0
+    assert rep["status"] == 0 and rep["error_word"] == 0, rep
     same = sum(s["ids_equal"] for s in rep["steps"])
     total = sum(s["ids"] for s in rep["steps"])
     assert same >= 0.97 * total, rep

@@ -16,7 +16,7 @@ sys.path[:0] = [str(REPO), str(REPO / "moss-tts-optimized_b200")]
 import torch  # noqa: E402
 import torch.distributed as dist  # noqa: E402
 
-from moss_tts._runtime import synthetic  # noqa: E402
+from moss_tts._runtime import native, synthetic  # noqa: E402
 from moss_tts._runtime.config import DecoderConfig, small_vocab  # noqa: E402
 from moss_tts._runtime.batch_engine import BatchDecodeEngine  # noqa: E402
 from moss_tts._runtime.engine import DecodeEngine, TensorParallel, shard_weights  # noqa: E402
@@ -36,6 +36,10 @@ def main(out_path: str) -> None:
     eng = DecodeEngine(shard_weights(full, rank, world), max_length=128, tp=tp)
     eng.capture()
     ref = DecodeEngine(full, max_length=128) if rank == 0 else None
+    # every rank enters the first step together (rank 0 built the reference engine meanwhile)
+    torch.cuda.synchronize(dev)
+    dist.barrier()
+    native.error_word(clear=True)
     ids = torch.full((33,), 7, dtype=torch.long)
     ids[0] = 5
     report = {"steps": []}
@@ -57,6 +61,10 @@ def main(out_path: str) -> None:
         dist.broadcast_object_list(obj, src=0)
         ids = obj[0]
     report["status"] = int(eng.status.item())
+    # a peer-exchange poll that gave up (error word 2) would have computed with stale rows
+    word = torch.tensor([native.error_word(clear=True)], device=dev, dtype=torch.int32)
+    dist.all_reduce(word, op=dist.ReduceOp.MAX)
+    report["error_word"] = int(word.item())
     eng.graph = None  # graphs holding NCCL work go before the process group
     # batched decode (tcgen05 GEMM projections, ragged contexts) through the same all-reduces
     B, nkv = 16, cfg.num_kv_heads // world
