@@ -319,12 +319,23 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t v[32];
 #pragma unroll
         for (int i = 0; i < 8; ++i) {  // code word i holds k = 8i .. 8i + 7
-          const uint32_t u = cw[i], hi = u >> 4;
+          const uint32_t u = cw[i];
           const uint32_t zz = i < 4 ? zz0 : zz1, ss = i < 4 ? s0 : s1;
+          if (PACKED) {
+            // packed words hold k = 8i + 2b in nibble b and k = 8i + 2b + 1 in nibble b + 4
+            // (mt_w4a16_gemm_pack), so one shift and mask give the pair: no byte permute
 #pragma unroll
-          for (int b = 0; b < 4; ++b) {
-            const uint32_t t = (prmt(u, hi, 0x0400u + 0x0101u * b) & 0x000F000Fu) | 0x43004300u;
-            v[4 * i + b] = bf16x2_mul(bf16x2_sub(t, zz), ss);
+            for (int b = 0; b < 4; ++b) {
+              const uint32_t t = ((u >> (4 * b)) & 0x000F000Fu) | 0x43004300u;
+              v[4 * i + b] = bf16x2_mul(bf16x2_sub(t, zz), ss);
+            }
+          } else {
+            const uint32_t hi = u >> 4;  // GPTQ words: byte b holds k = 8i + 2b (low), + 1 (high)
+#pragma unroll
+            for (int b = 0; b < 4; ++b) {
+              const uint32_t t = (prmt(u, hi, 0x0400u + 0x0101u * b) & 0x000F000Fu) | 0x43004300u;
+              v[4 * i + b] = bf16x2_mul(bf16x2_sub(t, zz), ss);
+            }
           }
         }
         __syncwarp();
@@ -552,9 +563,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // Load-time repack of a GPTQ-layout projection into the packed layout: per (tile, chunk) the
-// 128 rows' codes (16-byte pieces pre-swizzled as the 128-byte TMA swizzle would place them),
-// their 8 scales and 4 zero-point bytes (0x88 = zero point 8 without zero points). One thread
-// per (tile, chunk, row).
+// 128 rows' codes (16-byte pieces pre-swizzled as the 128-byte TMA swizzle would place them;
+// in every 32-bit word the codes of k = 0, 2, 4, 6 in nibbles 0-3 and of k = 1, 3, 5, 7 in
+// nibbles 4-7, so the dequantisation takes a pair with one shift and mask), their 8 scales
+// and 4 zero-point bytes (0x88 = zero point 8 without zero points). One thread per (tile,
+// chunk, row).
 template <bool PAIRED>
 __global__ void __launch_bounds__(256) w4a16_gemm_pack_kernel(const uint8_t* __restrict__ qweight,
                                                               const __nv_bfloat16* __restrict__ scales,
@@ -572,7 +585,19 @@ __global__ void __launch_bounds__(256) w4a16_gemm_pack_kernel(const uint8_t* __r
   const uint4* src = reinterpret_cast<const uint4*>(qweight + (size_t)row * (k / 2) + (size_t)c * (kChunk / 2));
   uint4* dst = reinterpret_cast<uint4*>(blk + (size_t)m * (kChunk / 2));
 #pragma unroll
-  for (int p = 0; p < 8; ++p) dst[p ^ (m & 7)] = src[p];
+  for (int p = 0; p < 8; ++p) {
+    // each 32-bit word: the even-k codes into nibbles 0-3, the odd-k codes into nibbles 4-7
+    uint4 q = src[p];
+    uint32_t w[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint32_t e = w[i] & 0x0F0F0F0Fu, o = (w[i] >> 4) & 0x0F0F0F0Fu;
+      const uint32_t e16 = (e & 0xFu) | ((e >> 4) & 0xF0u) | ((e >> 8) & 0xF00u) | ((e >> 12) & 0xF000u);
+      const uint32_t o16 = (o & 0xFu) | ((o >> 4) & 0xF0u) | ((o >> 8) & 0xF00u) | ((o >> 12) & 0xF000u);
+      w[i] = e16 | (o16 << 16);
+    }
+    dst[p ^ (m & 7)] = make_uint4(w[0], w[1], w[2], w[3]);
+  }
   *reinterpret_cast<uint4*>(blk + kScaleOff + m * 16) =
       *reinterpret_cast<const uint4*>(scales + (size_t)row * (k / 32) + (size_t)c * 8);
   *reinterpret_cast<uint32_t*>(blk + kPackedZeroOff + m * 4) =
