@@ -422,6 +422,20 @@ class DecodeEngine:
         self._staged = torch.cuda.Event()
         self._staged.record(torch.cuda.current_stream(self.device))
 
+    def health(self, clear: bool = True) -> dict:
+        """The device-side failure flags of the steps run so far (synchronises the device).
+
+        ``status``: 1 = a position or an id was out of range (clamped), 3 = a bounded copy wait
+        in the attention expired. ``error_word`` (the library's, shared by every call in this
+        process): 1 = a bounded pipeline wait expired, 2 = a tensor-parallel exchange poll gave up
+        on a dead or late peer, so that step used stale rows. ``clear`` resets both."""
+        torch.cuda.synchronize(self.device)
+        status = int(self.status.item())
+        word = native.error_word(clear=clear)
+        if clear:
+            self.status.zero_()
+        return {"status": status, "error_word": word}
+
     def read_next_ids(self) -> torch.Tensor:
         """Device-to-host copy of the step result into pinned memory (synchronises)."""
         self._host_next.copy_(self.next_ids, non_blocking=True)

@@ -116,6 +116,10 @@ class FastLLM:
             self._decode()
         return self.engine.read_next_ids()
 
+    def health(self, clear: bool = True) -> dict:
+        """Device-side failure flags of the decode steps so far (``DecodeEngine.health``)."""
+        return self.engine.health(clear)
+
     def _full_text_logits(self):
         head = self.model.head_text
         if head is None:

@@ -62,6 +62,7 @@ def test_teacher_forced_decode_matches_reference(model):
     print(f"reference model, 64 steps: worst |h - ref| / (1 + |ref|) = {worst:.4g}; "
           f"{mismatched} of {g['next'].size} ids differ, all on near-ties")
     assert int(eng.status.item()) == 0
+    assert eng.health() == {"status": 0, "error_word": 0}
     assert mismatched <= 0.02 * g["next"].size, mismatched
 
 
